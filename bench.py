@@ -1,0 +1,370 @@
+#!/usr/bin/env python3
+"""Benchmark of the causal transformer-block forward on B200 (one JSON line).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config C2]
+    torchrun --nproc-per-node N bench.py --gpus N ...     (N > 1: one process per GPU)
+
+Workload (N=1): BASELINE configuration 2 (``configs[1]``) -- causal pre-LN
+block, B=64, S=128, d=128, H=4, ffn=512, L=1, fp32 in/out, seeded default
+init, x ~ N(0,1) from the CPU generator (seed 1234+100000, as the reference
+harness's benchmark input, TTB:2061-2068).  N>1: every rank runs its own
+B=64 batch on its own GPU (batch sharding, no collective on the data path;
+weak scaling); timing is the max over ranks.
+
+``value``: tokens/s of the whole job with x resident in HBM (CUDA events on
+the launching stream around each step, L2 flushed between steps by a 256 MiB
+write, barrier + synchronize around the timed loop).  ``e2e``: the same
+metric through the public API (``UserOptimizedTransformer.__call__``) with
+the pinned host->device copy of x and the device->host copy of y inside each
+timed step.  ``roofline``: the dominant kernel, timed with CUDA events in an
+eager profiling pass over the same workload.  ``cpu_baseline``: the NumPy
+restatement of the reference module (oracle/) on the host cores.
+
+``--impl reference`` times the reference's algorithm on the CPU (the oracle
+port, all host threads; the reference's own code is Python and does not
+travel to the GPU box) on the same config and prints the same line with
+``"impl": "reference"``.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "block forward latency (ms) & tokens/s per shape at 1/2/4/8 B200; % of tensor/HBM roofline"
+CONFIGS = {
+    # name: (B per rank, S, d, H, ffn, L)
+    "C2": (64, 128, 128, 4, 512, 1),
+    "C3": (10000, 128, 128, 4, 512, 1),
+    "C4a": (64, 1024, 128, 4, 512, 1),
+    "C4b": (64, 128, 1024, 4, 4096, 1),
+}
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="C2")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def workload_name(cfg_name):
+    B, S, d, H, F, L = CONFIGS[cfg_name]
+    return f"{cfg_name}: causal pre-LN block B={B}/rank S={S} d={d} H={H} ffn={F} L={L}"
+
+
+def config_dict(cfg_name, n):
+    B, S, d, H, F, L = CONFIGS[cfg_name]
+    return {"workload": workload_name(cfg_name), "batch_per_rank": B, "global_batch": B * n, "seq_len": S,
+            "d_model": d, "heads": H, "head_dim": d // H, "ffn_dim": F, "layers": L, "causal": True,
+            "parallelism": f"batch-sharded x{n} (no data-path collective)" if n > 1 else "single GPU",
+            "l2": "flushed between timed steps (256 MiB write)", "seed": 1234}
+
+
+def load_peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "src": "measured"}
+    except Exception:  # noqa: BLE001
+        return dict(FALLBACK_PEAKS, src="fallback")
+
+
+# ---------------------------------------------------------------- algorithmic work per kernel
+def stage_work(B, S, d, H, F):
+    """(flops, bytes) per launch of each chain stage, counted once (causal pairs only)."""
+    M = B * S
+    return {
+        "ln1": (8 * M * d, M * d * 4 + M * d * 2 + 8 * d),
+        "qkv": (2 * M * d * 3 * d, M * d * 2 + 3 * d * d * 2 + M * 3 * d * 2 + 12 * d),
+        "attn": (2 * B * d * S * (S + 1), M * 3 * d * 2 + M * d * 2),
+        "out_proj": (2 * M * d * d, M * d * 2 + d * d * 2 + M * d * 4 * 2 + 4 * d),
+        "ln2": (8 * M * d, M * d * 4 + M * d * 2 + 8 * d),
+        "ffn_in": (2 * M * d * F, M * d * 2 + F * d * 2 + M * F * 2 + 4 * F),
+        "ffn_out": (2 * M * F * d, M * F * 2 + F * d * 2 + M * d * 4 * 2 + 4 * d),
+        "ln_f": (8 * M * d, M * d * 4 * 2 + 8 * d),
+    }
+
+
+def block_work(B, S, d, H, F):
+    M = B * S
+    flops = 2 * M * d * (3 * d + d) + 4 * M * d * F + 2 * B * d * S * (S + 1)  # = 24*M*d^2 + attn at F=4d
+    byts = 8 * M * d + 2 * (4 * d * d + 2 * d * F)
+    return flops, byts
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                          "-lms", "100", "-i", str(self.index)],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except Exception:  # noqa: BLE001
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:  # noqa: BLE001
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- CPU baseline (oracle port)
+def cpu_forward_rate(cfg_name, budget_s=12.0, min_reps=1):
+    """tokens/s of the NumPy restatement of the reference module on this host (all BLAS threads)."""
+    import numpy as np
+    import oracle
+    try:
+        from threadpoolctl import threadpool_info
+        cores = max([i.get("num_threads", 1) for i in threadpool_info()] or [os.cpu_count() or 1])
+    except Exception:  # noqa: BLE001
+        cores = os.cpu_count() or 1
+    B, S, d, H, F, L = CONFIGS[cfg_name]
+    Bs = B if B * S <= 16384 else max(1, 16384 // S)   # bounded sample of the workload
+    params = oracle.params_from_state_dict(oracle.init_state_dict(L, d, F, 1234))
+    x, _ = oracle.generate_random_case(Bs, S, d, 1234 + 100000)
+    xn = x.numpy()
+    cfg = oracle.OracleConfig(Bs, S, d, H, F, L, True)
+    oracle.model_forward(params, cfg, xn[:1])  # warm BLAS
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while len(times) < min_reps or time.perf_counter() < t_end:
+        t0 = time.perf_counter()
+        oracle.model_forward(params, cfg, xn)
+        times.append(time.perf_counter() - t0)
+        if len(times) >= 50:
+            break
+    med = statistics.median(times)
+    return {"value": Bs * S / med, "unit": "tokens/s", "cores": int(cores), "kind": "port",
+            "sample": f"{len(times)} forwards of B={Bs} x S={S} (NumPy fp32 restatement of the reference "
+                      f"module, oracle/), median {med * 1e3:.1f} ms"}, med, Bs
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return 0
+    B, S, d, H, F, L = CONFIGS[args.config]
+    import numpy as np
+    import oracle
+    base, med, Bs = cpu_forward_rate(args.config, budget_s=0.0, min_reps=1)
+    params = oracle.params_from_state_dict(oracle.init_state_dict(L, d, F, 1234))
+    x, _ = oracle.generate_random_case(Bs, S, d, 1234 + 100000)
+    xn = x.numpy()
+    cfg = oracle.OracleConfig(Bs, S, d, H, F, L, True)
+    for _ in range(args.warmup):
+        oracle.model_forward(params, cfg, xn)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.model_forward(params, cfg, xn)
+    el = time.perf_counter() - t0
+    tok = Bs * S * args.steps / el
+    base.update(value=tok, sample=f"{args.steps} timed forwards of B={Bs} x S={S} per step "
+                                   f"(NumPy fp32 restatement of the reference module)")
+    line = {"impl": "reference", "metric": METRIC, "value": tok, "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": el * 1e3 / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded N(0,1) input, seeded default init)",
+            "config": config_dict(args.config, 1), "cpu_baseline": base,
+            "e2e": {"value": tok, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------- GPU arm
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import torch
+    import torch.distributed as dist
+    import torch_transformer_benchmark as T
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    B, S, d, H, F, L = CONFIGS[args.config]
+    cfg = T.TransformerConfig(B, S, d, H, F, L, True)
+    torch.manual_seed(1234)
+    model = T.UserOptimizedTransformer(cfg).to(dev).eval()
+    gen = torch.Generator(device="cpu").manual_seed(1234 + 100000 + 7919 * rank)
+    x_host = torch.randn(B, S, d, generator=gen).pin_memory()
+    y_host = torch.empty(B, S, d).pin_memory()
+    x = x_host.to(dev)
+    mask = torch.ones(B, S, dtype=torch.bool, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+    tokens_rank = B * S
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    clk = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ else
+                       int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local]))
+    clk.start()
+    with torch.inference_mode():
+        for _ in range(max(args.warmup, 3)):
+            model(x, mask)
+        torch.cuda.synchronize()
+        # ---- device-resident timed region
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        barrier()
+        torch.cuda.synchronize()
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record(stream)
+            model(x, mask)
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        ms_rank = sum(a.elapsed_time(b) for a, b in zip(starts, ends))
+        ms_total = max_over_ranks(ms_rank)
+        # ---- end to end through the public API: pinned H2D of x, forward, D2H of y, every step
+        e_st = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        e_en = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        xd = torch.empty_like(x)
+        barrier()
+        torch.cuda.synchronize()
+        for i in range(args.steps):
+            flush.zero_()
+            e_st[i].record(stream)
+            xd.copy_(x_host, non_blocking=True)
+            y = model(xd, mask)
+            y_host.copy_(y, non_blocking=True)
+            e_en[i].record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        e2e_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in zip(e_st, e_en)))
+    clocks = clk.stop()
+
+    value = world * tokens_rank * args.steps / (ms_total / 1e3)
+    e2e_value = world * tokens_rank * args.steps / (e2e_ms / 1e3)
+    launches_per_step = kernels_per_forward(model)
+
+    roof = None
+    cpu = None
+    if rank == 0:
+        roof = roofline_pass(model, x, mask, flush, cfg, steps=max(20, min(args.steps, 200)))
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = cpu_forward_rate(args.config)[0]
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_total / args.steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f16 operands / f32 accumulate, f32 in-out",
+                "data": "synthetic (seeded N(0,1) input, seeded default init)",
+                "config": dict(config_dict(args.config, world), strategy=model.last_strategy),
+                "e2e": {"value": e2e_value, "unit": "tokens/s", "ms_per_step": e2e_ms / args.steps,
+                        "h2d_bytes_per_step": x_host.numel() * 4, "d2h_bytes_per_step": y_host.numel() * 4,
+                        "api": "UserOptimizedTransformer.__call__"},
+                "roofline": roof, "cpu_baseline": cpu, "clocks": clocks,
+                "gpu_launches": launches_per_step * args.steps}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def kernels_per_forward(model):
+    strat = model.last_strategy
+    nl = model.config.num_layers
+    if strat == "fused_small":
+        return nl
+    return 8 * nl if nl == 1 else 7 * nl + 1
+
+
+def roofline_pass(model, x, mask, flush, cfg, steps):
+    """Dominant-kernel roofline: per-stage CUDA-event timing of an eager pass on the same inputs."""
+    import torch
+    peaks = load_peaks()
+    B, S, d = x.shape
+    H, F = cfg.num_heads, cfg.ffn_dim
+    timing = model.profile_stages(x, steps=steps, flush=flush)
+    if not timing:
+        return None
+    work = stage_work(B, S, d, H, F)
+    name = max(timing, key=timing.get)
+    if name == "fused_small":
+        fl, by = block_work(B, S, d, H, F)
+    else:
+        fl, by = work[name]
+    ms = timing[name]
+    t_tensor = fl / (peaks["bf16_tflops"] * 1e12)
+    t_hbm = by / (peaks["hbm_gbs"] * 1e9)
+    if t_tensor >= t_hbm:
+        ach = fl / (ms * 1e-3) / 1e12
+        out = {"bound": "tensor", "achieved": ach, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s"}
+    else:
+        ach = by / (ms * 1e-3) / 1e9
+        out = {"bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s"}
+    out.update(frac=out["achieved"] / out["peak"], traffic=None, kernel=name, ms_per_launch=ms,
+               peak_src=f"{peaks['src']} (MEASURED_PEAKS.json burst)" if peaks["src"] == "measured" else "fallback",
+               stage_ms=timing, algorithmic={"flops": fl, "bytes": by})
+    return out
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

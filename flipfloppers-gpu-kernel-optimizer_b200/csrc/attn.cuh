@@ -1,0 +1,291 @@
+// Causal flash attention on tcgen05 for one (query tile, head, sequence) per CTA.
+//
+// Semantics follow the reference module's attention (TTB:117-132 of
+// torch_transformer_benchmark.py): scores = q.k^T * head_dim^-0.5, keys after
+// the query masked, fp32 softmax, probs.v.  Query row i of this call sits at
+// absolute position q_offset+i and sees keys 0..q_offset+i -- with q_offset=0
+// that is the reference's triu(1) mask, with q_offset>0 it is the prefix-causal
+// (bottom-right aligned) attention of the reference's chunked forward
+// (TTB:1491-1500) over an incrementally filled K/V cache.
+//
+// Per CTA (192 threads):
+//   warp 0     TMA producer: the 128-row Q tile once, then K_j/V_j tiles into a
+//              2-deep ring (kv_full / kv_empty mbarriers);
+//   warp 1     TMEM owner + MMA issuer: S_j = Q.K_j^T into TMEM columns
+//              [0,BN); O += P_j.V_j into columns [BN, BN+HD) with V read
+//              MN-major (head_dim contiguous) straight from the TMA tile;
+//   warps 2-5  softmax: one query row per thread (TMEM lane = row), running
+//              max / sum in the log2 domain, P_j (fp16) written to shared
+//              memory in the 128B-swizzled K-major layout UMMA reads, O rescaled
+//              in TMEM when the running max moves; final O/l -> fp16 context.
+// Key tiles past the diagonal are never loaded (causal tile skipping); only
+// tiles that straddle the diagonal apply the mask.
+#pragma once
+
+#include "ptx.cuh"
+
+namespace b200 {
+
+struct AttnParams {
+  int H;
+  int q_len;             // query rows per sequence handled by this call
+  int q_offset;          // absolute position of query row 0 inside its sequence
+  int kv_len;            // keys available per sequence (>= q_offset + q_len)
+  int q_seq_rows;        // rows between consecutive sequences in the Q tensor
+  int kv_seq_rows;       // rows between consecutive sequences in the K/V tensors
+  int q_row0, kv_row0;   // row of sequence 0 / position 0 in the Q and K/V tensors
+  int q_col0, k_col0, v_col0;  // column of head 0 in the Q / K / V tensors
+  __half* out;           // context [rows, ld_out]; head h at column h*HD
+  int64_t ld_out;
+  int out_seq_rows;      // rows between consecutive sequences in out
+  float scale_log2;      // head_dim^-0.5 * log2(e)
+};
+
+template <int HD, int BN>
+struct AttnCfg {
+  static constexpr int ATOM_E = HD >= 64 ? 64 : HD;   // elements per swizzle row
+  static constexpr int ROWB = ATOM_E * 2;             // bytes per swizzle row (128 or 64)
+  static constexpr uint32_t SWZ = ATOM_E == 64 ? UMMA_SW128 : UMMA_SW64;
+  static constexpr int NBOX = HD / ATOM_E;
+  static constexpr int Q_BYTES = 128 * HD * 2;
+  static constexpr int KV_BYTES = BN * HD * 2;
+  static constexpr int P_BYTES = 128 * BN * 2;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K0 = Q_BYTES;
+  static constexpr int OFF_V0 = OFF_K0 + KV_BYTES;
+  static constexpr int OFF_K1 = OFF_V0 + KV_BYTES;
+  static constexpr int OFF_V1 = OFF_K1 + KV_BYTES;
+  static constexpr int OFF_P = OFF_V1 + KV_BYTES;
+  static constexpr int OFF_BAR = OFF_P + P_BYTES;
+  static constexpr int TOTAL = OFF_BAR + 256 + 1024;
+  static constexpr uint32_t TMEM_COLS = (BN + HD) <= 256 ? 256 : 512;
+  static_assert(HD % ATOM_E == 0, "head_dim must tile the swizzle atom");
+  static_assert(BN % 64 == 0, "key tile must be a multiple of 64");
+};
+
+template <int HD, int BN>
+__global__ void __launch_bounds__(192, 1)
+    k_flash_causal(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
+  using C = AttnCfg<HD, BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;
+  uint64_t* p_full = bars + 6;
+  uint64_t* pv_done = bars + 7;
+  uint64_t* drain = bars + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nqt = (p.q_len + 127) / 128;
+  const int qt = nqt - 1 - static_cast<int>(blockIdx.x);  // longest (latest) query tiles first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int q_first = p.q_offset + qt * 128;
+  const int q_last = p.q_offset + min(p.q_len, (qt + 1) * 128) - 1;
+  const int nkt = min(q_last / BN + 1, (p.kv_len + BN - 1) / BN);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(&kv_full[0], 1);
+    mbar_init(&kv_full[1], 1);
+    mbar_init(&kv_empty[0], 1);
+    mbar_init(&kv_empty[1], 1);
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 128);
+    mbar_init(pv_done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      const int qrow = p.q_row0 + b * p.q_seq_rows + qt * 128;
+      mbar_arrive_expect_tx(q_full, C::Q_BYTES);
+#pragma unroll
+      for (int bx = 0; bx < C::NBOX; ++bx)
+        tma_load_2d(smem + C::OFF_Q + bx * 128 * C::ROWB, &tmQ, q_full, p.q_col0 + h * HD + bx * C::ATOM_E, qrow);
+      int issued = 0;
+      for (int j = 0; j < nkt; ++j) {
+        const int s = j & 1;
+        if (j >= 2 && !mbar_wait(&kv_empty[s], ((j >> 1) - 1) & 1, abort_flag, DERR_WAIT_SLOT)) break;
+        const int krow = p.kv_row0 + b * p.kv_seq_rows + j * BN;
+        uint8_t* ks = smem + (s ? C::OFF_K1 : C::OFF_K0);
+        uint8_t* vs = smem + (s ? C::OFF_V1 : C::OFF_V0);
+        mbar_arrive_expect_tx(&kv_full[s], 2 * C::KV_BYTES);
+#pragma unroll
+        for (int bx = 0; bx < C::NBOX; ++bx)
+          tma_load_2d(ks + bx * BN * C::ROWB, &tmK, &kv_full[s], p.k_col0 + h * HD + bx * C::ATOM_E, krow);
+#pragma unroll
+        for (int bx = 0; bx < C::NBOX; ++bx)
+          tma_load_2d(vs + bx * BN * C::ROWB, &tmV, &kv_full[s], p.v_col0 + h * HD + bx * C::ATOM_E, krow);
+        issued = j + 1;
+      }
+      if (*abort_flag) {
+        mbar_wait_drain(q_full, 0);
+        for (int j = (issued > 2 ? issued - 2 : 0); j < issued; ++j) mbar_wait_drain(&kv_full[j & 1], (j >> 1) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = make_idesc_f16(128, BN, false);
+      constexpr uint32_t idesc_o = make_idesc_f16(128, HD, true);
+      const uint32_t q_addr = smem_u32(smem + C::OFF_Q);
+      const uint32_t p_addr = smem_u32(smem + C::OFF_P);
+      auto issue_s = [&](int j) {
+        const uint32_t k_addr = smem_u32(smem + ((j & 1) ? C::OFF_K1 : C::OFF_K0));
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const int box = (kk * 16) / C::ATOM_E;
+          const uint32_t within = ((kk * 16) % C::ATOM_E) * 2;
+          const uint64_t ad = make_sdesc(q_addr + box * 128 * C::ROWB + within, 16, 8 * C::ROWB, C::SWZ);
+          const uint64_t bd = make_sdesc(k_addr + box * BN * C::ROWB + within, 16, 8 * C::ROWB, C::SWZ);
+          umma_f16_ss(tmem, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(s_full);
+      };
+      bool ok = mbar_wait(q_full, 0, abort_flag, DERR_WAIT_TMA) && mbar_wait(&kv_full[0], 0, abort_flag, DERR_WAIT_TMA);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0);
+      }
+      for (int j = 0; ok && j < nkt; ++j) {
+        if (!mbar_wait(p_full, j & 1, abort_flag, DERR_WAIT_SOFTMAX)) break;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(smem + ((j & 1) ? C::OFF_V1 : C::OFF_V0));
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint64_t ad = make_sdesc(p_addr + (kk >> 2) * (128 * 128) + (kk & 3) * 32, 16, 1024, UMMA_SW128);
+          const uint64_t bd = make_sdesc(v_addr + kk * 16 * C::ROWB, BN * C::ROWB, 8 * C::ROWB, C::SWZ);
+          umma_f16_ss(tmem + BN, ad, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc_commit(pv_done);
+        tc_commit(&kv_empty[j & 1]);
+        if (j + 1 < nkt) {
+          if (!mbar_wait(&kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag, DERR_WAIT_TMA)) break;
+          tc_fence_after();
+          issue_s(j + 1);
+        }
+      }
+      if (*abort_flag) {
+        tc_commit(drain);
+        mbar_wait_drain(drain, 0);
+      }
+    }
+  } else {
+    // softmax / epilogue warps: one query row per thread
+    const int qd = warp & 3;
+    const int rl = qd * 32 + lane;
+    const int qpos = q_first + rl;
+    const uint32_t trow = tmem + (static_cast<uint32_t>(qd * 32) << 16);
+    uint8_t* ps = smem + C::OFF_P;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkt; ++j) {
+      ok = mbar_wait_warp(s_full, j & 1, abort_flag, DERR_WAIT_MMA);
+      if (!ok) break;
+      tc_fence_after();
+      float s[BN];
+#pragma unroll
+      for (int c = 0; c < BN; c += 32) {
+        float t[32];
+        tmem_ld32(trow + c, t);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[c + i] = t[i];
+      }
+      const int k0 = j * BN;
+      const bool need_mask = (k0 + BN - 1) > q_first;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < BN; ++c) {
+        float t = s[c] * p.scale_log2;
+        if (need_mask && (k0 + c) > qpos) t = -INFINITY;
+        s[c] = t;
+        mx = fmaxf(mx, t);
+      }
+      const float m_new = fmaxf(m, mx);
+      // rows with nothing visible yet keep p = 0 (cannot happen for real rows: key 0 is always visible)
+      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+      const float alpha = fast_exp2(m - m_use);  // m = -inf on the first tile -> 0
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < BN; ++c) {
+        const float e = fast_exp2(s[c] - m_use);
+        s[c] = e;
+        sum += e;
+      }
+      l = l * alpha + sum;
+      m = m_new;
+      if (j > 0) {
+        ok = mbar_wait_warp(pv_done, (j - 1) & 1, abort_flag, DERR_WAIT_MMA);
+        if (!ok) break;
+        tc_fence_after();
+      }
+      // P_j -> shared memory, 128B-swizzled K-major (keys contiguous), 64 keys per swizzle atom
+#pragma unroll
+      for (int ch = 0; ch < BN / 8; ++ch) {
+        const uint4 v = make_uint4(pack_half2(s[8 * ch + 0], s[8 * ch + 1]), pack_half2(s[8 * ch + 2], s[8 * ch + 3]),
+                                   pack_half2(s[8 * ch + 4], s[8 * ch + 5]), pack_half2(s[8 * ch + 6], s[8 * ch + 7]));
+        *reinterpret_cast<uint4*>(ps + (ch >> 3) * (128 * 128) + sw128_off(rl, ch & 7)) = v;
+      }
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll 1
+        for (int c = 0; c < HD; c += 32) {
+          float o[32];
+          tmem_ld32(trow + BN + c, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tmem_st32(trow + BN + c, o);
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (ok) ok = mbar_wait_warp(pv_done, (nkt - 1) & 1, abort_flag, DERR_WAIT_MMA);
+    if (ok && !*abort_flag) {
+      tc_fence_after();
+      const float inv_l = 1.f / l;
+      const int row_in_seq = qt * 128 + rl;
+      __half* orow = p.out + (static_cast<int64_t>(b) * p.out_seq_rows + row_in_seq) * p.ld_out + h * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD; c += 32) {
+        float o[32];
+        tmem_ld32(trow + BN + c, o);
+        if (row_in_seq < p.q_len) {
+          uint4* o4 = reinterpret_cast<uint4*>(orow + c);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            o4[i] = make_uint4(pack_half2(o[8 * i + 0] * inv_l, o[8 * i + 1] * inv_l),
+                               pack_half2(o[8 * i + 2] * inv_l, o[8 * i + 3] * inv_l),
+                               pack_half2(o[8 * i + 4] * inv_l, o[8 * i + 5] * inv_l),
+                               pack_half2(o[8 * i + 6] * inv_l, o[8 * i + 7] * inv_l));
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+}  // namespace b200

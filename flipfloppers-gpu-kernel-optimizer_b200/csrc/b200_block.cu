@@ -1,0 +1,425 @@
+// Host side of libb200block.so: argument checks, TMA tensor maps, tile
+// selection, launches, and the per-layer chain b200_block_forward.
+// The whole library is this one translation unit (kernel headers included
+// below), built for sm_100a only.
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+#include <set>
+#include <utility>
+
+#include "b200_block.h"
+#include "ptx.cuh"
+#include "ln.cuh"
+#include "gemm.cuh"
+#include "attn.cuh"
+
+using namespace b200;
+
+namespace {
+
+// ------------------------------------------------------------------ runtime state
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+std::mutex g_mu;
+std::set<std::pair<const void*, int>> g_attr_done;  // (kernel, device) with smem opt-in set
+int g_arch_state[128] = {0};                          // per device: 0 unknown, 1 ok, -1 not sm_100
+
+int ensure_encode() {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    else
+      cudaGetLastError();
+  });
+  return g_encode ? B200_OK : B200_ERR_TMAP;
+}
+
+int current_device() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return dev;
+}
+
+int check_arch() {
+  const int dev = current_device();
+  if (dev < 0 || dev >= 128) return B200_ERR_ARCH;
+  int st;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    st = g_arch_state[dev];
+  }
+  if (st == 0) {
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    st = (major == 10 && minor == 0) ? 1 : -1;
+    std::lock_guard<std::mutex> lk(g_mu);
+    g_arch_state[dev] = st;
+  }
+  return st == 1 ? B200_OK : B200_ERR_ARCH;
+}
+
+int set_smem(const void* fn, int bytes) {
+  const int dev = current_device();
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_attr_done.count({fn, dev})) return B200_OK;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return B200_ERR_SMEM;
+  }
+  g_attr_done.insert({fn, dev});
+  return B200_OK;
+}
+
+int launch_status() { return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_LAUNCH; }
+
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// 2-D fp16 tensor [rows, cols] with row stride ld (elements); box box_rows x box_cols.
+int make_map_f16(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_cols,
+                 uint32_t box_rows, CUtensorMapSwizzle sw) {
+  if (ensure_encode() != B200_OK) return B200_ERR_TMAP;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? B200_OK : B200_ERR_TMAP;
+}
+
+// ------------------------------------------------------------------ GEMM
+template <int BN, int STAGES, int EPI>
+int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p, cudaStream_t st) {
+  auto kern = k_gemm_tn<BN, STAGES, EPI>;
+  const int smem = GemmSmem<BN, STAGES>::TOTAL;
+  if (int rc = set_smem(reinterpret_cast<const void*>(kern), smem)) return rc;
+  dim3 grid((p.N + BN - 1) / BN, (p.M + 127) / 128);
+  kern<<<grid, 192, smem, st>>>(ta, tw, p);
+  return launch_status();
+}
+
+template <int BN, int STAGES>
+int launch_gemm_bn(int epi, const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p, cudaStream_t st) {
+  switch (epi) {
+    case EPI_BIAS_F16: return launch_gemm_t<BN, STAGES, EPI_BIAS_F16>(ta, tw, p, st);
+    case EPI_BIAS_GELU_F16: return launch_gemm_t<BN, STAGES, EPI_BIAS_GELU_F16>(ta, tw, p, st);
+    case EPI_BIAS_RESID_F32: return launch_gemm_t<BN, STAGES, EPI_BIAS_RESID_F32>(ta, tw, p, st);
+    default: return B200_ERR_CONFIG;
+  }
+}
+
+int pick_bn(long long M, int N) {
+  const long long mt = (M + 127) / 128;
+  if (N % 256 == 0 && mt * (N / 256) >= 2 * 148) return 256;
+  return 128;
+}
+
+int gemm_impl(int epi, const void* A, long long lda, const void* W, long long ldw, const float* bias,
+              const float* resid, long long ld_resid, void* out, long long ld_out, int M, int N, int K,
+              cudaStream_t st) {
+  if (!A || !W || !out || M < 0 || N <= 0 || K <= 0) return B200_ERR_ARG;
+  if (epi < 0 || epi > 2) return B200_ERR_CONFIG;
+  if (epi == EPI_BIAS_RESID_F32 && !resid) return B200_ERR_ARG;
+  if (M == 0) return B200_OK;
+  if (N % 32 || K % 8 || lda % 8 || ldw % 8 || lda < K || ldw < K) return B200_ERR_TILE;
+  const bool f32_out = epi == EPI_BIAS_RESID_F32;
+  if (ld_out < N || ld_out % (f32_out ? 4 : 8)) return B200_ERR_ALIGN;
+  if (!al16(A) || !al16(W) || !al16(out) || (bias && !al16(bias))) return B200_ERR_ALIGN;
+  if (f32_out && (!al16(resid) || ld_resid % 4 || ld_resid < N)) return B200_ERR_ALIGN;
+  if ((M + 127) / 128 > 65535) return B200_ERR_TILE;
+  if (int rc = check_arch()) return rc;
+  const int BN = pick_bn(M, N);
+  CUtensorMap ta, tw;
+  if (int rc = make_map_f16(&ta, A, M, K, lda, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
+  if (int rc = make_map_f16(&tw, W, N, K, ldw, 64, BN, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
+  GemmParams p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.a_row0 = 0;
+  p.bias = bias;
+  p.resid = resid;
+  p.ld_resid = ld_resid;
+  p.out = out;
+  p.ld_out = ld_out;
+  if (BN == 256) return launch_gemm_bn<256, 4>(epi, ta, tw, p, st);
+  return launch_gemm_bn<128, 6>(epi, ta, tw, p, st);
+}
+
+// ------------------------------------------------------------------ LayerNorm
+template <int VPL, bool VEC4>
+int launch_ln_t(const float* x, long long ldx, const float* g, const float* b, void* out, long long ldo, bool f16,
+                int rows, int d, float eps, cudaStream_t st) {
+  const int warps = 8;
+  dim3 grid((rows + warps - 1) / warps);
+  if (f16)
+    k_layernorm<VPL, VEC4, true><<<grid, 32 * warps, 0, st>>>(x, ldx, g, b, out, ldo, rows, d, eps);
+  else
+    k_layernorm<VPL, VEC4, false><<<grid, 32 * warps, 0, st>>>(x, ldx, g, b, out, ldo, rows, d, eps);
+  return launch_status();
+}
+
+int ln_impl(const float* x, long long ldx, const float* g, const float* b, void* out, long long ldo, int f16,
+            int rows, int d, float eps, cudaStream_t st) {
+  if (!x || !g || !b || !out || rows < 0 || d <= 0) return B200_ERR_ARG;
+  if (rows == 0) return B200_OK;
+  if (d % 32 || d > 4096 || ldx < d || ldo < d) return B200_ERR_TILE;
+  if (int rc = check_arch()) return rc;
+  if (d % 128 == 0 && ldx % 4 == 0 && ldo % 4 == 0 && al16(x) && al16(out) && al16(g) && al16(b)) {
+    switch (d / 128) {
+      case 1: return launch_ln_t<1, true>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
+      case 2: return launch_ln_t<2, true>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
+      case 4: return launch_ln_t<4, true>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
+      case 8: return launch_ln_t<8, true>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
+      case 16: return launch_ln_t<16, true>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
+      case 32: return launch_ln_t<32, true>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
+      default: break;
+    }
+  }
+  switch (d / 32) {
+    case 1: return launch_ln_t<1, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
+    case 2: return launch_ln_t<2, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
+    case 3: return launch_ln_t<3, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
+    case 4: return launch_ln_t<4, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
+    case 6: return launch_ln_t<6, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
+    case 8: return launch_ln_t<8, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
+    case 12: return launch_ln_t<12, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
+    case 16: return launch_ln_t<16, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
+    case 24: return launch_ln_t<24, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
+    case 32: return launch_ln_t<32, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
+    default: return B200_ERR_TILE;
+  }
+}
+
+// ------------------------------------------------------------------ attention
+template <int HD, int BN>
+int launch_attn_t(const B200AttnArgs& a, cudaStream_t st) {
+  using C = AttnCfg<HD, BN>;
+  constexpr CUtensorMapSwizzle SW = C::ATOM_E == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  CUtensorMap tq, tk, tv;
+  if (int rc = make_map_f16(&tq, a.q, a.q_rows, a.ld_q, a.ld_q, C::ATOM_E, 128, SW)) return rc;
+  if (int rc = make_map_f16(&tk, a.k, a.kv_rows, a.ld_k, a.ld_k, C::ATOM_E, BN, SW)) return rc;
+  if (int rc = make_map_f16(&tv, a.v, a.kv_rows, a.ld_v, a.ld_v, C::ATOM_E, BN, SW)) return rc;
+  AttnParams p{};
+  p.H = a.heads;
+  p.q_len = a.q_len;
+  p.q_offset = a.q_offset;
+  p.kv_len = a.kv_len;
+  p.q_seq_rows = a.q_seq_rows;
+  p.kv_seq_rows = a.kv_seq_rows;
+  p.q_row0 = a.q_row0;
+  p.kv_row0 = a.kv_row0;
+  p.q_col0 = a.q_col0;
+  p.k_col0 = a.k_col0;
+  p.v_col0 = a.v_col0;
+  p.out = static_cast<__half*>(a.out) + static_cast<int64_t>(a.out_row0) * a.ld_out;
+  p.ld_out = a.ld_out;
+  p.out_seq_rows = a.out_seq_rows;
+  p.scale_log2 = static_cast<float>(1.4426950408889634 / __builtin_sqrt(static_cast<double>(HD)));
+  // TMEM: at most two 256-column CTAs per SM, so request enough shared memory
+  // that a third cannot be co-resident and block in tcgen05.alloc.
+  int smem = C::TOTAL;
+  if (C::TMEM_COLS == 256 && smem < 80 * 1024) smem = 80 * 1024;
+  auto kern = k_flash_causal<HD, BN>;
+  if (int rc = set_smem(reinterpret_cast<const void*>(kern), smem)) return rc;
+  dim3 grid((a.q_len + 127) / 128, a.heads, a.batch);
+  kern<<<grid, 192, smem, st>>>(tq, tk, tv, p);
+  return launch_status();
+}
+
+int attn_impl(const B200AttnArgs* a, cudaStream_t st) {
+  if (!a || !a->q || !a->k || !a->v || !a->out) return B200_ERR_ARG;
+  if (a->batch <= 0 || a->heads <= 0 || a->q_len < 0 || a->q_offset < 0 || a->kv_len <= 0) return B200_ERR_ARG;
+  if (a->q_len == 0) return B200_OK;
+  if (a->q_offset + a->q_len > a->kv_len) return B200_ERR_ARG;
+  const int hd = a->head_dim;
+  if (hd != 32 && hd != 64 && hd != 128 && hd != 256) return B200_ERR_HEAD_DIM;
+  if (a->ld_q % 8 || a->ld_k % 8 || a->ld_v % 8 || a->ld_out % 8) return B200_ERR_ALIGN;
+  if (!al16(a->q) || !al16(a->k) || !al16(a->v) || !al16(a->out)) return B200_ERR_ALIGN;
+  if (a->q_col0 % 8 || a->k_col0 % 8 || a->v_col0 % 8) return B200_ERR_ALIGN;
+  const long long span = static_cast<long long>(a->heads) * hd;
+  if (a->q_col0 + span > a->ld_q || a->k_col0 + span > a->ld_k || a->v_col0 + span > a->ld_v || span > a->ld_out)
+    return B200_ERR_ARG;
+  if (static_cast<long long>(a->q_row0) + static_cast<long long>(a->batch - 1) * a->q_seq_rows + a->q_len > a->q_rows)
+    return B200_ERR_ARG;
+  if (static_cast<long long>(a->kv_row0) + static_cast<long long>(a->batch - 1) * a->kv_seq_rows + a->kv_len >
+      a->kv_rows)
+    return B200_ERR_ARG;
+  if (a->heads > 65535 || a->batch > 65535) return B200_ERR_TILE;
+  if (int rc = check_arch()) return rc;
+  switch (hd) {
+    case 32: return launch_attn_t<32, 128>(*a, st);
+    case 64: return launch_attn_t<64, 128>(*a, st);
+    case 128: return launch_attn_t<128, 128>(*a, st);
+    case 256: return launch_attn_t<256, 64>(*a, st);
+    default: return B200_ERR_HEAD_DIM;
+  }
+}
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+struct BlockWs {
+  __half* n;     // [M, d] fp16 LayerNorm output (LN1, then LN2)
+  __half* qkv;   // [M, 3d] fp16
+  __half* ctx;   // [M, d] fp16
+  float* x1;     // [M, d] fp32 residual stream after attention (then after FFN)
+  __half* h;     // [M, ffn] fp16 GELU activations
+  size_t bytes;
+};
+
+BlockWs carve(void* base, long long M, int d, int ffn) {
+  BlockWs w{};
+  uint8_t* p = static_cast<uint8_t*>(base);
+  size_t off = 0;
+  auto take = [&](size_t n) {
+    uint8_t* r = p ? p + off : nullptr;
+    off += align256(n);
+    return r;
+  };
+  w.n = reinterpret_cast<__half*>(take(static_cast<size_t>(M) * d * 2));
+  w.qkv = reinterpret_cast<__half*>(take(static_cast<size_t>(M) * 3 * d * 2));
+  w.ctx = reinterpret_cast<__half*>(take(static_cast<size_t>(M) * d * 2));
+  w.x1 = reinterpret_cast<float*>(take(static_cast<size_t>(M) * d * 4));
+  w.h = reinterpret_cast<__half*>(take(static_cast<size_t>(M) * ffn * 2));
+  w.bytes = off;
+  return w;
+}
+
+int block_impl(const B200BlockArgs* a, cudaStream_t st) {
+  if (!a || !a->x || !a->y || !a->w_qkv || !a->w_o || !a->w_in || !a->w_out) return B200_ERR_ARG;
+  if (!a->ln1_w || !a->ln1_b || !a->ln2_w || !a->ln2_b || !a->b_qkv || !a->b_o || !a->b_in || !a->b_out)
+    return B200_ERR_ARG;
+  if ((a->lnf_w == nullptr) != (a->lnf_b == nullptr)) return B200_ERR_ARG;
+  if (a->batch <= 0 || a->seq_len <= 0 || a->d_model <= 0 || a->num_heads <= 0 || a->ffn_dim <= 0) return B200_ERR_ARG;
+  if (a->d_model % a->num_heads) return B200_ERR_ARG;
+  if (a->x == a->y) return B200_ERR_ARG;
+  const long long M = static_cast<long long>(a->batch) * a->seq_len;
+  const int d = a->d_model, F = a->ffn_dim, H = a->num_heads, hd = d / H;
+  if (hd != 32 && hd != 64 && hd != 128 && hd != 256) return B200_ERR_HEAD_DIM;
+  if (M > 0x7fffffffLL) return B200_ERR_TILE;
+  BlockWs w = carve(a->workspace, M, d, F);
+  if (!a->workspace || a->workspace_bytes < w.bytes) return B200_ERR_WORKSPACE;
+  if (!al16(a->workspace)) return B200_ERR_ALIGN;
+  int rc;
+  // 1. n = LN1(x) (fp16)
+  if ((rc = ln_impl(a->x, d, a->ln1_w, a->ln1_b, w.n, d, 1, static_cast<int>(M), d, a->eps, st))) return rc;
+  // 2. qkv = n . Wqkv^T + bqkv
+  if ((rc = gemm_impl(EPI_BIAS_F16, w.n, d, a->w_qkv, d, a->b_qkv, nullptr, 0, w.qkv, 3 * d, static_cast<int>(M),
+                      3 * d, d, st)))
+    return rc;
+  // 3. ctx = causal_attention(q, k, v)
+  B200AttnArgs at{};
+  at.q = at.k = at.v = w.qkv;
+  at.ld_q = at.ld_k = at.ld_v = 3 * d;
+  at.q_rows = at.kv_rows = M;
+  at.batch = a->batch;
+  at.heads = H;
+  at.head_dim = hd;
+  at.q_len = at.kv_len = a->seq_len;
+  at.q_offset = 0;
+  at.q_seq_rows = at.kv_seq_rows = a->seq_len;
+  at.q_row0 = at.kv_row0 = 0;
+  at.q_col0 = 0;
+  at.k_col0 = d;
+  at.v_col0 = 2 * d;
+  at.out = w.ctx;
+  at.ld_out = d;
+  at.out_seq_rows = a->seq_len;
+  at.out_row0 = 0;
+  if ((rc = attn_impl(&at, st))) return rc;
+  // 4. x1 = x + ctx . Wo^T + bo
+  if ((rc = gemm_impl(EPI_BIAS_RESID_F32, w.ctx, d, a->w_o, d, a->b_o, a->x, d, w.x1, d, static_cast<int>(M), d, d,
+                      st)))
+    return rc;
+  // 5. n = LN2(x1)
+  if ((rc = ln_impl(w.x1, d, a->ln2_w, a->ln2_b, w.n, d, 1, static_cast<int>(M), d, a->eps, st))) return rc;
+  // 6. h = gelu(n . W1^T + b1)
+  if ((rc = gemm_impl(EPI_BIAS_GELU_F16, w.n, d, a->w_in, d, a->b_in, nullptr, 0, w.h, F, static_cast<int>(M), F, d,
+                      st)))
+    return rc;
+  // 7. x2 = x1 + h . W2^T + b2 (in place in x1, or straight into y without a final norm)
+  float* x2 = a->lnf_w ? w.x1 : a->y;
+  if ((rc = gemm_impl(EPI_BIAS_RESID_F32, w.h, F, a->w_out, F, a->b_out, w.x1, d, x2, d, static_cast<int>(M), d, F,
+                      st)))
+    return rc;
+  // 8. y = LN_f(x2)
+  if (a->lnf_w) {
+    if ((rc = ln_impl(w.x1, d, a->lnf_w, a->lnf_b, a->y, d, 0, static_cast<int>(M), d, a->eps, st))) return rc;
+  }
+  return B200_OK;
+}
+
+}  // namespace
+
+// ====================================================================== C ABI
+extern "C" {
+
+int b200_abi_version(void) { return B200_ABI_VERSION; }
+
+const char* b200_status_str(int s) {
+  switch (s) {
+    case B200_OK: return "ok";
+    case B200_ERR_CONFIG: return "unsupported configuration or epilogue";
+    case B200_ERR_TILE: return "dimension is not a multiple of the required granule";
+    case B200_ERR_SPLIT: return "K is not a multiple of the split size";
+    case B200_ERR_SMEM: return "dynamic shared memory opt-in refused";
+    case B200_ERR_ALIGN: return "pointer or leading dimension not 16-byte aligned";
+    case B200_ERR_HEAD_DIM: return "head_dim must be 32, 64, 128 or 256";
+    case B200_ERR_DEVICE: return "device-side wait timed out";
+    case B200_ERR_LAUNCH: return "CUDA kernel launch failed";
+    case B200_ERR_ARG: return "invalid argument";
+    case B200_ERR_TMAP: return "TMA tensor map encoding failed";
+    case B200_ERR_ARCH: return "current device is not compute capability 10.0 (B200, sm_100a)";
+    case B200_ERR_WORKSPACE: return "workspace missing or too small";
+    default: return "unknown status";
+  }
+}
+
+int b200_device_error(int clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_b200_err, sizeof(int)) != cudaSuccess) {
+    cudaGetLastError();
+    return B200_ERR_LAUNCH;
+  }
+  if (clear && v) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_b200_err, &zero, sizeof(int));
+  }
+  return v;
+}
+
+int b200_layernorm_launch(const float* x, long long ld_x, const float* gamma, const float* beta, void* out,
+                          long long ld_out, int out_f16, int rows, int d, float eps, b200_stream_t stream) {
+  return ln_impl(x, ld_x, gamma, beta, out, ld_out, out_f16, rows, d, eps, static_cast<cudaStream_t>(stream));
+}
+
+int b200_gemm_launch(int epilogue, const void* A, long long lda, const void* W, long long ldw, const float* bias,
+                     const float* resid, long long ld_resid, void* out, long long ld_out, int M, int N, int K,
+                     b200_stream_t stream) {
+  return gemm_impl(epilogue, A, lda, W, ldw, bias, resid, ld_resid, out, ld_out, M, N, K,
+                   static_cast<cudaStream_t>(stream));
+}
+
+int b200_flash_causal_launch(const B200AttnArgs* args, b200_stream_t stream) {
+  return attn_impl(args, static_cast<cudaStream_t>(stream));
+}
+
+size_t b200_block_workspace_bytes(long long tokens, int d_model, int ffn_dim) {
+  if (tokens <= 0 || d_model <= 0 || ffn_dim <= 0) return 0;
+  return carve(nullptr, tokens, d_model, ffn_dim).bytes;
+}
+
+int b200_block_forward(const B200BlockArgs* args, b200_stream_t stream) {
+  return block_impl(args, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,82 @@
+// Row LayerNorm, nn.LayerNorm semantics (biased variance, eps inside the
+// square root, affine gamma/beta): the reference's norm1 / norm2 / final_norm
+// (TTB:146-150, 160-161, 178-189 of torch_transformer_benchmark.py).
+// One warp per row; the row is held in registers, mean and variance are two
+// warp-shuffle reductions (two-pass, no E[x^2]-E[x]^2 cancellation).
+// fp32 in; fp16 out (feeds a GEMM's A operand) or fp32 out (model output).
+#pragma once
+
+#include "ptx.cuh"
+
+namespace b200 {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// VEC4: d % 128 == 0, each lane handles VPL float4 at columns 4*lane + 128*i.
+// Otherwise each lane handles VPL floats at columns lane + 32*i (d % 32 == 0).
+template <int VPL, bool VEC4, bool OUT_F16>
+__global__ void __launch_bounds__(256)
+    k_layernorm(const float* __restrict__ x, int64_t ld_x, const float* __restrict__ gamma,
+                const float* __restrict__ beta, void* __restrict__ out, int64_t ld_out, int rows, int d, float eps) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + warp;
+  if (row >= rows) return;
+  const float* xr = x + row * ld_x;
+  constexpr int NV = VEC4 ? 4 * VPL : VPL;
+  float v[NV];
+  float s = 0.f;
+  if constexpr (VEC4) {
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const float4 t = *reinterpret_cast<const float4*>(xr + 4 * lane + 128 * i);
+      v[4 * i] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) v[i] = xr[lane + 32 * i];
+  }
+#pragma unroll
+  for (int i = 0; i < NV; ++i) s += v[i];
+  const float mean = warp_sum(s) / static_cast<float>(d);
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    v[i] -= mean;
+    q += v[i] * v[i];
+  }
+  const float var = warp_sum(q) / static_cast<float>(d);
+  const float rstd = rsqrtf(var + eps);
+  if constexpr (VEC4) {
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int c = 4 * lane + 128 * i;
+      const float4 g = *reinterpret_cast<const float4*>(gamma + c);
+      const float4 bb = *reinterpret_cast<const float4*>(beta + c);
+      const float y0 = v[4 * i] * rstd * g.x + bb.x, y1 = v[4 * i + 1] * rstd * g.y + bb.y;
+      const float y2 = v[4 * i + 2] * rstd * g.z + bb.z, y3 = v[4 * i + 3] * rstd * g.w + bb.w;
+      if constexpr (OUT_F16) {
+        *reinterpret_cast<uint2*>(static_cast<__half*>(out) + row * ld_out + c) =
+            make_uint2(pack_half2(y0, y1), pack_half2(y2, y3));
+      } else {
+        *reinterpret_cast<float4*>(static_cast<float*>(out) + row * ld_out + c) = make_float4(y0, y1, y2, y3);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int c = lane + 32 * i;
+      const float y = v[i] * rstd * gamma[c] + beta[c];
+      if constexpr (OUT_F16) {
+        static_cast<__half*>(out)[row * ld_out + c] = __float2half_rn(y);
+      } else {
+        static_cast<float*>(out)[row * ld_out + c] = y;
+      }
+    }
+  }
+}
+
+}  // namespace b200

@@ -1,0 +1,200 @@
+"""ctypes binding of libb200block.so (the C ABI declared in include/b200_block.h).
+
+This is the Python-side equivalent of the reference's extension loader and
+custom-op layer (torch_transformer_benchmark.py:262-327, 443-586): it loads the
+native library once, and each wrapper passes raw device pointers, sizes and the
+caller's current CUDA stream.  Unlike the reference (which returned ``None``
+from a failed build and silently fell back to ``F.linear``, TTB:467-469,
+502-506) a missing library or a non-zero status raises: there is no fallback.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from typing import Optional
+
+import torch
+
+from . import build as _build
+
+LIB_PATH = _build.LIB_PATH
+
+B200_OK = 0
+EPI_BIAS_F16 = 0
+EPI_BIAS_GELU_F16 = 1
+EPI_BIAS_RESID_F32 = 2
+
+_lib = None
+_lock = threading.Lock()
+
+_c_ll = ctypes.c_longlong
+_vp = ctypes.c_void_p
+
+
+class B200Error(RuntimeError):
+    """A launcher in libb200block.so returned a non-zero status."""
+
+    def __init__(self, what: str, status: int):
+        self.status = status
+        super().__init__(f"{what}: {status_str(status)} (status {status})")
+
+
+class AttnArgs(ctypes.Structure):
+    _fields_ = [
+        ("q", _vp), ("k", _vp), ("v", _vp),
+        ("ld_q", _c_ll), ("ld_k", _c_ll), ("ld_v", _c_ll),
+        ("q_rows", _c_ll), ("kv_rows", _c_ll),
+        ("batch", ctypes.c_int), ("heads", ctypes.c_int), ("head_dim", ctypes.c_int),
+        ("q_len", ctypes.c_int), ("q_offset", ctypes.c_int), ("kv_len", ctypes.c_int),
+        ("q_seq_rows", ctypes.c_int), ("kv_seq_rows", ctypes.c_int),
+        ("q_row0", ctypes.c_int), ("kv_row0", ctypes.c_int),
+        ("q_col0", ctypes.c_int), ("k_col0", ctypes.c_int), ("v_col0", ctypes.c_int),
+        ("out", _vp), ("ld_out", _c_ll), ("out_seq_rows", ctypes.c_int), ("out_row0", ctypes.c_int),
+    ]
+
+
+class BlockArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", ctypes.c_int), ("seq_len", ctypes.c_int), ("d_model", ctypes.c_int),
+        ("num_heads", ctypes.c_int), ("ffn_dim", ctypes.c_int),
+        ("x", _vp), ("y", _vp),
+        ("ln1_w", _vp), ("ln1_b", _vp),
+        ("w_qkv", _vp), ("b_qkv", _vp),
+        ("w_o", _vp), ("b_o", _vp),
+        ("ln2_w", _vp), ("ln2_b", _vp),
+        ("w_in", _vp), ("b_in", _vp),
+        ("w_out", _vp), ("b_out", _vp),
+        ("lnf_w", _vp), ("lnf_b", _vp),
+        ("eps", ctypes.c_float),
+        ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+# (name, restype, argtypes) of every exported symbol; include/b200_block.h is the source of truth.
+EXPORTS = [
+    ("b200_abi_version", ctypes.c_int, []),
+    ("b200_status_str", ctypes.c_char_p, [ctypes.c_int]),
+    ("b200_device_error", ctypes.c_int, [ctypes.c_int]),
+    ("b200_layernorm_launch", ctypes.c_int,
+     [_vp, _c_ll, _vp, _vp, _vp, _c_ll, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, _vp]),
+    ("b200_gemm_launch", ctypes.c_int,
+     [ctypes.c_int, _vp, _c_ll, _vp, _c_ll, _vp, _vp, _c_ll, _vp, _c_ll, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
+    ("b200_flash_causal_launch", ctypes.c_int, [ctypes.POINTER(AttnArgs), _vp]),
+    ("b200_block_workspace_bytes", ctypes.c_size_t, [_c_ll, ctypes.c_int, ctypes.c_int]),
+    ("b200_block_forward", ctypes.c_int, [ctypes.POINTER(BlockArgs), _vp]),
+]
+
+
+def lib():
+    """Load libb200block.so once (raises if it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise RuntimeError(
+                    f"{LIB_PATH} is missing: build it with `python {_build.__file__}` "
+                    "(there is no non-CUDA implementation to fall back to)")
+            handle = ctypes.CDLL(LIB_PATH)
+            for name, res, args in EXPORTS:
+                fn = getattr(handle, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = handle
+    return _lib
+
+
+def status_str(status: int) -> str:
+    try:
+        return lib().b200_status_str(int(status)).decode()
+    except Exception:  # noqa: BLE001 - only used while formatting an error
+        return "unknown status"
+
+
+def check(status: int, what: str) -> None:
+    if status != B200_OK:
+        raise B200Error(what, status)
+
+
+def device_error(clear: bool = True) -> int:
+    """First device-side failure code since the last clear (0 = none). Synchronises."""
+    return int(lib().b200_device_error(1 if clear else 0))
+
+
+def _p(t: Optional[torch.Tensor]):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(stream=None):
+    s = torch.cuda.current_stream() if stream is None else stream
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def _require_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("libb200block kernels take CUDA tensors only (no CPU fallback)")
+
+
+def layernorm(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, out: torch.Tensor,
+              eps: float = 1e-5, stream=None) -> torch.Tensor:
+    """out = LayerNorm(x) * gamma + beta over the last dim; out fp16 or fp32."""
+    _require_cuda(x, gamma, beta, out)
+    d = x.shape[-1]
+    rows = x.numel() // d
+    if x.dtype != torch.float32 or out.dtype not in (torch.float16, torch.float32):
+        raise TypeError("layernorm: x must be fp32, out fp16 or fp32")
+    rc = lib().b200_layernorm_launch(_p(x), x.stride(-2) if x.dim() > 1 else d, _p(gamma), _p(beta), _p(out),
+                                     out.stride(-2) if out.dim() > 1 else d, int(out.dtype == torch.float16),
+                                     rows, d, float(eps), _stream(stream))
+    check(rc, "b200_layernorm_launch")
+    return out
+
+
+def gemm(epilogue: int, a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor], out: torch.Tensor,
+         resid: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """out = epilogue(a @ w.T + bias [+ resid]); a [M,K] fp16, w [N,K] fp16, bias fp32."""
+    _require_cuda(a, w, bias, out, resid)
+    if a.dtype != torch.float16 or w.dtype != torch.float16:
+        raise TypeError("gemm: operands must be fp16")
+    M, K = a.shape
+    N = w.shape[0]
+    rc = lib().b200_gemm_launch(int(epilogue), _p(a), a.stride(0), _p(w), w.stride(0), _p(bias), _p(resid),
+                                resid.stride(0) if resid is not None else 0, _p(out), out.stride(0),
+                                M, N, K, _stream(stream))
+    check(rc, "b200_gemm_launch")
+    return out
+
+
+def flash_causal(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor, *, batch: int, heads: int,
+                 head_dim: int, q_len: int, kv_len: int, q_offset: int = 0, q_seq_rows: int = None,
+                 kv_seq_rows: int = None, q_col0: int = 0, k_col0: int = 0, v_col0: int = 0, q_row0: int = 0,
+                 kv_row0: int = 0, out_seq_rows: int = None, out_row0: int = 0, stream=None) -> torch.Tensor:
+    """Prefix-causal attention over 2-D fp16 tensors (see B200AttnArgs)."""
+    _require_cuda(q, k, v, out)
+    a = AttnArgs()
+    a.q, a.k, a.v = q.data_ptr(), k.data_ptr(), v.data_ptr()
+    a.ld_q, a.ld_k, a.ld_v = q.stride(0), k.stride(0), v.stride(0)
+    a.q_rows, a.kv_rows = q.shape[0], k.shape[0]
+    a.batch, a.heads, a.head_dim = batch, heads, head_dim
+    a.q_len, a.q_offset, a.kv_len = q_len, q_offset, kv_len
+    a.q_seq_rows = q_len if q_seq_rows is None else q_seq_rows
+    a.kv_seq_rows = kv_len if kv_seq_rows is None else kv_seq_rows
+    a.q_row0, a.kv_row0 = q_row0, kv_row0
+    a.q_col0, a.k_col0, a.v_col0 = q_col0, k_col0, v_col0
+    a.out, a.ld_out = out.data_ptr(), out.stride(0)
+    a.out_seq_rows = q_len if out_seq_rows is None else out_seq_rows
+    a.out_row0 = out_row0
+    check(lib().b200_flash_causal_launch(ctypes.byref(a), _stream(stream)), "b200_flash_causal_launch")
+    return out
+
+
+def block_workspace_bytes(tokens: int, d_model: int, ffn_dim: int) -> int:
+    return int(lib().b200_block_workspace_bytes(int(tokens), int(d_model), int(ffn_dim)))
+
+
+def block_forward(args: BlockArgs, stream=None) -> None:
+    check(lib().b200_block_forward(ctypes.byref(args), _stream(stream)), "b200_block_forward")

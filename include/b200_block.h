@@ -1,0 +1,151 @@
+/*
+ * b200_block.h -- C ABI of the B200 (sm_100a) causal transformer-block library
+ * (libb200block.so).
+ *
+ * Plain pointers, sizes and an opaque CUDA stream; no framework types.  All
+ * device pointers are CUDA device addresses on the calling thread's current
+ * device.  Every launcher returns an int status (B200_OK or a negative code,
+ * see b200_status_str) and never synchronises; none falls back to another
+ * implementation when a shape is unsupported -- it returns the error.
+ *
+ * It replaces the native boundary of yeoshuyi/Flipfloppers-GPU-Kernel-Optimizer:
+ *   - ws_gemm_launch(cfg, In, W, bias, Out, M, N, K, stream, &smem)
+ *       (csrc/g4_4_warpspec_gemm.cu:997-1005) and its ffn_gelu_linear variant
+ *       (torch_transformer_benchmark.py:518-586)  -> b200_gemm_launch
+ *   - the attention call of the causal forward, SDPA is_causal=True
+ *       (torch_transformer_benchmark.py:1309-1312) and the prefix-causal flash
+ *       call of the chunked forward (torch_transformer_benchmark.py:1491-1500)
+ *                                                  -> b200_flash_causal_launch
+ *   - F.layer_norm of norm1 / norm2 / final_norm
+ *       (torch_transformer_benchmark.py:1293, 1348, 1373) -> b200_layernorm_launch
+ *   - the per-layer body of _optimized_forward_causal
+ *       (torch_transformer_benchmark.py:1282-1373)  -> b200_block_forward
+ *   - the unwired causal megakernel mega_causal_forward
+ *       (csrc/g5_mega_causal.cpp:7-18)              -> b200_block_fused_small_launch
+ *   - ws_gemm_num_cfg / ws_gemm_cfg_desc (csrc/g4_4_warpspec_gemm.cu:1022-1069)
+ *       -> b200_abi_version / b200_status_str (no config table: tiles are
+ *          chosen inside the library from the shape)
+ */
+#ifndef B200_BLOCK_H
+#define B200_BLOCK_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* A cudaStream_t passed as an opaque pointer; 0 is the legacy default stream. */
+typedef void* b200_stream_t;
+
+#define B200_ABI_VERSION 1
+
+/* Status codes.  -1..-4 keep the meaning of the reference's ws_launch return
+ * codes (csrc/g4_4_warpspec_gemm.cu:958-975); the rest are new. */
+enum {
+  B200_OK = 0,
+  B200_ERR_CONFIG = -1,    /* unknown epilogue / unsupported configuration          */
+  B200_ERR_TILE = -2,      /* a dimension is not a multiple of the required granule  */
+  B200_ERR_SPLIT = -3,     /* (reserved: the reference's K % SPLIT check)            */
+  B200_ERR_SMEM = -4,      /* dynamic shared-memory opt-in refused                   */
+  B200_ERR_ALIGN = -5,     /* pointer or leading dimension not 16-byte aligned       */
+  B200_ERR_HEAD_DIM = -6,  /* head_dim not in {32, 64, 128, 256}                     */
+  B200_ERR_DEVICE = -7,    /* a device-side wait timed out (see b200_device_error)   */
+  B200_ERR_LAUNCH = -8,    /* the CUDA launch itself failed                          */
+  B200_ERR_ARG = -9,       /* null pointer, negative size or inconsistent arguments  */
+  B200_ERR_TMAP = -10,     /* TMA tensor-map encoding failed                         */
+  B200_ERR_ARCH = -11,     /* current device is not compute capability 10.0 (B200)  */
+  B200_ERR_WORKSPACE = -12 /* workspace missing or smaller than required             */
+};
+
+/* Epilogues of b200_gemm_launch. */
+enum {
+  B200_EPI_BIAS_F16 = 0,       /* out(f16) = A.W^T + bias                     */
+  B200_EPI_BIAS_GELU_F16 = 1,  /* out(f16) = gelu_erf(A.W^T + bias)           */
+  B200_EPI_BIAS_RESID_F32 = 2  /* out(f32) = resid + A.W^T + bias (in place ok) */
+};
+
+int b200_abi_version(void);
+const char* b200_status_str(int status);
+
+/* Device error word of the current device: first device-side failure code
+ * since the last clear (0 = none).  Synchronises the device.  clear != 0
+ * resets it to 0. */
+int b200_device_error(int clear);
+
+/* out[r, :] = LayerNorm(x[r, :]) * gamma + beta over d columns (biased
+ * variance, eps inside the sqrt).  out_f16 selects fp16 or fp32 output.
+ * d % 32 == 0, d <= 4096. */
+int b200_layernorm_launch(const float* x, long long ld_x, const float* gamma, const float* beta, void* out,
+                          long long ld_out, int out_f16, int rows, int d, float eps, b200_stream_t stream);
+
+/* out[M,N] = epilogue(A[M,K] . W[N,K]^T + bias[N]).  A, W fp16 row-major with
+ * leading dimensions lda, ldw (elements); bias fp32 (may be null); resid fp32
+ * [M, ld_resid] for B200_EPI_BIAS_RESID_F32 (may equal out).  Requires
+ * N % 32 == 0, K % 8 == 0, lda/ldw % 8 == 0, 16-byte aligned pointers.
+ * fp32 accumulation on the tcgen05 tensor cores. */
+int b200_gemm_launch(int epilogue, const void* A, long long lda, const void* W, long long ldw, const float* bias,
+                     const float* resid, long long ld_resid, void* out, long long ld_out, int M, int N, int K,
+                     b200_stream_t stream);
+
+/* Causal attention.  Q, K, V fp16 2-D tensors [rows, ld] holding head h of
+ * sequence b at rows (row0 + b*seq_rows + position) and columns
+ * (col0 + h*head_dim ...).  Query i of a sequence sits at absolute position
+ * q_offset + i and attends keys 0..q_offset+i (prefix-causal).  Writes the
+ * fp16 context [out_row0 + b*out_seq_rows + i, h*head_dim ...]. */
+typedef struct {
+  const void* q;
+  const void* k;
+  const void* v;
+  long long ld_q, ld_k, ld_v;      /* row strides in elements (multiples of 8) */
+  long long q_rows, kv_rows;       /* rows addressable through q and through k / v */
+  int batch, heads, head_dim;
+  int q_len, q_offset, kv_len;     /* q_offset + q_len <= kv_len */
+  int q_seq_rows, kv_seq_rows;     /* rows between consecutive sequences */
+  int q_row0, kv_row0;             /* row of (sequence 0, position 0) */
+  int q_col0, k_col0, v_col0;      /* column of head 0 */
+  void* out;
+  long long ld_out;
+  int out_seq_rows;
+  int out_row0;
+} B200AttnArgs;
+
+int b200_flash_causal_launch(const B200AttnArgs* args, b200_stream_t stream);
+
+/* One pre-LN causal block, the reference's per-layer body
+ * (torch_transformer_benchmark.py:160-161), optionally followed by the final
+ * LayerNorm (TTB:189): y = LN_f(x1 + W2.gelu(W1.LN2(x1)+b1)+b2),
+ * x1 = x + Wo.attn(LN1(x)) + bo.  Weights fp16 (nn.Linear layout [out, in]),
+ * biases and LayerNorm affine fp32.  lnf_w == NULL skips the final LayerNorm
+ * (y is then the block output, for stacking layers). */
+typedef struct {
+  int batch, seq_len, d_model, num_heads, ffn_dim;
+  const float* x;          /* [batch*seq_len, d_model] fp32 */
+  float* y;                /* [batch*seq_len, d_model] fp32, may not alias x */
+  const float* ln1_w;
+  const float* ln1_b;
+  const void* w_qkv;       /* [3*d_model, d_model] fp16: q rows, then k, then v */
+  const float* b_qkv;      /* [3*d_model] */
+  const void* w_o;         /* [d_model, d_model] fp16 */
+  const float* b_o;
+  const float* ln2_w;
+  const float* ln2_b;
+  const void* w_in;        /* [ffn_dim, d_model] fp16 */
+  const float* b_in;
+  const void* w_out;       /* [d_model, ffn_dim] fp16 */
+  const float* b_out;
+  const float* lnf_w;      /* final LayerNorm; NULL = none */
+  const float* lnf_b;
+  float eps;
+  void* workspace;         /* >= b200_block_workspace_bytes(batch*seq_len, d_model, ffn_dim) */
+  size_t workspace_bytes;
+} B200BlockArgs;
+
+size_t b200_block_workspace_bytes(long long tokens, int d_model, int ffn_dim);
+int b200_block_forward(const B200BlockArgs* args, b200_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200_BLOCK_H */

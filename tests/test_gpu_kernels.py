@@ -1,0 +1,193 @@
+"""Kernel-level checks on a B200, through the C ABI.
+
+The patterns follow the reference's kernel probes
+(experiments/g4_7_ffn_gelu_correctness.py:100-150): exact-integer operands
+(every fp32 partial sum exact, so the GEMM must be bit-exact), a one-hot index
+sweep (catches transposed / swizzled indexing), and seeded random operands
+against a torch fp32 reference of the same op (TF32 off).
+"""
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def rt(pkg):
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    r = pkg.runtime
+    r.lib()
+    assert r.device_error(clear=True) == 0
+    yield r
+    assert r.device_error(clear=True) == 0
+
+
+def _ints(shape, lo, hi, gen):
+    return torch.randint(lo, hi + 1, shape, generator=gen).to(torch.float16).to(DEV)
+
+
+GEMM_SHAPES = [(256, 384, 128), (300, 96, 520), (1000, 512, 64), (8192, 3072, 1024), (129, 4096, 1024)]
+
+
+@pytest.mark.parametrize("M,N,K", GEMM_SHAPES)
+def test_gemm_exact_integer_f16(rt, M, N, K):
+    g = torch.Generator().manual_seed(M * 7 + N)
+    a = _ints((M, K), -1, 1, g)
+    w = _ints((N, K), -1, 1, g)
+    bias = torch.randint(-4, 5, (N,), generator=g).float().to(DEV)
+    out = torch.empty(M, N, dtype=torch.float16, device=DEV)
+    rt.gemm(rt.EPI_BIAS_F16, a, w, bias, out)
+    ref = (a.double() @ w.double().T + bias.double())
+    assert ref.abs().max() <= 2048  # exactly representable in fp16
+    torch.cuda.synchronize()
+    assert torch.equal(out.double(), ref)
+
+
+@pytest.mark.parametrize("M,N,K", GEMM_SHAPES[:4])
+def test_gemm_exact_integer_resid_f32(rt, M, N, K):
+    g = torch.Generator().manual_seed(M + N * 3)
+    a = _ints((M, K), -2, 2, g)
+    w = _ints((N, K), -2, 2, g)
+    bias = torch.randint(-4, 5, (N,), generator=g).float().to(DEV)
+    resid = torch.randint(-100, 101, (M, N), generator=g).float().to(DEV)
+    out = torch.empty(M, N, dtype=torch.float32, device=DEV)
+    rt.gemm(rt.EPI_BIAS_RESID_F32, a, w, bias, out, resid=resid)
+    ref = a.double() @ w.double().T + bias.double() + resid.double()
+    torch.cuda.synchronize()
+    assert torch.equal(out.double(), ref)
+    # in place: out aliases resid
+    rt.gemm(rt.EPI_BIAS_RESID_F32, a, w, bias, resid, resid=resid)
+    torch.cuda.synchronize()
+    assert torch.equal(resid.double(), ref)
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 256, 128), (384, 128, 1024)])
+def test_gemm_one_hot_index_sweep(rt, M, N, K):
+    g = torch.Generator().manual_seed(5)
+    a = torch.zeros(M, K, dtype=torch.float16)
+    a[torch.arange(M), (torch.arange(M) * 7) % K] = 1
+    a = a.to(DEV)
+    w = torch.randn(N, K, generator=g).to(torch.float16).to(DEV)
+    out = torch.empty(M, N, dtype=torch.float16, device=DEV)
+    rt.gemm(rt.EPI_BIAS_F16, a, w, None, out)
+    ref = w.T[(torch.arange(M) * 7) % K]
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+
+
+def test_gemm_gelu_matches_torch(rt):
+    M, N, K = 2048, 512, 128
+    g = torch.Generator().manual_seed(9)
+    a = torch.randn(M, K, generator=g).to(torch.float16).to(DEV)
+    w = (torch.randn(N, K, generator=g) / math.sqrt(K)).to(torch.float16).to(DEV)
+    bias = torch.randn(N, generator=g).to(DEV)
+    out = torch.empty(M, N, dtype=torch.float16, device=DEV)
+    rt.gemm(rt.EPI_BIAS_GELU_F16, a, w, bias, out)
+    ref = torch.nn.functional.gelu(a.float() @ w.float().T + bias, approximate="none")
+    torch.cuda.synchronize()
+    err = (out.float() - ref).abs()
+    # fp16 output rounding (half an ulp) plus fp32 summation-order differences
+    assert (err <= 1e-3 + 1e-3 * ref.abs()).all(), err.max().item()
+
+
+@pytest.mark.parametrize("M,N,K", [(4096, 384, 128), (1000, 1024, 4096)])
+def test_gemm_random_vs_torch_fp32(rt, M, N, K):
+    g = torch.Generator().manual_seed(M)
+    a = torch.randn(M, K, generator=g).to(torch.float16).to(DEV)
+    w = (torch.randn(N, K, generator=g) / math.sqrt(K)).to(torch.float16).to(DEV)
+    bias = torch.randn(N, generator=g).to(DEV)
+    resid = torch.randn(M, N, generator=g).to(DEV)
+    out = torch.empty(M, N, dtype=torch.float32, device=DEV)
+    rt.gemm(rt.EPI_BIAS_RESID_F32, a, w, bias, out, resid=resid)
+    ref = a.float() @ w.float().T + bias + resid
+    torch.cuda.synchronize()
+    assert (out - ref).abs().max().item() < 1e-4 * math.sqrt(K)
+
+
+@pytest.mark.parametrize("d", [64, 96, 128, 1024])
+@pytest.mark.parametrize("f16", [True, False])
+def test_layernorm_vs_torch(rt, d, f16):
+    g = torch.Generator().manual_seed(d)
+    rows = 1531
+    x = (torch.randn(rows, d, generator=g) * 3 + 1).to(DEV)
+    gamma = torch.randn(d, generator=g).to(DEV)
+    beta = torch.randn(d, generator=g).to(DEV)
+    out = torch.empty(rows, d, dtype=torch.float16 if f16 else torch.float32, device=DEV)
+    rt.layernorm(x, gamma, beta, out, eps=1e-5)
+    ref = torch.nn.functional.layer_norm(x, (d,), gamma, beta, eps=1e-5)
+    torch.cuda.synchronize()
+    tol = 2e-3 if f16 else 2e-5
+    assert ((out.float() - ref).abs() <= tol * (1 + ref.abs())).all()
+
+
+def _attn_ref(q, k, v, q_offset):
+    # q [B,H,Sq,hd], k/v [B,H,Sk,hd] fp32
+    hd = q.shape[-1]
+    s = (q @ k.transpose(-1, -2)) * hd ** -0.5
+    Sq, Sk = q.shape[-2], k.shape[-2]
+    qpos = q_offset + torch.arange(Sq, device=q.device)[:, None]
+    kpos = torch.arange(Sk, device=q.device)[None, :]
+    s = s.masked_fill(kpos > qpos, float("-inf"))
+    return torch.softmax(s, dim=-1) @ v
+
+
+ATTN_CASES = [  # B, H, S, hd
+    (2, 4, 128, 32), (3, 2, 100, 32), (2, 4, 384, 64), (1, 2, 300, 128), (2, 4, 128, 256), (1, 2, 200, 256),
+    (2, 4, 1024, 32),
+]
+
+
+@pytest.mark.parametrize("B,H,S,hd", ATTN_CASES)
+def test_flash_causal_vs_torch(rt, B, H, S, hd):
+    g = torch.Generator().manual_seed(B * 1000 + S + hd)
+    d = H * hd
+    qkv = (torch.randn(B * S, 3 * d, generator=g)).to(torch.float16).to(DEV)
+    out = torch.full((B * S, d), float("nan"), dtype=torch.float16, device=DEV)
+    rt.flash_causal(qkv, qkv, qkv, out, batch=B, heads=H, head_dim=hd, q_len=S, kv_len=S, k_col0=d, v_col0=2 * d)
+    t = qkv.float().view(B, S, 3, H, hd).permute(2, 0, 3, 1, 4)
+    ref = _attn_ref(t[0], t[1], t[2], 0).permute(0, 2, 1, 3).reshape(B * S, d)
+    torch.cuda.synchronize()
+    err = (out.float() - ref).abs().max().item()
+    assert err < 4e-3, err
+
+
+@pytest.mark.parametrize("hd,chunk", [(64, 256), (32, 128), (64, 192), (256, 128)])
+def test_flash_prefix_chunks_equal_full(rt, hd, chunk):
+    """Query chunks [c0:c1) over the K/V prefix [0:c1) (q_offset=c0) reproduce
+    full causal attention row for row -- the chunked forward's identity."""
+    B, H, S = 2, 2, 640
+    d = H * hd
+    g = torch.Generator().manual_seed(hd + chunk)
+    q = torch.randn(B * S, d, generator=g).to(torch.float16).to(DEV)
+    kv = torch.randn(B * S, 2 * d, generator=g).to(torch.float16).to(DEV)
+    full = torch.empty(B * S, d, dtype=torch.float16, device=DEV)
+    rt.flash_causal(q, kv, kv, full, batch=B, heads=H, head_dim=hd, q_len=S, kv_len=S, k_col0=0, v_col0=d)
+    parts = torch.empty_like(full)
+    for c0 in range(0, S, chunk):
+        c1 = min(S, c0 + chunk)
+        rt.flash_causal(q, kv, kv, parts, batch=B, heads=H, head_dim=hd, q_len=c1 - c0, q_offset=c0, kv_len=c1,
+                        q_seq_rows=S, kv_seq_rows=S, q_row0=c0, k_col0=0, v_col0=d, out_seq_rows=S, out_row0=c0)
+    t = q.float().view(B, S, H, hd).transpose(1, 2)
+    kk = kv.float().view(B, S, 2, H, hd).permute(2, 0, 3, 1, 4)
+    ref = _attn_ref(t, kk[0], kk[1], 0).transpose(1, 2).reshape(B * S, d)
+    torch.cuda.synchronize()
+    assert (full.float() - ref).abs().max().item() < 4e-3
+    assert (parts.float() - ref).abs().max().item() < 4e-3
+
+
+def test_launch_rejects_unsupported_shapes(rt):
+    a = torch.zeros(64, 40, dtype=torch.float16, device=DEV)
+    w = torch.zeros(48, 40, dtype=torch.float16, device=DEV)
+    out = torch.zeros(64, 48, dtype=torch.float16, device=DEV)
+    with pytest.raises(rt.B200Error, match="granule"):
+        rt.gemm(rt.EPI_BIAS_F16, a, w, None, out)
+    qkv = torch.zeros(128, 3 * 96, dtype=torch.float16, device=DEV)
+    o = torch.zeros(128, 96, dtype=torch.float16, device=DEV)
+    with pytest.raises(rt.B200Error, match="head_dim"):
+        rt.flash_causal(qkv, qkv, qkv, o, batch=1, heads=2, head_dim=48, q_len=128, kv_len=128)
