@@ -20,8 +20,6 @@
  *       (torch_transformer_benchmark.py:1293, 1348, 1373) -> b200_layernorm_launch
  *   - the per-layer body of _optimized_forward_causal
  *       (torch_transformer_benchmark.py:1282-1373)  -> b200_block_forward
- *   - the unwired causal megakernel mega_causal_forward
- *       (csrc/g5_mega_causal.cpp:7-18)              -> b200_block_fused_small_launch
  *   - ws_gemm_num_cfg / ws_gemm_cfg_desc (csrc/g4_4_warpspec_gemm.cu:1022-1069)
  *       -> b200_abi_version / b200_status_str (no config table: tiles are
  *          chosen inside the library from the shape)
