@@ -380,6 +380,10 @@ const char* b200_status_str(int s) {
     case B200_ERR_TMAP: return "TMA tensor map encoding failed";
     case B200_ERR_ARCH: return "current device is not compute capability 10.0 (B200, sm_100a)";
     case B200_ERR_WORKSPACE: return "workspace missing or too small";
+    case B200_ERR_NOALLOC_LIMIT:
+      return "problem needs more scratch than the no-allocation entry point's static buffer "
+             "(B200_NOALLOC_SCRATCH_BYTES = 32 MiB); use b200_block_forward with a workspace";
+    case B200_ERR_SCRATCH_SETUP: return "could not resolve the static scratch buffer's device address";
     default: return "unknown status";
   }
 }
@@ -423,3 +427,47 @@ int b200_block_forward(const B200BlockArgs* args, b200_stream_t stream) {
 }
 
 }  // extern "C"
+
+// ====================================================================== no-allocation entry point
+// Scratch for b200_block_forward_noalloc: one static device buffer per GPU
+// that loads the library, held until exit.  In host code `g_noalloc_scratch`
+// names a host-side stand-in, not a device address; its device address is
+// looked up with cudaGetSymbolAddress once per device (with that device
+// current) and that address is what the kernels are given.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[B200_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+void* g_noalloc_addr[128] = {nullptr};
+
+int noalloc_scratch_addr(void** out) {
+  const int dev = current_device();
+  if (dev < 0 || dev >= 128) return B200_ERR_SCRATCH_SETUP;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      cudaGetLastError();
+      return B200_ERR_SCRATCH_SETUP;
+    }
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return B200_OK;
+}
+}  // namespace
+
+extern "C" int b200_block_forward_noalloc(const B200BlockArgs* args, b200_stream_t stream) {
+  if (!args || args->batch <= 0 || args->seq_len <= 0 || args->d_model <= 0 || args->ffn_dim <= 0)
+    return B200_ERR_ARG;
+  const long long tokens = static_cast<long long>(args->batch) * args->seq_len;
+  if (carve(nullptr, tokens, args->d_model, args->ffn_dim).bytes > B200_NOALLOC_SCRATCH_BYTES)
+    return B200_ERR_NOALLOC_LIMIT;
+  if (int rc = check_arch()) return rc;
+  void* scratch = nullptr;
+  if (int rc = noalloc_scratch_addr(&scratch)) return rc;
+  B200BlockArgs a = *args;
+  a.workspace = scratch;
+  a.workspace_bytes = B200_NOALLOC_SCRATCH_BYTES;
+  return block_impl(&a, static_cast<cudaStream_t>(stream));
+}

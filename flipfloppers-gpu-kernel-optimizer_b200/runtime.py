@@ -84,6 +84,7 @@ EXPORTS = [
     ("b200_flash_causal_launch", ctypes.c_int, [ctypes.POINTER(AttnArgs), _vp]),
     ("b200_block_workspace_bytes", ctypes.c_size_t, [_c_ll, ctypes.c_int, ctypes.c_int]),
     ("b200_block_forward", ctypes.c_int, [ctypes.POINTER(BlockArgs), _vp]),
+    ("b200_block_forward_noalloc", ctypes.c_int, [ctypes.POINTER(BlockArgs), _vp]),
 ]
 
 
@@ -198,3 +199,14 @@ def block_workspace_bytes(tokens: int, d_model: int, ffn_dim: int) -> int:
 
 def block_forward(args: BlockArgs, stream=None) -> None:
     check(lib().b200_block_forward(ctypes.byref(args), _stream(stream)), "b200_block_forward")
+
+
+# Size of the static scratch buffer behind b200_block_forward_noalloc (B200_NOALLOC_SCRATCH_BYTES).
+NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024
+
+
+def block_forward_noalloc(args: BlockArgs, stream=None) -> None:
+    """b200_block_forward without a workspace: for callers that cannot allocate device
+    memory (the library's static 32 MiB buffer holds the intermediates; calls that
+    overlap on the GPU race on it).  args.workspace is ignored."""
+    check(lib().b200_block_forward_noalloc(ctypes.byref(args), _stream(stream)), "b200_block_forward_noalloc")

@@ -53,7 +53,9 @@ enum {
   B200_ERR_ARG = -9,       /* null pointer, negative size or inconsistent arguments  */
   B200_ERR_TMAP = -10,     /* TMA tensor-map encoding failed                         */
   B200_ERR_ARCH = -11,     /* current device is not compute capability 10.0 (B200)  */
-  B200_ERR_WORKSPACE = -12 /* workspace missing or smaller than required             */
+  B200_ERR_WORKSPACE = -12, /* workspace missing or smaller than required            */
+  B200_ERR_NOALLOC_LIMIT = -13, /* problem needs more scratch than B200_NOALLOC_SCRATCH_BYTES */
+  B200_ERR_SCRATCH_SETUP = -14  /* the static scratch buffer's device address could not be resolved */
 };
 
 /* Epilogues of b200_gemm_launch. */
@@ -141,6 +143,30 @@ typedef struct {
 
 size_t b200_block_workspace_bytes(long long tokens, int d_model, int ffn_dim);
 int b200_block_forward(const B200BlockArgs* args, b200_stream_t stream);
+
+/* Same computation as b200_block_forward, for callers that cannot allocate
+ * device memory: a plugin host whose memory belongs to someone else's pool
+ * and that hands out no workspace, a foreign-language caller with no CUDA
+ * allocator of its own, or a latency-critical loop that cannot afford the
+ * implicit device synchronisation of cudaMalloc/cudaFree.  It allocates
+ * nothing: the intermediates live in one static device buffer of
+ * B200_NOALLOC_SCRATCH_BYTES that the library defines, which every GPU that
+ * loads the library holds until the process exits.  The caller still passes
+ * x, y and the weights; args->workspace and args->workspace_bytes are ignored.
+ *
+ * Limit: b200_block_workspace_bytes(batch*seq_len, d_model, ffn_dim) must not
+ * exceed B200_NOALLOC_SCRATCH_BYTES (e.g. up to 11915 tokens at d_model=128,
+ * ffn_dim=512); larger problems return B200_ERR_NOALLOC_LIMIT before anything
+ * is launched.
+ * Set-up: the first call on a device (with that device current) looks up the
+ * buffer's device address; make that first call before any stream capture.
+ * Sharing: every call on a device uses the same buffer, which keeps the last
+ * call's contents (nothing in it needs to start at zero: every region is
+ * written before it is read).  Calls whose work overlaps on the GPU (other
+ * streams, other host threads) race on the buffer; serialise them.
+ * No counterpart in the reference: its extensions allocate through PyTorch. */
+#define B200_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
+int b200_block_forward_noalloc(const B200BlockArgs* args, b200_stream_t stream);
 
 #ifdef __cplusplus
 }
