@@ -16,6 +16,7 @@
 #include "ln.cuh"
 #include "gemm.cuh"
 #include "attn.cuh"
+#include "fused_small.cuh"
 
 using namespace b200;
 
@@ -265,6 +266,62 @@ int attn_impl(const B200AttnArgs* a, cudaStream_t st) {
   }
 }
 
+// ------------------------------------------------------------------ fused small-model kernel
+int num_sms() {
+  int dev = current_device(), n = 0;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+int fused_small_impl(const B200FusedSmallArgs* a, cudaStream_t st) {
+  if (!a || !a->x || !a->y || !a->w_qkv || !a->w_o || !a->w_in || !a->w_out) return B200_ERR_ARG;
+  if (!a->ln1_w || !a->ln1_b || !a->ln2_w || !a->ln2_b || !a->lnf_w || !a->lnf_b || !a->b_qkv || !a->b_o ||
+      !a->b_in || !a->b_out)
+    return B200_ERR_ARG;
+  if (a->batch <= 0 || a->seq_len <= 0 || a->num_layers <= 0) return B200_ERR_ARG;
+  if (a->d_model != 128 || a->num_heads != 4 || a->ffn_dim <= 0 || a->ffn_dim % 128 || a->ffn_dim > 512 ||
+      a->seq_len > 128)
+    return B200_ERR_CONFIG;
+  if (a->x == a->y) return B200_ERR_ARG;
+  if (!al16(a->x) || !al16(a->y) || !al16(a->w_qkv) || !al16(a->w_o) || !al16(a->w_in) || !al16(a->w_out))
+    return B200_ERR_ALIGN;
+  const float* vecs[] = {a->ln1_w, a->ln1_b, a->ln2_w, a->ln2_b, a->lnf_w, a->lnf_b, a->b_qkv, a->b_o, a->b_in, a->b_out};
+  for (const float* v : vecs)
+    if (!al16(v)) return B200_ERR_ALIGN;
+  if (static_cast<long long>(a->batch) * a->seq_len > 0x7fffffffLL) return B200_ERR_TILE;
+  if (int rc = check_arch()) return rc;
+  const int L = a->num_layers, F = a->ffn_dim;
+  CUtensorMap tq, to, ti, tout;
+  if (int rc = make_map_f16(&tq, a->w_qkv, static_cast<uint64_t>(L) * 384, 128, 128, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
+  if (int rc = make_map_f16(&to, a->w_o, static_cast<uint64_t>(L) * 128, 128, 128, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
+  if (int rc = make_map_f16(&ti, a->w_in, static_cast<uint64_t>(L) * F, 128, 128, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
+  if (int rc = make_map_f16(&tout, a->w_out, static_cast<uint64_t>(L) * 128, F, F, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
+  SmallParams p{};
+  p.num_seq = a->batch;
+  p.seq_len = a->seq_len;
+  p.layers = L;
+  p.ffn = F;
+  p.x = a->x;
+  p.y = a->y;
+  p.ln1_w = a->ln1_w;
+  p.ln1_b = a->ln1_b;
+  p.b_qkv = a->b_qkv;
+  p.b_o = a->b_o;
+  p.ln2_w = a->ln2_w;
+  p.ln2_b = a->ln2_b;
+  p.b_in = a->b_in;
+  p.b_out = a->b_out;
+  p.lnf_w = a->lnf_w;
+  p.lnf_b = a->lnf_b;
+  p.eps = a->eps;
+  p.scale_log2 = static_cast<float>(1.4426950408889634 / __builtin_sqrt(32.0));
+  const int smem = SmallCfg::TOTAL;
+  if (int rc = set_smem(reinterpret_cast<const void*>(k_block_small), smem)) return rc;
+  const int grid = a->batch < num_sms() ? a->batch : num_sms();
+  k_block_small<<<grid, SmallCfg::THREADS, smem, st>>>(tq, to, ti, tout, p);
+  return launch_status();
+}
+
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
 struct BlockWs {
@@ -424,6 +481,10 @@ size_t b200_block_workspace_bytes(long long tokens, int d_model, int ffn_dim) {
 
 int b200_block_forward(const B200BlockArgs* args, b200_stream_t stream) {
   return block_impl(args, static_cast<cudaStream_t>(stream));
+}
+
+int b200_block_fused_small_launch(const B200FusedSmallArgs* args, b200_stream_t stream) {
+  return fused_small_impl(args, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -1,0 +1,508 @@
+// Fused causal block for small models: d_model = 128, 4 heads of 32,
+// ffn_dim in {128, 256, 384, 512}, seq_len <= 128, any number of layers.
+//
+// This is the B200 counterpart of the reference's unwired megakernel
+// (csrc/g5_mega_causal.cu:160-290, one CTA per sequence, residual on chip,
+// hard-specialised to d=128) and of its causal forward (TTB:1282-1373): one
+// persistent CTA per SM walks sequences; for each sequence and layer the whole
+// pre-LN block runs on chip -- LN1, QKV projection, 4-head causal attention,
+// out_proj + residual, LN2, ffn_in + erf-GELU, ffn_out + residual, and the
+// final LayerNorm after the last layer.  Only x is read and y written in HBM;
+// weights (384 KB per layer at ffn=512) are streamed from L2 by TMA.
+//
+// Roles (18 warps):
+//   warp 0      TMA producer: 128x64 fp16 weight boxes (SWIZZLE_128B) through a
+//               3-stage ring, in exactly the order the MMA warp consumes them;
+//   warp 1      TMEM owner (512 columns) and tcgen05.mma issuer;
+//   warps 2-17  workers: warp w owns TMEM lane quadrant q = w%4 (rows
+//               32q..32q+31, one row per lane) and column group g = (w-2)/4
+//               (32 of the 128 columns; in attention g is also the head).
+//               Row statistics (LayerNorm mean/variance, softmax max/sum) are
+//               combined across the 4 groups of a row in shared memory behind
+//               one named barrier per quadrant.
+//
+// TMEM columns:  [0,384) QKV accumulator | then [0,128),[128,256) S of two
+//   heads in flight, [256,384) O of the 4 heads, [384,512) out_proj
+//   accumulator, overwritten in place by the fp32 residual x1 | then
+//   [0,128),[128,256) ffn_in chunk accumulators (ping-pong), [256,384) ffn_out
+//   accumulator.
+// Shared memory (1 CTA/SM): XA 32 KB (LN1 out -> context -> LN2 out, fp16,
+//   SW128 K-major), Q/K/V 3 x 4 heads x 8 KB (SW64; V read MN-major), P 32 KB,
+//   weight ring 48 KB, GELU chunk ping-pong aliasing the Q and K areas.
+//
+// Every wait is bounded (ptx.cuh); a worker that gives up still executes every
+// named barrier (control flow never depends on data), so the CTA always
+// reaches its teardown.
+#pragma once
+
+#include "ptx.cuh"
+
+namespace b200 {
+
+struct SmallParams {
+  int num_seq;        // sequences
+  int seq_len;        // rows per sequence (<= 128)
+  int layers;
+  int ffn;            // multiple of 128, <= 512
+  const float* x;     // [num_seq*seq_len, 128]
+  float* y;           // [num_seq*seq_len, 128]; holds the residual between layers
+  const float* ln1_w; const float* ln1_b;   // [layers, 128]
+  const float* b_qkv;                       // [layers, 384]
+  const float* b_o;                         // [layers, 128]
+  const float* ln2_w; const float* ln2_b;   // [layers, 128]
+  const float* b_in;                        // [layers, ffn]
+  const float* b_out;                       // [layers, 128]
+  const float* lnf_w; const float* lnf_b;   // [128]
+  float eps;
+  float scale_log2;   // 32^-0.5 * log2(e)
+};
+
+struct SmallCfg {
+  static constexpr int D = 128;
+  static constexpr int NW = 16;                 // worker warps
+  static constexpr int THREADS = 32 * (2 + NW);
+  static constexpr int WST = 3;                 // weight ring stages
+  static constexpr int BOX = 128 * 64 * 2;      // one 128x64 fp16 weight box
+  static constexpr int OFF_XA = 0;              // 32 KB
+  static constexpr int OFF_Q = 32768;           // 4 x 8 KB
+  static constexpr int OFF_K = 65536;
+  static constexpr int OFF_V = 98304;
+  static constexpr int OFF_P = 131072;          // 32 KB
+  static constexpr int OFF_W = 163840;          // WST x 16 KB
+  static constexpr int OFF_STATS = OFF_W + WST * BOX;   // float [2][4][128]
+  static constexpr int OFF_BAR = OFF_STATS + 2 * 4 * 128 * 4;
+  static constexpr int TOTAL = OFF_BAR + 512 + 1024;
+};
+
+// Barrier slots
+enum SmallBar : int {
+  SB_WFULL = 0,        // [WST]
+  SB_WEMPTY = 3,       // [WST]
+  SB_N1 = 6,           // workers: LN1 output in XA
+  SB_QKV_DONE = 7,     // MMA: QKV accumulator complete
+  SB_QKV_SMEM = 8,     // workers: Q/K/V in shared memory, QKV TMEM read
+  SB_S_FULL = 9,       // [2] MMA: S of a head complete
+  SB_P_FULL = 11,      // workers: P of a head in shared memory
+  SB_PV_DONE = 12,     // MMA: O += P.V of a head complete
+  SB_CTX = 13,         // workers: context in XA
+  SB_OP_DONE = 14,     // MMA: out_proj accumulator complete
+  SB_N2 = 15,          // workers: LN2 output in XA, x1 in TMEM
+  SB_FIN = 16,         // [2] MMA: ffn_in chunk accumulator complete
+  SB_H = 18,           // [2] workers: GELU chunk in shared memory
+  SB_HFREE = 20,       // [2] MMA: ffn_out consumed a GELU chunk buffer
+  SB_FOUT = 22,        // MMA: ffn_out accumulator complete
+  SB_DRAIN = 23,
+  SB_COUNT = 24
+};
+
+__device__ __forceinline__ void named_bar(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// completion parity of the idx-th completion (within one sequence-layer step)
+// of a barrier that completes `per` times per step, at step `step`
+__device__ __forceinline__ uint32_t par(int step, int per, int idx) {
+  return static_cast<uint32_t>((step * per + idx) & 1);
+}
+
+__global__ void __maxnreg__(112)
+    k_block_small(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_o,
+                  const __grid_constant__ CUtensorMap tm_in, const __grid_constant__ CUtensorMap tm_out,
+                  const SmallParams p) {
+  using C = SmallCfg;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + SB_COUNT);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* stats = reinterpret_cast<float*>(smem + C::OFF_STATS);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nch = p.ffn / 128;                              // ffn chunks of 128
+  const int nseq_cta = (p.num_seq - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                       static_cast<int>(gridDim.x);         // sequences this CTA handles
+  const int nsteps = nseq_cta * p.layers;
+  // completions per step of the ping-pong barriers (buffer b serves chunks b, b+2, ...)
+  const int per_b0 = (nch + 1) / 2, per_b1 = nch / 2;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::WST; ++s) {
+      mbar_init(&bar[SB_WFULL + s], 1);
+      mbar_init(&bar[SB_WEMPTY + s], 1);
+    }
+    mbar_init(&bar[SB_N1], 32 * C::NW);
+    mbar_init(&bar[SB_QKV_DONE], 1);
+    mbar_init(&bar[SB_QKV_SMEM], 32 * C::NW);
+    mbar_init(&bar[SB_S_FULL + 0], 1);
+    mbar_init(&bar[SB_S_FULL + 1], 1);
+    mbar_init(&bar[SB_P_FULL], 32 * C::NW);
+    mbar_init(&bar[SB_PV_DONE], 1);
+    mbar_init(&bar[SB_CTX], 32 * C::NW);
+    mbar_init(&bar[SB_OP_DONE], 1);
+    mbar_init(&bar[SB_N2], 32 * C::NW);
+    mbar_init(&bar[SB_FIN + 0], 1);
+    mbar_init(&bar[SB_FIN + 1], 1);
+    mbar_init(&bar[SB_H + 0], 32 * C::NW);
+    mbar_init(&bar[SB_H + 1], 32 * C::NW);
+    mbar_init(&bar[SB_HFREE + 0], 1);
+    mbar_init(&bar[SB_HFREE + 1], 1);
+    mbar_init(&bar[SB_FOUT], 1);
+    mbar_init(&bar[SB_DRAIN], 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_qkv);
+      tma_prefetch_desc(&tm_o);
+      tma_prefetch_desc(&tm_in);
+      tma_prefetch_desc(&tm_out);
+      int box = 0;
+      bool ok = true;
+      auto load = [&](const CUtensorMap* m, int col, int row) {
+        const int s = box % C::WST;
+        if (box >= C::WST && !mbar_wait(&bar[SB_WEMPTY + s], ((box / C::WST) - 1) & 1, abort_flag, DERR_WAIT_SLOT)) {
+          ok = false;
+          return;
+        }
+        mbar_arrive_expect_tx(&bar[SB_WFULL + s], C::BOX);
+        tma_load_2d(smem + C::OFF_W + s * C::BOX, m, &bar[SB_WFULL + s], col, row);
+        ++box;
+      };
+      for (int step = 0; ok && step < nsteps; ++step) {
+        const int l = step % p.layers;
+        for (int nt = 0; ok && nt < 3; ++nt)
+          for (int kh = 0; ok && kh < 2; ++kh) load(&tm_qkv, kh * 64, l * 384 + nt * 128);
+        for (int kh = 0; ok && kh < 2; ++kh) load(&tm_o, kh * 64, l * 128);
+        for (int kh = 0; ok && kh < 2; ++kh) load(&tm_in, kh * 64, l * p.ffn);
+        for (int c = 0; ok && c < nch; ++c) {
+          if (c + 1 < nch)
+            for (int kh = 0; ok && kh < 2; ++kh) load(&tm_in, kh * 64, l * p.ffn + (c + 1) * 128);
+          for (int kh = 0; ok && kh < 2; ++kh) load(&tm_out, c * 128 + kh * 64, l * 128);
+        }
+      }
+      if (*abort_flag)
+        for (int b = (box > C::WST ? box - C::WST : 0); b < box; ++b)
+          mbar_wait_drain(&bar[SB_WFULL + b % C::WST], (b / C::WST) & 1);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t ID_N128 = make_idesc_f16(128, 128, false);
+      constexpr uint32_t ID_PV = make_idesc_f16(128, 32, true);
+      const uint32_t xa = smem_u32(smem + C::OFF_XA);
+      const uint32_t qs = smem_u32(smem + C::OFF_Q), ks = smem_u32(smem + C::OFF_K), vs = smem_u32(smem + C::OFF_V);
+      const uint32_t ps = smem_u32(smem + C::OFF_P);
+      const uint32_t ws = smem_u32(smem + C::OFF_W);
+      int box = 0;
+      bool ok = true;
+      // D[tmem_col] (+)= A(128x128, SW128 K-major at a) . W-box^T over two 64-wide K halves
+      auto gemm_k128 = [&](uint32_t a, uint32_t dcol, bool acc_in) {
+        for (int kh = 0; kh < 2 && ok; ++kh) {
+          const int s = box % C::WST;
+          if (!mbar_wait(&bar[SB_WFULL + s], (box / C::WST) & 1, abort_flag, DERR_WAIT_TMA)) {
+            ok = false;
+            return;
+          }
+          tc_fence_after();
+          const uint32_t w = ws + s * C::BOX;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_f16_ss(tmem + dcol, make_sdesc(a + kh * 16384 + kk * 32, 16, 1024, UMMA_SW128),
+                        make_sdesc(w + kk * 32, 16, 1024, UMMA_SW128), ID_N128, (acc_in || kh || kk) ? 1u : 0u);
+          tc_commit(&bar[SB_WEMPTY + s]);
+          ++box;
+        }
+      };
+      auto issue_s = [&](int h) {
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk)
+          umma_f16_ss(tmem + (h & 1) * 128, make_sdesc(qs + h * 8192 + kk * 32, 16, 512, UMMA_SW64),
+                      make_sdesc(ks + h * 8192 + kk * 32, 16, 512, UMMA_SW64), ID_N128, kk ? 1u : 0u);
+        tc_commit(&bar[SB_S_FULL + (h & 1)]);
+      };
+      for (int step = 0; ok && step < nsteps; ++step) {
+        // QKV projection
+        if (!mbar_wait(&bar[SB_N1], par(step, 1, 0), abort_flag, DERR_WAIT_SOFTMAX)) break;
+        tc_fence_after();
+        for (int nt = 0; nt < 3 && ok; ++nt) gemm_k128(xa, nt * 128, false);
+        if (!ok) break;
+        tc_commit(&bar[SB_QKV_DONE]);
+        // attention: S of heads 0 and 1, then per head PV and the S two heads ahead
+        if (!mbar_wait(&bar[SB_QKV_SMEM], par(step, 1, 0), abort_flag, DERR_WAIT_SOFTMAX)) break;
+        tc_fence_after();
+        issue_s(0);
+        issue_s(1);
+        for (int h = 0; h < 4 && ok; ++h) {
+          if (!mbar_wait(&bar[SB_P_FULL], par(step, 4, h), abort_flag, DERR_WAIT_SOFTMAX)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_f16_ss(tmem + 256 + 32 * h,
+                        make_sdesc(ps + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024, UMMA_SW128),
+                        make_sdesc(vs + h * 8192 + kk * 16 * 64, 128 * 64, 512, UMMA_SW64), ID_PV, kk ? 1u : 0u);
+          tc_commit(&bar[SB_PV_DONE]);
+          if (h + 2 < 4) issue_s(h + 2);
+        }
+        if (!ok) break;
+        // out_proj
+        if (!mbar_wait(&bar[SB_CTX], par(step, 1, 0), abort_flag, DERR_WAIT_SOFTMAX)) break;
+        tc_fence_after();
+        gemm_k128(xa, 384, false);
+        if (!ok) break;
+        tc_commit(&bar[SB_OP_DONE]);
+        // FFN: fin_0, then per chunk c: fin_{c+1}, fout_c
+        if (!mbar_wait(&bar[SB_N2], par(step, 1, 0), abort_flag, DERR_WAIT_SOFTMAX)) break;
+        tc_fence_after();
+        gemm_k128(xa, 0, false);
+        if (!ok) break;
+        tc_commit(&bar[SB_FIN + 0]);
+        for (int c = 0; c < nch && ok; ++c) {
+          if (c + 1 < nch) {
+            gemm_k128(xa, ((c + 1) & 1) * 128, false);
+            if (!ok) break;
+            tc_commit(&bar[SB_FIN + ((c + 1) & 1)]);
+          }
+          const int b = c & 1;
+          if (!mbar_wait(&bar[SB_H + b], par(step, b ? per_b1 : per_b0, c >> 1), abort_flag, DERR_WAIT_SOFTMAX)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          gemm_k128(smem_u32(smem + (b ? C::OFF_K : C::OFF_Q)), 256, c > 0);
+          if (!ok) break;
+          tc_commit(&bar[SB_HFREE + b]);
+        }
+        if (!ok) break;
+        tc_commit(&bar[SB_FOUT]);
+      }
+      if (*abort_flag) {
+        tc_commit(&bar[SB_DRAIN]);
+        mbar_wait_drain(&bar[SB_DRAIN], 0);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ workers
+    const int q = warp & 3;
+    const int g = (warp - 2) >> 2;       // column group (32 columns; head g in attention)
+    const int r = q * 32 + lane;         // row of the tile (TMEM lane)
+    const int c0 = 32 * g;               // first column of this thread
+    const int bar_id = 1 + q;            // named barrier of the quadrant (4 warps)
+    const uint32_t trow = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    float* st0 = stats;                  // [4][128]
+    float* st1 = stats + 512;
+    uint8_t* xa = smem + C::OFF_XA;
+    bool ok = true;
+    float v[32];
+
+    auto wait_w = [&](int slot, uint32_t parity) {
+      if (ok) ok = mbar_wait_warp(&bar[slot], parity, abort_flag, DERR_WAIT_MMA);
+      if (ok) tc_fence_after();
+    };
+    // sum of one per-thread partial over the 4 column groups of the row
+    auto row_sum = [&](float part, float* buf) {
+      buf[g * 128 + r] = part;
+      named_bar(bar_id, 128);
+      return buf[r] + buf[128 + r] + buf[256 + r] + buf[384 + r];
+    };
+    auto row_max = [&](float part, float* buf) {
+      buf[g * 128 + r] = part;
+      named_bar(bar_id, 128);
+      return fmaxf(fmaxf(buf[r], buf[128 + r]), fmaxf(buf[256 + r], buf[384 + r]));
+    };
+    // LayerNorm of v (32 columns of this row) in place, two-pass statistics
+    auto layer_norm = [&](const float* gamma, const float* beta) {
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) s += v[i];
+      const float mean = row_sum(s, st0) * (1.f / 128.f);
+      float qq = 0.f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        v[i] -= mean;
+        qq += v[i] * v[i];
+      }
+      const float rstd = rsqrtf(row_sum(qq, st1) * (1.f / 128.f) + p.eps);
+#pragma unroll
+      for (int i = 0; i < 32; i += 4) {
+        const float4 gg = __ldg(reinterpret_cast<const float4*>(gamma + c0 + i));
+        const float4 bb = __ldg(reinterpret_cast<const float4*>(beta + c0 + i));
+        v[i] = v[i] * rstd * gg.x + bb.x;
+        v[i + 1] = v[i + 1] * rstd * gg.y + bb.y;
+        v[i + 2] = v[i + 2] * rstd * gg.z + bb.z;
+        v[i + 3] = v[i + 3] * rstd * gg.w + bb.w;
+      }
+    };
+    // 32 fp16 values of this row at column c0 of a 128-wide SW128 K-major tile (2 atoms of 64)
+    auto store_sw128 = [&](uint8_t* base) {
+      uint8_t* atom = base + (c0 >> 6) * 16384;
+      const int ch0 = (c0 & 63) >> 3;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        *reinterpret_cast<uint4*>(atom + sw128_off(r, ch0 + j)) =
+            make_uint4(pack_half2(v[8 * j], v[8 * j + 1]), pack_half2(v[8 * j + 2], v[8 * j + 3]),
+                       pack_half2(v[8 * j + 4], v[8 * j + 5]), pack_half2(v[8 * j + 6], v[8 * j + 7]));
+    };
+    // 32 fp16 values of this row into a 128x32 SW64 tile (64-byte rows)
+    auto store_sw64 = [&](uint8_t* base) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        *reinterpret_cast<uint4*>(base + r * 64 + ((j ^ ((r >> 1) & 3)) << 4)) =
+            make_uint4(pack_half2(v[8 * j], v[8 * j + 1]), pack_half2(v[8 * j + 2], v[8 * j + 3]),
+                       pack_half2(v[8 * j + 4], v[8 * j + 5]), pack_half2(v[8 * j + 6], v[8 * j + 7]));
+    };
+    auto publish = [&](int slot) {
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bar[slot]);
+    };
+
+    for (int step = 0; step < nsteps; ++step) {
+      const int l = step % p.layers;
+      const int seq = static_cast<int>(blockIdx.x) + (step / p.layers) * static_cast<int>(gridDim.x);
+      const bool row_ok = r < p.seq_len;
+      const int64_t grow = static_cast<int64_t>(seq) * p.seq_len + r;
+      const float* xin = (l == 0 ? p.x : p.y) + grow * C::D + c0;
+      // ---- W1: LN1 -> XA
+#pragma unroll
+      for (int i = 0; i < 32; i += 4) {
+        float4 t = row_ok ? *reinterpret_cast<const float4*>(xin + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        v[i] = t.x; v[i + 1] = t.y; v[i + 2] = t.z; v[i + 3] = t.w;
+      }
+      layer_norm(p.ln1_w + l * 128, p.ln1_b + l * 128);
+      store_sw128(xa);
+      publish(SB_N1);
+      // ---- W2: QKV accumulator -> Q/K/V tiles (head g = column group g)
+      wait_w(SB_QKV_DONE, par(step, 1, 0));
+#pragma unroll 1
+      for (int nt = 0; nt < 3; ++nt) {
+        if (ok) tmem_ld32(trow + nt * 128 + c0, v);
+        const float* bq = p.b_qkv + l * 384 + nt * 128 + c0;
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          const float4 bb = __ldg(reinterpret_cast<const float4*>(bq + i));
+          v[i] += bb.x; v[i + 1] += bb.y; v[i + 2] += bb.z; v[i + 3] += bb.w;
+        }
+        store_sw64(smem + (nt == 0 ? C::OFF_Q : nt == 1 ? C::OFF_K : C::OFF_V) + g * 8192);
+      }
+      publish(SB_QKV_SMEM);
+      // ---- W3: causal softmax per head (this thread: row r, keys c0..c0+31)
+      float my_l = 1.f;  // softmax denominator of head g (this thread's head in the context step)
+#pragma unroll 1
+      for (int h = 0; h < 4; ++h) {
+        wait_w(SB_S_FULL + (h & 1), par(step, 2, h >> 1));
+        if (ok) tmem_ld32(trow + (h & 1) * 128 + c0, v);
+        float mx = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float t = (c0 + i <= r) ? v[i] * p.scale_log2 : -INFINITY;
+          v[i] = t;
+          mx = fmaxf(mx, t);
+        }
+        const float m = row_max(mx, st0);  // reductions alternate st0/st1 strictly
+        float sum = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float e = fast_exp2(v[i] - m);
+          v[i] = e;
+          sum += e;
+        }
+        // P of the previous head must have been consumed before P is overwritten
+        if (h > 0) wait_w(SB_PV_DONE, par(step, 4, h - 1));
+        store_sw128(smem + C::OFF_P);
+        publish(SB_P_FULL);
+        const float lh = row_sum(sum, st1);
+        if (h == g) my_l = lh;
+      }
+      // ---- W4: context = O_g / l_g -> XA (head g's 32 columns)
+      wait_w(SB_PV_DONE, par(step, 4, 3));
+      if (ok) tmem_ld32(trow + 256 + c0, v);
+      {
+        const float inv = 1.f / my_l;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] *= inv;
+      }
+      store_sw128(xa);
+      publish(SB_CTX);
+      // ---- W5: x1 = x + ctx.Wo^T + bo (kept in TMEM) ; LN2 -> XA
+      wait_w(SB_OP_DONE, par(step, 1, 0));
+      if (ok) tmem_ld32(trow + 384 + c0, v);
+      {
+        const float* bo = p.b_o + l * 128 + c0;
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          const float4 bb = __ldg(reinterpret_cast<const float4*>(bo + i));
+          const float4 xr = row_ok ? *reinterpret_cast<const float4*>(xin + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+          v[i] += bb.x + xr.x; v[i + 1] += bb.y + xr.y; v[i + 2] += bb.z + xr.z; v[i + 3] += bb.w + xr.w;
+        }
+      }
+      if (ok) tmem_st32(trow + 384 + c0, v);
+      layer_norm(p.ln2_w + l * 128, p.ln2_b + l * 128);
+      store_sw128(xa);
+      publish(SB_N2);
+      // ---- W6: GELU chunks -> H ping-pong
+#pragma unroll 1
+      for (int c = 0; c < nch; ++c) {
+        const int b = c & 1;
+        wait_w(SB_FIN + b, par(step, b ? per_b1 : per_b0, c >> 1));
+        if (ok) tmem_ld32(trow + b * 128 + c0, v);
+        const float* b1 = p.b_in + l * p.ffn + c * 128 + c0;
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          const float4 bb = __ldg(reinterpret_cast<const float4*>(b1 + i));
+          v[i] = gelu_erf(v[i] + bb.x);
+          v[i + 1] = gelu_erf(v[i + 1] + bb.y);
+          v[i + 2] = gelu_erf(v[i + 2] + bb.z);
+          v[i + 3] = gelu_erf(v[i + 3] + bb.w);
+        }
+        // the buffer's previous chunk (c-2) must have been consumed by ffn_out
+        if (c >= 2) wait_w(SB_HFREE + b, par(step, b ? per_b1 : per_b0, (c >> 1) - 1));
+        store_sw128(smem + (b ? C::OFF_K : C::OFF_Q));
+        publish(SB_H + b);
+      }
+      // ---- W7: x2 = x1 + h.W2^T + b2 ; final LayerNorm (last layer) -> y
+      wait_w(SB_FOUT, par(step, 1, 0));
+      if (ok) tmem_ld32(trow + 256 + c0, v);
+      {
+        float x1[32];
+        if (ok) tmem_ld32(trow + 384 + c0, x1);
+        const float* b2 = p.b_out + l * 128 + c0;
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          const float4 bb = __ldg(reinterpret_cast<const float4*>(b2 + i));
+          v[i] += bb.x + x1[i]; v[i + 1] += bb.y + x1[i + 1]; v[i + 2] += bb.z + x1[i + 2]; v[i + 3] += bb.w + x1[i + 3];
+        }
+      }
+      if (l == p.layers - 1) layer_norm(p.lnf_w, p.lnf_b);
+      if (row_ok && ok) {
+        float* yo = p.y + grow * C::D + c0;
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(yo + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+      }
+      // the next step's LN1 (which reuses the statistics buffers) must not race
+      // this step's final row reduction
+      named_bar(bar_id, 128);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace b200

@@ -42,10 +42,6 @@ struct GemmSmem {
   static constexpr int TOTAL = BAR_OFF + 256 + 1024;  // barriers + 1 KB alignment slack
 };
 
-__device__ __forceinline__ float gelu_erf(float v) {
-  return 0.5f * v * (1.0f + erff(v * 0.70710678118654752440f));
-}
-
 template <int BN, int STAGES, int EPI>
 __global__ void __launch_bounds__(192, 1)
     k_gemm_tn(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW, const GemmParams p) {

@@ -236,6 +236,11 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// Exact GELU, F.gelu(approximate="none"): v/2 * (1 + erf(v/sqrt(2))), with CUDA's erff.
+__device__ __forceinline__ float gelu_erf(float v) {
+  return 0.5f * v * (1.0f + erff(v * 0.70710678118654752440f));
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);

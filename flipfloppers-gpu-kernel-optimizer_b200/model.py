@@ -112,6 +112,7 @@ _CHUNK_FORCE_ROWS = int(os.environ.get("B200_CHUNK_ROWS", "0"))
 _GRAPH_MAX_ELEMS = int(os.environ.get("B200_GRAPH_MAX_ELEMS", str(1 << 26)))
 _GRAPHS_ON = os.environ.get("B200_CUDA_GRAPHS", "1") != "0"
 _GRAPH_CACHE = 8
+_FUSED_SMALL_ON = os.environ.get("B200_FUSED_SMALL", "1") != "0"
 
 
 @dataclass
@@ -144,7 +145,9 @@ class UserOptimizedTransformer(nn.Module):
         # plain-attribute caches, never Parameters / buffers (TTB:624-630)
         self._pack_key = None
         self._packs = None
+        self._stack = None
         self._lnf = None
+        self.force_strategy: Optional[str] = None  # tests / benchmarks: "chain" or "fused_small"
         self._ws: Dict[Tuple, torch.Tensor] = {}
         self._mask_cache: dict = {}
         self._plan: Dict[Tuple, str] = {}
@@ -177,6 +180,12 @@ class UserOptimizedTransformer(nn.Module):
                 ))
             self._lnf = (f32(self.final_norm.weight), f32(self.final_norm.bias))
         self._packs = packs
+        self._stack = None
+        if self._fused_small_eligible():
+            with torch.no_grad():
+                cat = lambda name: torch.cat([getattr(pk, name) for pk in packs], 0).contiguous()  # noqa: E731
+                self._stack = {n: cat(n) for n in ("ln1_w", "ln1_b", "w_qkv", "b_qkv", "w_o", "b_o", "ln2_w",
+                                                    "ln2_b", "w_in", "b_in", "w_out", "b_out")}
         self._pack_key = key
         self._graphs.clear()  # captured graphs point at the old weight copies
 
@@ -192,13 +201,29 @@ class UserOptimizedTransformer(nn.Module):
             self._mask_cache[key] = hit
         return hit
 
+    def _fused_small_eligible(self) -> bool:
+        c = self.config
+        return (c.d_model == 128 and c.num_heads == 4 and c.ffn_dim % 128 == 0 and c.ffn_dim <= 512
+                and _FUSED_SMALL_ON)
+
     def _strategy(self, B: int, S: int, device: torch.device) -> str:
-        """Pick the execution strategy for a shape, once (keyed by shape only)."""
+        """Pick the execution strategy for a shape, once (keyed by shape only).
+
+        * ``fused_small`` -- the whole model in one persistent kernel
+          (d_model=128, 4 heads, ffn<=512, seq_len<=128: every intermediate
+          fits on chip);
+        * ``chain`` -- per layer: LN, QKV GEMM, flash attention, out_proj GEMM
+          (+residual), LN, ffn_in GEMM (+GELU), ffn_out GEMM (+residual), final
+          LN, all tcgen05 kernels."""
+        if self.force_strategy is not None:
+            if self.force_strategy == "fused_small" and not (self._fused_small_eligible() and S <= 128):
+                raise ValueError("fused_small needs d_model=128, 4 heads, ffn_dim<=512 (multiple of 128), seq_len<=128")
+            return self.force_strategy
         key = (B, S, device.index)
         hit = self._plan.get(key)
         if hit is not None:
             return hit
-        strat = "chain"
+        strat = "fused_small" if (self._fused_small_eligible() and S <= 128) else "chain"
         self._plan[key] = strat
         return strat
 
@@ -232,11 +257,14 @@ class UserOptimizedTransformer(nn.Module):
             strat = self._strategy(B, S, dev)
             self.last_strategy = strat
             y = torch.empty_like(xin)
-            ws = self._workspace(rt.block_workspace_bytes(B * S, d, self.config.ffn_dim), dev)
+            if strat == "chain":
+                ws = self._workspace(rt.block_workspace_bytes(B * S, d, self.config.ffn_dim), dev)
+            else:
+                ws = self._workspace(256, dev)
             if _GRAPHS_ON and xin.numel() <= _GRAPH_MAX_ELEMS:
                 self._run_graphed(xin, y, ws, strat)
             else:
-                self._forward_chain(xin, y, ws)
+                self._launch(xin, y, ws, strat)
         return y if out_dtype == torch.float32 else y.to(out_dtype)
 
     def _run_graphed(self, x: torch.Tensor, y: torch.Tensor, ws: torch.Tensor, strat: str) -> None:
@@ -252,19 +280,40 @@ class UserOptimizedTransformer(nn.Module):
             shape_key = (tuple(x.shape), strat)
             if shape_key not in self._warm:
                 # first call at this shape: launch eagerly (sets kernel attributes, validates arguments)
-                self._forward_chain(x, y, ws)
+                self._launch(x, y, ws, strat)
                 torch.cuda.current_stream().synchronize()
                 self._warm.add(shape_key)
                 return
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
-                self._forward_chain(x, y, ws)
+                self._launch(x, y, ws, strat)
             self._graphs[key] = g
             while len(self._graphs) > _GRAPH_CACHE:
                 self._graphs.popitem(last=False)
         else:
             self._graphs.move_to_end(key)
         g.replay()
+
+    def _launch(self, x: torch.Tensor, y: torch.Tensor, ws: torch.Tensor, strat: str) -> None:
+        if strat == "fused_small":
+            self._forward_fused_small(x, y)
+        else:
+            self._forward_chain(x, y, ws)
+
+    def _forward_fused_small(self, x: torch.Tensor, y: torch.Tensor) -> None:
+        cfg = self.config
+        B, S, d = x.shape
+        st = self._stack
+        a = rt.FusedSmallArgs()
+        a.batch, a.seq_len, a.d_model, a.num_heads = B, S, d, cfg.num_heads
+        a.ffn_dim, a.num_layers = cfg.ffn_dim, len(self._packs)
+        a.x, a.y = x.data_ptr(), y.data_ptr()
+        for name in ("ln1_w", "ln1_b", "w_qkv", "b_qkv", "w_o", "b_o", "ln2_w", "ln2_b", "w_in", "b_in",
+                     "w_out", "b_out"):
+            setattr(a, name, st[name].data_ptr())
+        a.lnf_w, a.lnf_b = self._lnf[0].data_ptr(), self._lnf[1].data_ptr()
+        a.eps = float(self.layers[0].norm1.eps)
+        rt.fused_small(a)
 
     def _forward_chain(self, x: torch.Tensor, y: torch.Tensor, ws: torch.Tensor) -> None:
         cfg = self.config

@@ -72,6 +72,22 @@ class BlockArgs(ctypes.Structure):
     ]
 
 
+class FusedSmallArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", ctypes.c_int), ("seq_len", ctypes.c_int), ("d_model", ctypes.c_int),
+        ("num_heads", ctypes.c_int), ("ffn_dim", ctypes.c_int), ("num_layers", ctypes.c_int),
+        ("x", _vp), ("y", _vp),
+        ("ln1_w", _vp), ("ln1_b", _vp),
+        ("w_qkv", _vp), ("b_qkv", _vp),
+        ("w_o", _vp), ("b_o", _vp),
+        ("ln2_w", _vp), ("ln2_b", _vp),
+        ("w_in", _vp), ("b_in", _vp),
+        ("w_out", _vp), ("b_out", _vp),
+        ("lnf_w", _vp), ("lnf_b", _vp),
+        ("eps", ctypes.c_float),
+    ]
+
+
 # (name, restype, argtypes) of every exported symbol; include/b200_block.h is the source of truth.
 EXPORTS = [
     ("b200_abi_version", ctypes.c_int, []),
@@ -85,6 +101,7 @@ EXPORTS = [
     ("b200_block_workspace_bytes", ctypes.c_size_t, [_c_ll, ctypes.c_int, ctypes.c_int]),
     ("b200_block_forward", ctypes.c_int, [ctypes.POINTER(BlockArgs), _vp]),
     ("b200_block_forward_noalloc", ctypes.c_int, [ctypes.POINTER(BlockArgs), _vp]),
+    ("b200_block_fused_small_launch", ctypes.c_int, [ctypes.POINTER(FusedSmallArgs), _vp]),
 ]
 
 
@@ -199,6 +216,10 @@ def block_workspace_bytes(tokens: int, d_model: int, ffn_dim: int) -> int:
 
 def block_forward(args: BlockArgs, stream=None) -> None:
     check(lib().b200_block_forward(ctypes.byref(args), _stream(stream)), "b200_block_forward")
+
+
+def fused_small(args: FusedSmallArgs, stream=None) -> None:
+    check(lib().b200_block_fused_small_launch(ctypes.byref(args), _stream(stream)), "b200_block_fused_small_launch")
 
 
 # Size of the static scratch buffer behind b200_block_forward_noalloc (B200_NOALLOC_SCRATCH_BYTES).

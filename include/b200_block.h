@@ -20,6 +20,8 @@
  *       (torch_transformer_benchmark.py:1293, 1348, 1373) -> b200_layernorm_launch
  *   - the per-layer body of _optimized_forward_causal
  *       (torch_transformer_benchmark.py:1282-1373)  -> b200_block_forward
+ *   - the unwired causal megakernel mega_causal_forward
+ *       (csrc/g5_mega_causal.cpp:7-18)              -> b200_block_fused_small_launch
  *   - ws_gemm_num_cfg / ws_gemm_cfg_desc (csrc/g4_4_warpspec_gemm.cu:1022-1069)
  *       -> b200_abi_version / b200_status_str (no config table: tiles are
  *          chosen inside the library from the shape)
@@ -143,6 +145,36 @@ typedef struct {
 
 size_t b200_block_workspace_bytes(long long tokens, int d_model, int ffn_dim);
 int b200_block_forward(const B200BlockArgs* args, b200_stream_t stream);
+
+/* Whole causal model (num_layers pre-LN blocks + final LayerNorm) in ONE
+ * persistent kernel, for small models: d_model == 128, num_heads == 4,
+ * ffn_dim a multiple of 128 up to 512, seq_len <= 128.  Every intermediate
+ * stays on chip (TMEM / shared memory); per layer the weights are stacked
+ * along rows: w_qkv [L*3d, d], w_o [L*d, d], w_in [L*ffn, d], w_out [L*d, ffn]
+ * (fp16), biases / LayerNorm parameters [L, n] (fp32).  y must not alias x (y
+ * carries the residual between layers).  Other shapes return B200_ERR_CONFIG. */
+typedef struct {
+  int batch, seq_len, d_model, num_heads, ffn_dim, num_layers;
+  const float* x;
+  float* y;
+  const float* ln1_w;
+  const float* ln1_b;
+  const void* w_qkv;
+  const float* b_qkv;
+  const void* w_o;
+  const float* b_o;
+  const float* ln2_w;
+  const float* ln2_b;
+  const void* w_in;
+  const float* b_in;
+  const void* w_out;
+  const float* b_out;
+  const float* lnf_w;
+  const float* lnf_b;
+  float eps;
+} B200FusedSmallArgs;
+
+int b200_block_fused_small_launch(const B200FusedSmallArgs* args, b200_stream_t stream);
 
 /* Same computation as b200_block_forward, for callers that cannot allocate
  * device memory: a plugin host whose memory belongs to someone else's pool
