@@ -6,6 +6,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstdint>
+#include <cstdio>
 #include <cstring>
 #include <mutex>
 #include <set>
@@ -28,6 +29,12 @@ std::once_flag g_encode_once;
 std::mutex g_mu;
 std::set<std::pair<const void*, int>> g_attr_done;  // (kernel, device) with smem opt-in set
 int g_arch_state[128] = {0};                          // per device: 0 unknown, 1 ok, -1 not sm_100
+
+thread_local char g_detail[256] = "";
+
+void set_detail(const char* what, cudaError_t e) {
+  snprintf(g_detail, sizeof(g_detail), "%s: %s (%d)", what, cudaGetErrorString(e), static_cast<int>(e));
+}
 
 int ensure_encode() {
   std::call_once(g_encode_once, [] {
@@ -71,15 +78,38 @@ int set_smem(const void* fn, int bytes) {
   const int dev = current_device();
   std::lock_guard<std::mutex> lk(g_mu);
   if (g_attr_done.count({fn, dev})) return B200_OK;
-  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) {
+  const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) {
     cudaGetLastError();
+    set_detail("cudaFuncSetAttribute(MaxDynamicSharedMemorySize)", e);
     return B200_ERR_SMEM;
   }
   g_attr_done.insert({fn, dev});
   return B200_OK;
 }
 
-int launch_status() { return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_LAUNCH; }
+int launch_status() {
+  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) return B200_OK;
+  set_detail("kernel launch", e);
+  return B200_ERR_LAUNCH;
+}
+
+// Refuse a launch the kernel's compiled resources cannot satisfy, with the reason recorded.
+int check_block_fits(const void* fn, int threads) {
+  cudaFuncAttributes fa{};
+  const cudaError_t e = cudaFuncGetAttributes(&fa, fn);
+  if (e != cudaSuccess) {
+    set_detail("cudaFuncGetAttributes", e);
+    return B200_ERR_LAUNCH;
+  }
+  if (fa.maxThreadsPerBlock < threads) {
+    snprintf(g_detail, sizeof(g_detail), "kernel allows %d threads per block (%d registers/thread), %d requested",
+             fa.maxThreadsPerBlock, fa.numRegs, threads);
+    return B200_ERR_CONFIG;
+  }
+  return B200_OK;
+}
 
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
@@ -317,6 +347,7 @@ int fused_small_impl(const B200FusedSmallArgs* a, cudaStream_t st) {
   p.scale_log2 = static_cast<float>(1.4426950408889634 / __builtin_sqrt(32.0));
   const int smem = SmallCfg::TOTAL;
   if (int rc = set_smem(reinterpret_cast<const void*>(k_block_small), smem)) return rc;
+  if (int rc = check_block_fits(reinterpret_cast<const void*>(k_block_small), SmallCfg::THREADS)) return rc;
   const int grid = a->batch < num_sms() ? a->batch : num_sms();
   k_block_small<<<grid, SmallCfg::THREADS, smem, st>>>(tq, to, ti, tout, p);
   return launch_status();
@@ -421,6 +452,8 @@ int block_impl(const B200BlockArgs* a, cudaStream_t st) {
 extern "C" {
 
 int b200_abi_version(void) { return B200_ABI_VERSION; }
+
+const char* b200_last_error_detail(void) { return g_detail; }
 
 const char* b200_status_str(int s) {
   switch (s) {

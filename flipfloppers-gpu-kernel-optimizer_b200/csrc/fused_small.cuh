@@ -105,7 +105,7 @@ __device__ __forceinline__ uint32_t par(int step, int per, int idx) {
   return static_cast<uint32_t>((step * per + idx) & 1);
 }
 
-__global__ void __maxnreg__(112)
+__global__ void __maxnreg__(104)
     k_block_small(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_o,
                   const __grid_constant__ CUtensorMap tm_in, const __grid_constant__ CUtensorMap tm_out,
                   const SmallParams p) {

@@ -38,7 +38,11 @@ class B200Error(RuntimeError):
 
     def __init__(self, what: str, status: int):
         self.status = status
-        super().__init__(f"{what}: {status_str(status)} (status {status})")
+        try:
+            detail = lib().b200_last_error_detail().decode()
+        except Exception:  # noqa: BLE001
+            detail = ""
+        super().__init__(f"{what}: {status_str(status)} (status {status})" + (f" [{detail}]" if detail else ""))
 
 
 class AttnArgs(ctypes.Structure):
@@ -92,6 +96,7 @@ class FusedSmallArgs(ctypes.Structure):
 EXPORTS = [
     ("b200_abi_version", ctypes.c_int, []),
     ("b200_status_str", ctypes.c_char_p, [ctypes.c_int]),
+    ("b200_last_error_detail", ctypes.c_char_p, []),
     ("b200_device_error", ctypes.c_int, [ctypes.c_int]),
     ("b200_layernorm_launch", ctypes.c_int,
      [_vp, _c_ll, _vp, _vp, _vp, _c_ll, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, _vp]),

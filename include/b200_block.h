@@ -70,6 +70,10 @@ enum {
 int b200_abi_version(void);
 const char* b200_status_str(int status);
 
+/* Human-readable detail of the calling thread's last failed CUDA call inside
+ * the library (e.g. the CUDA error string of a failed launch); "" if none. */
+const char* b200_last_error_detail(void);
+
 /* Device error word of the current device: first device-side failure code
  * since the last clear (0 = none).  Synchronises the device.  clear != 0
  * resets it to 0. */
