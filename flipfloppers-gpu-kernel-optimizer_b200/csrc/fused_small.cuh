@@ -105,7 +105,7 @@ __device__ __forceinline__ uint32_t par(int step, int per, int idx) {
   return static_cast<uint32_t>((step * per + idx) & 1);
 }
 
-__global__ void __maxnreg__(104)
+__global__ void __launch_bounds__(SmallCfg::THREADS, 1)
     k_block_small(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_o,
                   const __grid_constant__ CUtensorMap tm_in, const __grid_constant__ CUtensorMap tm_out,
                   const SmallParams p) {
@@ -476,14 +476,16 @@ __global__ void __maxnreg__(104)
       // ---- W7: x2 = x1 + h.W2^T + b2 ; final LayerNorm (last layer) -> y
       wait_w(SB_FOUT, par(step, 1, 0));
       if (ok) tmem_ld32(trow + 256 + c0, v);
-      {
-        float x1[32];
-        if (ok) tmem_ld32(trow + 384 + c0, x1);
-        const float* b2 = p.b_out + l * 128 + c0;
 #pragma unroll
-        for (int i = 0; i < 32; i += 4) {
+      for (int half = 0; half < 2; ++half) {
+        float x1[16];
+        if (ok) tmem_ld16(trow + 384 + c0 + 16 * half, x1);
+        const float* b2 = p.b_out + l * 128 + c0 + 16 * half;
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) {
           const float4 bb = __ldg(reinterpret_cast<const float4*>(b2 + i));
-          v[i] += bb.x + x1[i]; v[i + 1] += bb.y + x1[i + 1]; v[i + 2] += bb.z + x1[i + 2]; v[i + 3] += bb.w + x1[i + 3];
+          float* w = v + 16 * half + i;
+          w[0] += bb.x + x1[i]; w[1] += bb.y + x1[i + 1]; w[2] += bb.z + x1[i + 2]; w[3] += bb.w + x1[i + 3];
         }
       }
       if (l == p.layers - 1) layer_norm(p.lnf_w, p.lnf_b);
