@@ -349,6 +349,7 @@ def roofline_pass(model, x, mask, flush, cfg, steps):
     name = max(timing, key=timing.get)
     if name == "fused_small":
         fl, by = block_work(B, S, d, H, F)
+        fl *= cfg.num_layers
     else:
         fl, by = work[name]
     ms = timing[name]
