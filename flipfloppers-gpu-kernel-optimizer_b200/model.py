@@ -253,18 +253,8 @@ class UserOptimizedTransformer(nn.Module):
         xin = x if (x.dtype == torch.float32 and x.is_contiguous()) else x.to(torch.float32).contiguous()
         dev = xin.device
         with torch.cuda.device(dev):
-            self._ensure_packs(dev)
-            strat = self._strategy(B, S, dev)
-            self.last_strategy = strat
             y = torch.empty_like(xin)
-            if strat == "chain":
-                ws = self._workspace(rt.block_workspace_bytes(B * S, d, self.config.ffn_dim), dev)
-            else:
-                ws = self._workspace(256, dev)
-            if _GRAPHS_ON and xin.numel() <= _GRAPH_MAX_ELEMS:
-                self._run_graphed(xin, y, ws, strat)
-            else:
-                self._launch(xin, y, ws, strat)
+            self._forward_into(xin, y)
         return y if out_dtype == torch.float32 else y.to(out_dtype)
 
     def _run_graphed(self, x: torch.Tensor, y: torch.Tensor, ws: torch.Tensor, strat: str) -> None:
@@ -341,6 +331,98 @@ class UserOptimizedTransformer(nn.Module):
             a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
             rt.block_forward(a)
             cur = out
+
+    # ------------------------------------------------------------------ host-buffer pipeline
+    def forward_host(self, x_host: torch.Tensor, out: Optional[torch.Tensor] = None, *, device=None,
+                     wait: bool = True, flush: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Forward of a HOST tensor into a host tensor, pipelined across calls.
+
+        Three CUDA streams carry call i's upload (pinned H2D of x into device
+        slot i % 2), its forward (graph replay on that slot) and its download
+        (D2H of y into ``out``), ordered by events, so that consecutive calls
+        overlap one call's download, the next call's forward and the one
+        after's upload -- the way a serving loop keeps PCIe busy in both
+        directions.  ``wait=False`` returns as soon as the work is queued;
+        ``out`` is valid after ``synchronize_host()``.  Pass pinned tensors for
+        the copies to be asynchronous.  ``flush`` (a device buffer) is zeroed on
+        the forward stream before the forward, for benchmarks that flush L2.
+        """
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        if x_host.dtype != torch.float32 or x_host.dim() != 3:
+            raise ValueError("forward_host expects a float32 [B, S, d] host tensor")
+        pipe = self._pipe_state(tuple(x_host.shape), dev)
+        if out is None:
+            out = torch.empty(x_host.shape, dtype=torch.float32, pin_memory=True)
+        i = pipe["calls"]
+        pipe["calls"] += 1
+        slot = i % 2
+        xd, yd = pipe["x"][slot], pipe["y"][slot]
+        ev = pipe["ev"][slot]
+        with torch.cuda.device(dev):
+            up, comp, down = pipe["streams"]
+            with torch.cuda.stream(up):
+                if i >= 2:
+                    up.wait_event(ev["comp"])      # slot's previous forward has read x
+                xd.copy_(x_host, non_blocking=True)
+                ev["up"].record(up)
+            with torch.cuda.stream(comp):
+                comp.wait_event(ev["up"])
+                if i >= 2:
+                    comp.wait_event(ev["down"])    # slot's previous y has been downloaded
+                if flush is not None:
+                    flush.zero_()
+                self._forward_into(xd, yd)
+                ev["comp"].record(comp)
+            with torch.cuda.stream(down):
+                down.wait_event(ev["comp"])
+                out.copy_(yd, non_blocking=True)
+                ev["down"].record(down)
+        if wait:
+            pipe["streams"][2].synchronize()
+        return out
+
+    def host_done_event(self, shape, device=None) -> "torch.cuda.Event":
+        """Event recorded after the last queued ``forward_host`` download of ``shape``."""
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        pipe = self._pipe_state(tuple(shape), dev)
+        return pipe["ev"][(pipe["calls"] - 1) % 2]["down"]
+
+    def synchronize_host(self) -> None:
+        """Wait until every queued ``forward_host`` download has landed."""
+        for pipe in getattr(self, "_pipes", {}).values():
+            pipe["streams"][2].synchronize()
+
+    def _pipe_state(self, shape, dev):
+        pipes = self.__dict__.setdefault("_pipes", {})
+        key = (shape, dev.index)
+        pipe = pipes.get(key)
+        if pipe is None:
+            with torch.cuda.device(dev):
+                pipe = {
+                    "calls": 0,
+                    "x": [torch.empty(shape, dtype=torch.float32, device=dev) for _ in range(2)],
+                    "y": [torch.empty(shape, dtype=torch.float32, device=dev) for _ in range(2)],
+                    "streams": [torch.cuda.Stream(device=dev) for _ in range(3)],
+                    "ev": [{k: torch.cuda.Event() for k in ("up", "comp", "down")} for _ in range(2)],
+                }
+            pipes[key] = pipe
+        return pipe
+
+    def _forward_into(self, xin: torch.Tensor, y: torch.Tensor) -> None:
+        """Forward of a contiguous fp32 CUDA tensor into a preallocated ``y`` (current stream)."""
+        B, S, d = xin.shape
+        dev = xin.device
+        self._ensure_packs(dev)
+        strat = self._strategy(B, S, dev)
+        self.last_strategy = strat
+        if strat == "chain":
+            ws = self._workspace(rt.block_workspace_bytes(B * S, d, self.config.ffn_dim), dev)
+        else:
+            ws = self._workspace(256, dev)
+        if _GRAPHS_ON and xin.numel() <= _GRAPH_MAX_ELEMS:
+            self._run_graphed(xin, y, ws, strat)
+        else:
+            self._launch(xin, y, ws, strat)
 
     # ------------------------------------------------------------------ profiling helper
     @torch.no_grad()

@@ -158,3 +158,20 @@ def test_c5_shape_sampled_rows(tt):
     res = oracle.compare_outputs(ref, y[1, rows], rtol=RTOL, atol=ATOL)
     print(f"C5 rows: max_abs={res.max_abs_error:.4g}")
     assert res.passed, res
+
+
+@pytest.mark.parametrize("d,H,F", [(128, 4, 512), (256, 4, 1024)])
+def test_forward_host_pipeline_matches_device_path(tt, d, H, F):
+    """Pipelined host-buffer calls (uploads, forwards and downloads of consecutive
+    calls overlapping on three streams, device slots reused) give exactly the
+    device path's outputs, each call its own."""
+    model, _ = _model(tt, 16, 128, d, H, F, 1)
+    xs = [oracle.generate_random_case(16, 128, d, 300 + i)[0].pin_memory() for i in range(5)]
+    outs = [torch.empty_like(x).pin_memory() for x in xs]
+    with torch.inference_mode():
+        for x, o in zip(xs, outs):
+            model.forward_host(x, out=o, wait=False)
+        model.synchronize_host()
+        for x, o in zip(xs, outs):
+            ref = model(x.to(DEV)).cpu()
+            assert torch.equal(o, ref)
