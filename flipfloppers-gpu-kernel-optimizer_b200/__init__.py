@@ -12,5 +12,5 @@ name is not a Python identifier):
 * ``parallel.py`` -- one-process-per-GPU batch sharding and tensor parallelism.
 """
 
-from . import build, runtime  # noqa: F401
+from . import build, parallel, runtime  # noqa: F401
 from .model import TransformerConfig, UserOptimizedTransformer  # noqa: F401

@@ -144,6 +144,7 @@ int launch_gemm_bn(int epi, const CUtensorMap& ta, const CUtensorMap& tw, const 
     case EPI_BIAS_F16: return launch_gemm_t<BN, STAGES, EPI_BIAS_F16>(ta, tw, p, st);
     case EPI_BIAS_GELU_F16: return launch_gemm_t<BN, STAGES, EPI_BIAS_GELU_F16>(ta, tw, p, st);
     case EPI_BIAS_RESID_F32: return launch_gemm_t<BN, STAGES, EPI_BIAS_RESID_F32>(ta, tw, p, st);
+    case EPI_BIAS_F32: return launch_gemm_t<BN, STAGES, EPI_BIAS_F32>(ta, tw, p, st);
     default: return B200_ERR_CONFIG;
   }
 }
@@ -158,14 +159,14 @@ int gemm_impl(int epi, const void* A, long long lda, const void* W, long long ld
               const float* resid, long long ld_resid, void* out, long long ld_out, int M, int N, int K,
               cudaStream_t st) {
   if (!A || !W || !out || M < 0 || N <= 0 || K <= 0) return B200_ERR_ARG;
-  if (epi < 0 || epi > 2) return B200_ERR_CONFIG;
+  if (epi < 0 || epi > 3) return B200_ERR_CONFIG;
   if (epi == EPI_BIAS_RESID_F32 && !resid) return B200_ERR_ARG;
   if (M == 0) return B200_OK;
   if (N % 32 || K % 8 || lda % 8 || ldw % 8 || lda < K || ldw < K) return B200_ERR_TILE;
-  const bool f32_out = epi == EPI_BIAS_RESID_F32;
+  const bool f32_out = epi == EPI_BIAS_RESID_F32 || epi == EPI_BIAS_F32;
   if (ld_out < N || ld_out % (f32_out ? 4 : 8)) return B200_ERR_ALIGN;
   if (!al16(A) || !al16(W) || !al16(out) || (bias && !al16(bias))) return B200_ERR_ALIGN;
-  if (f32_out && (!al16(resid) || ld_resid % 4 || ld_resid < N)) return B200_ERR_ALIGN;
+  if (epi == EPI_BIAS_RESID_F32 && (!al16(resid) || ld_resid % 4 || ld_resid < N)) return B200_ERR_ALIGN;
   if ((M + 127) / 128 > 65535) return B200_ERR_TILE;
   if (int rc = check_arch()) return rc;
   const int BN = pick_bn(M, N);
@@ -227,6 +228,36 @@ int ln_impl(const float* x, long long ldx, const float* g, const float* b, void*
     case 16: return launch_ln_t<16, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
     case 24: return launch_ln_t<24, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
     case 32: return launch_ln_t<32, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
+    default: return B200_ERR_TILE;
+  }
+}
+
+template <int VPL>
+int launch_add_ln_t(const float* a, const float* b, const float* bias, float* sum_out, const float* g,
+                    const float* be, void* out, bool f16, int rows, int d, float eps, cudaStream_t st) {
+  dim3 grid((rows + 7) / 8);
+  if (f16)
+    k_add_layernorm<VPL, true><<<grid, 256, 0, st>>>(a, b, bias, sum_out, g, be, out, rows, d, eps);
+  else
+    k_add_layernorm<VPL, false><<<grid, 256, 0, st>>>(a, b, bias, sum_out, g, be, out, rows, d, eps);
+  return launch_status();
+}
+
+int add_ln_impl(const float* a, const float* b, const float* bias, float* sum_out, const float* g, const float* be,
+                void* out, int f16, int rows, int d, float eps, cudaStream_t st) {
+  if (!a || !b || !sum_out || !g || !be || !out || rows < 0 || d <= 0) return B200_ERR_ARG;
+  if (rows == 0) return B200_OK;
+  if (d % 128 || d > 4096) return B200_ERR_TILE;
+  if (!al16(a) || !al16(b) || !al16(sum_out) || !al16(g) || !al16(be) || !al16(out) || (bias && !al16(bias)))
+    return B200_ERR_ALIGN;
+  if (int rc = check_arch()) return rc;
+  switch (d / 128) {
+    case 1: return launch_add_ln_t<1>(a, b, bias, sum_out, g, be, out, f16, rows, d, eps, st);
+    case 2: return launch_add_ln_t<2>(a, b, bias, sum_out, g, be, out, f16, rows, d, eps, st);
+    case 4: return launch_add_ln_t<4>(a, b, bias, sum_out, g, be, out, f16, rows, d, eps, st);
+    case 8: return launch_add_ln_t<8>(a, b, bias, sum_out, g, be, out, f16, rows, d, eps, st);
+    case 16: return launch_add_ln_t<16>(a, b, bias, sum_out, g, be, out, f16, rows, d, eps, st);
+    case 32: return launch_add_ln_t<32>(a, b, bias, sum_out, g, be, out, f16, rows, d, eps, st);
     default: return B200_ERR_TILE;
   }
 }
@@ -446,6 +477,108 @@ int block_impl(const B200BlockArgs* a, cudaStream_t st) {
   return B200_OK;
 }
 
+// ------------------------------------------------------------------ sequence-chunked forward
+// The reference's _chunked_forward_causal (TTB:1378-1609): for each sequence,
+// query chunks [c0, c1) in order; the chunk's K/V rows are appended to an fp16
+// cache [tokens, 2d] and its queries attend keys [0, c1) through the
+// prefix-causal attention (q_offset = c0, TTB:1491-1500); the position-wise
+// rest of the block runs on the chunk only.  Peak memory: the K/V cache plus
+// one chunk's activations.
+struct ChunkWs {
+  __half* kv;    // [M, 2d]
+  __half* q;     // [R, d]
+  __half* n;     // [R, d]
+  __half* ctx;   // [R, d]
+  float* x1;     // [R, d]
+  __half* h;     // [R, F]
+  size_t bytes;
+};
+
+ChunkWs carve_chunked(void* base, long long M, long long R, int d, int F) {
+  ChunkWs w{};
+  uint8_t* p = static_cast<uint8_t*>(base);
+  size_t off = 0;
+  auto take = [&](size_t n) {
+    uint8_t* r = p ? p + off : nullptr;
+    off += align256(n);
+    return r;
+  };
+  w.kv = reinterpret_cast<__half*>(take(static_cast<size_t>(M) * 2 * d * 2));
+  w.q = reinterpret_cast<__half*>(take(static_cast<size_t>(R) * d * 2));
+  w.n = reinterpret_cast<__half*>(take(static_cast<size_t>(R) * d * 2));
+  w.ctx = reinterpret_cast<__half*>(take(static_cast<size_t>(R) * d * 2));
+  w.x1 = reinterpret_cast<float*>(take(static_cast<size_t>(R) * d * 4));
+  w.h = reinterpret_cast<__half*>(take(static_cast<size_t>(R) * F * 2));
+  w.bytes = off;
+  return w;
+}
+
+int block_chunked_impl(const B200BlockArgs* a, int chunk_rows, cudaStream_t st) {
+  if (!a || !a->x || !a->y || !a->w_qkv || !a->w_o || !a->w_in || !a->w_out) return B200_ERR_ARG;
+  if (!a->ln1_w || !a->ln1_b || !a->ln2_w || !a->ln2_b || !a->b_qkv || !a->b_o || !a->b_in || !a->b_out)
+    return B200_ERR_ARG;
+  if ((a->lnf_w == nullptr) != (a->lnf_b == nullptr)) return B200_ERR_ARG;
+  if (a->batch <= 0 || a->seq_len <= 0 || a->d_model <= 0 || a->num_heads <= 0 || a->ffn_dim <= 0 || chunk_rows <= 0)
+    return B200_ERR_ARG;
+  if (a->d_model % a->num_heads || a->x == a->y) return B200_ERR_ARG;
+  const long long M = static_cast<long long>(a->batch) * a->seq_len;
+  const int d = a->d_model, F = a->ffn_dim, H = a->num_heads, hd = d / H, S = a->seq_len;
+  if (hd != 32 && hd != 64 && hd != 128 && hd != 256) return B200_ERR_HEAD_DIM;
+  if (M > 0x7fffffffLL) return B200_ERR_TILE;
+  const int R = chunk_rows < S ? chunk_rows : S;
+  ChunkWs w = carve_chunked(a->workspace, M, R, d, F);
+  if (!a->workspace || a->workspace_bytes < w.bytes) return B200_ERR_WORKSPACE;
+  if (!al16(a->workspace)) return B200_ERR_ALIGN;
+  const __half* wq = static_cast<const __half*>(a->w_qkv);
+  int rc;
+  for (int b = 0; b < a->batch; ++b) {
+    for (int c0 = 0; c0 < S; c0 += R) {
+      const int Rc = (S - c0) < R ? (S - c0) : R;
+      const long long row0 = static_cast<long long>(b) * S + c0;
+      const float* xr = a->x + row0 * d;
+      float* yr = a->y + row0 * d;
+      if ((rc = ln_impl(xr, d, a->ln1_w, a->ln1_b, w.n, d, 1, Rc, d, a->eps, st))) return rc;
+      // q rows of the fused QKV weight -> chunk buffer; k|v rows -> the cache at this chunk's rows
+      if ((rc = gemm_impl(EPI_BIAS_F16, w.n, d, wq, d, a->b_qkv, nullptr, 0, w.q, d, Rc, d, d, st))) return rc;
+      if ((rc = gemm_impl(EPI_BIAS_F16, w.n, d, wq + static_cast<size_t>(d) * d, d, a->b_qkv + d, nullptr, 0,
+                          w.kv + row0 * 2 * d, 2 * d, Rc, 2 * d, d, st)))
+        return rc;
+      B200AttnArgs at{};
+      at.q = w.q;
+      at.k = at.v = w.kv;
+      at.ld_q = d;
+      at.ld_k = at.ld_v = 2 * d;
+      at.q_rows = Rc;
+      at.kv_rows = M;
+      at.batch = 1;
+      at.heads = H;
+      at.head_dim = hd;
+      at.q_len = Rc;
+      at.q_offset = c0;
+      at.kv_len = c0 + Rc;
+      at.q_seq_rows = Rc;
+      at.kv_seq_rows = S;
+      at.q_row0 = 0;
+      at.kv_row0 = static_cast<int>(static_cast<long long>(b) * S);
+      at.q_col0 = 0;
+      at.k_col0 = 0;
+      at.v_col0 = d;
+      at.out = w.ctx;
+      at.ld_out = d;
+      at.out_seq_rows = Rc;
+      at.out_row0 = 0;
+      if ((rc = attn_impl(&at, st))) return rc;
+      if ((rc = gemm_impl(EPI_BIAS_RESID_F32, w.ctx, d, a->w_o, d, a->b_o, xr, d, w.x1, d, Rc, d, d, st))) return rc;
+      if ((rc = ln_impl(w.x1, d, a->ln2_w, a->ln2_b, w.n, d, 1, Rc, d, a->eps, st))) return rc;
+      if ((rc = gemm_impl(EPI_BIAS_GELU_F16, w.n, d, a->w_in, d, a->b_in, nullptr, 0, w.h, F, Rc, F, d, st))) return rc;
+      float* x2 = a->lnf_w ? w.x1 : yr;
+      if ((rc = gemm_impl(EPI_BIAS_RESID_F32, w.h, F, a->w_out, F, a->b_out, w.x1, d, x2, d, Rc, d, F, st))) return rc;
+      if (a->lnf_w && (rc = ln_impl(w.x1, d, a->lnf_w, a->lnf_b, yr, d, 0, Rc, d, a->eps, st))) return rc;
+    }
+  }
+  return B200_OK;
+}
+
 }  // namespace
 
 // ====================================================================== C ABI
@@ -496,6 +629,12 @@ int b200_layernorm_launch(const float* x, long long ld_x, const float* gamma, co
   return ln_impl(x, ld_x, gamma, beta, out, ld_out, out_f16, rows, d, eps, static_cast<cudaStream_t>(stream));
 }
 
+int b200_add_layernorm_launch(const float* a, const float* b, const float* bias, float* sum_out, const float* gamma,
+                              const float* beta, void* out, int out_f16, int rows, int d, float eps,
+                              b200_stream_t stream) {
+  return add_ln_impl(a, b, bias, sum_out, gamma, beta, out, out_f16, rows, d, eps, static_cast<cudaStream_t>(stream));
+}
+
 int b200_gemm_launch(int epilogue, const void* A, long long lda, const void* W, long long ldw, const float* bias,
                      const float* resid, long long ld_resid, void* out, long long ld_out, int M, int N, int K,
                      b200_stream_t stream) {
@@ -514,6 +653,15 @@ size_t b200_block_workspace_bytes(long long tokens, int d_model, int ffn_dim) {
 
 int b200_block_forward(const B200BlockArgs* args, b200_stream_t stream) {
   return block_impl(args, static_cast<cudaStream_t>(stream));
+}
+
+size_t b200_block_chunked_workspace_bytes(long long tokens, int chunk_rows, int d_model, int ffn_dim) {
+  if (tokens <= 0 || chunk_rows <= 0 || d_model <= 0 || ffn_dim <= 0) return 0;
+  return carve_chunked(nullptr, tokens, chunk_rows, d_model, ffn_dim).bytes;
+}
+
+int b200_block_forward_chunked(const B200BlockArgs* args, int chunk_rows, b200_stream_t stream) {
+  return block_chunked_impl(args, chunk_rows, static_cast<cudaStream_t>(stream));
 }
 
 int b200_block_fused_small_launch(const B200FusedSmallArgs* args, b200_stream_t stream) {

@@ -6,6 +6,8 @@
 //   EPI_BIAS_GELU_F16  fp16 gelu_erf(.)    (ffn_in + exact GELU, TTB:1350-1354)
 //   EPI_BIAS_RESID_F32 fp32 out = resid+.  (out_proj / ffn_out + residual,
 //                                           TTB:1333-1339, 1368-1369)
+//   EPI_BIAS_F32       fp32 out            (row-parallel partial sums before
+//                                           the tensor-parallel all-reduce)
 // It replaces the reference's mma.sync GEMM `ws_gemm_kernel`
 // (csrc/g4_4_warpspec_gemm.cu:273-795) with a Blackwell design:
 //   warp 0     TMA producer: 64-wide K slices of A and W, SWIZZLE_128B, into a
@@ -21,7 +23,7 @@
 
 namespace b200 {
 
-enum GemmEpilogue : int { EPI_BIAS_F16 = 0, EPI_BIAS_GELU_F16 = 1, EPI_BIAS_RESID_F32 = 2 };
+enum GemmEpilogue : int { EPI_BIAS_F16 = 0, EPI_BIAS_GELU_F16 = 1, EPI_BIAS_RESID_F32 = 2, EPI_BIAS_F32 = 3 };
 
 struct GemmParams {
   int M, N, K;
@@ -149,6 +151,10 @@ __global__ void __launch_bounds__(192, 1)
               const float4 r = r4[i];
               o4[i] = make_float4(v[4 * i] + r.x, v[4 * i + 1] + r.y, v[4 * i + 2] + r.z, v[4 * i + 3] + r.w);
             }
+          } else if constexpr (EPI == EPI_BIAS_F32) {
+            float4* o4 = reinterpret_cast<float4*>(static_cast<float*>(p.out) + static_cast<int64_t>(row) * p.ld_out + col);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
           } else {
             if constexpr (EPI == EPI_BIAS_GELU_F16) {
 #pragma unroll

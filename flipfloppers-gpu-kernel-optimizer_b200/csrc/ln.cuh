@@ -79,4 +79,55 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// sum = a + b (+ bias per column), written out in fp32, then LayerNorm(sum) ->
+// out (fp16 or fp32): the residual add after a tensor-parallel all-reduce fused
+// with the LayerNorm that follows it.  d % 128 == 0.  sum_out may alias a
+// (each element is read and written by the same thread).
+template <int VPL, bool OUT_F16>
+__global__ void __launch_bounds__(256)
+    k_add_layernorm(const float* a, const float* __restrict__ b, const float* __restrict__ bias,
+                    float* sum_out, const float* __restrict__ gamma, const float* __restrict__ beta,
+                    void* __restrict__ out, int rows, int d, float eps) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + warp;
+  if (row >= rows) return;
+  float v[4 * VPL];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = 4 * lane + 128 * i;
+    const float4 ta = *reinterpret_cast<const float4*>(a + row * d + c);
+    const float4 tb = *reinterpret_cast<const float4*>(b + row * d + c);
+    float4 tc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (bias) tc = *reinterpret_cast<const float4*>(bias + c);
+    v[4 * i] = ta.x + tb.x + tc.x;
+    v[4 * i + 1] = ta.y + tb.y + tc.y;
+    v[4 * i + 2] = ta.z + tb.z + tc.z;
+    v[4 * i + 3] = ta.w + tb.w + tc.w;
+    *reinterpret_cast<float4*>(sum_out + row * d + c) = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    s += v[4 * i] + v[4 * i + 1] + v[4 * i + 2] + v[4 * i + 3];
+  }
+  const float mean = warp_sum(s) / static_cast<float>(d);
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4 * VPL; ++i) {
+    v[i] -= mean;
+    q += v[i] * v[i];
+  }
+  const float rstd = rsqrtf(warp_sum(q) / static_cast<float>(d) + eps);
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = 4 * lane + 128 * i;
+    const float4 g = *reinterpret_cast<const float4*>(gamma + c);
+    const float4 bb = *reinterpret_cast<const float4*>(beta + c);
+    const float y0 = v[4 * i] * rstd * g.x + bb.x, y1 = v[4 * i + 1] * rstd * g.y + bb.y;
+    const float y2 = v[4 * i + 2] * rstd * g.z + bb.z, y3 = v[4 * i + 3] * rstd * g.w + bb.w;
+    if constexpr (OUT_F16) {
+      *reinterpret_cast<uint2*>(static_cast<__half*>(out) + row * d + c) = make_uint2(pack_half2(y0, y1), pack_half2(y2, y3));
+    } else {
+      *reinterpret_cast<float4*>(static_cast<float*>(out) + row * d + c) = make_float4(y0, y1, y2, y3);
+    }
+  }
+}
+
 }  // namespace b200

@@ -147,7 +147,9 @@ class UserOptimizedTransformer(nn.Module):
         self._packs = None
         self._stack = None
         self._lnf = None
-        self.force_strategy: Optional[str] = None  # tests / benchmarks: "chain" or "fused_small"
+        self.force_strategy: Optional[str] = None  # tests / benchmarks: "chain", "chunked" or "fused_small"
+        self.chunk_rows: Optional[int] = None      # query rows per chunk of the chunked strategy (None: gate decides)
+        self._chunk_plan: Dict[Tuple, int] = {}
         self._ws: Dict[Tuple, torch.Tensor] = {}
         self._mask_cache: dict = {}
         self._plan: Dict[Tuple, str] = {}
@@ -214,18 +216,56 @@ class UserOptimizedTransformer(nn.Module):
           fits on chip);
         * ``chain`` -- per layer: LN, QKV GEMM, flash attention, out_proj GEMM
           (+residual), LN, ffn_in GEMM (+GELU), ffn_out GEMM (+residual), final
-          LN, all tcgen05 kernels."""
+          LN, all tcgen05 kernels;
+        * ``chunked`` -- the chain over query chunks with an fp16 K/V cache,
+          chosen by the memory gate (the reference's ``_would_oom_causal``,
+          TTB:1036-1116) when the chain's workspace would exceed
+          ``B200_CHUNK_MEM_FRAC`` of the free device memory."""
         if self.force_strategy is not None:
             if self.force_strategy == "fused_small" and not (self._fused_small_eligible() and S <= 128):
                 raise ValueError("fused_small needs d_model=128, 4 heads, ffn_dim<=512 (multiple of 128), seq_len<=128")
+            if self.force_strategy == "chunked":
+                self._chunk_plan[(B, S, device.index)] = self._chunk_rows_for(B, S, device)
             return self.force_strategy
         key = (B, S, device.index)
         hit = self._plan.get(key)
         if hit is not None:
             return hit
-        strat = "fused_small" if (self._fused_small_eligible() and S <= 128) else "chain"
+        cfg = self.config
+        if self._fused_small_eligible() and S <= 128:
+            strat = "fused_small"
+        elif _CHUNK_FORCE_ROWS > 0 or self._would_oom(B, S, device):
+            strat = "chunked"
+            self._chunk_plan[key] = self._chunk_rows_for(B, S, device)
+        else:
+            strat = "chain"
         self._plan[key] = strat
         return strat
+
+    def _memory_budget(self, device: torch.device) -> int:
+        free, _total = torch.cuda.mem_get_info(device)
+        return int(free * _CHUNK_MEM_FRAC)
+
+    def _would_oom(self, B: int, S: int, device: torch.device) -> bool:
+        """The chain path needs its workspace plus one fp32 [B,S,d] buffer per extra layer."""
+        cfg = self.config
+        M = B * S
+        need = rt.block_workspace_bytes(M, cfg.d_model, cfg.ffn_dim) + 4 * M * cfg.d_model * min(cfg.num_layers - 1, 2)
+        return need > self._memory_budget(device)
+
+    def _chunk_rows_for(self, B: int, S: int, device: torch.device) -> int:
+        """Largest query chunk (multiple of 128, <= S) whose workspace fits the budget."""
+        if self.chunk_rows:
+            return int(self.chunk_rows)
+        if _CHUNK_FORCE_ROWS > 0:
+            return _CHUNK_FORCE_ROWS
+        cfg = self.config
+        budget = self._memory_budget(device)
+        rows = min(S, 16384)
+        rows = max(128, rows - rows % 128)
+        while rows > 128 and rt.chunked_workspace_bytes(B * S, rows, cfg.d_model, cfg.ffn_dim) > budget:
+            rows -= 128
+        return rows
 
     def _workspace(self, nbytes: int, device: torch.device) -> torch.Tensor:
         key = (device.index,)
@@ -287,6 +327,9 @@ class UserOptimizedTransformer(nn.Module):
     def _launch(self, x: torch.Tensor, y: torch.Tensor, ws: torch.Tensor, strat: str) -> None:
         if strat == "fused_small":
             self._forward_fused_small(x, y)
+        elif strat == "chunked":
+            B, S, _ = x.shape
+            self._forward_chain(x, y, ws, chunk_rows=self._chunk_plan[(B, S, x.device.index)])
         else:
             self._forward_chain(x, y, ws)
 
@@ -305,7 +348,8 @@ class UserOptimizedTransformer(nn.Module):
         a.eps = float(self.layers[0].norm1.eps)
         rt.fused_small(a)
 
-    def _forward_chain(self, x: torch.Tensor, y: torch.Tensor, ws: torch.Tensor) -> None:
+    def _forward_chain(self, x: torch.Tensor, y: torch.Tensor, ws: torch.Tensor,
+                       chunk_rows: Optional[int] = None) -> None:
         cfg = self.config
         B, S, d = x.shape
         cur = x
@@ -329,7 +373,10 @@ class UserOptimizedTransformer(nn.Module):
                 a.lnf_w, a.lnf_b = None, None
             a.eps = float(self.layers[i].norm1.eps)
             a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
-            rt.block_forward(a)
+            if chunk_rows:
+                rt.block_forward_chunked(a, chunk_rows)
+            else:
+                rt.block_forward(a)
             cur = out
 
     # ------------------------------------------------------------------ host-buffer pipeline
@@ -417,6 +464,9 @@ class UserOptimizedTransformer(nn.Module):
         self.last_strategy = strat
         if strat == "chain":
             ws = self._workspace(rt.block_workspace_bytes(B * S, d, self.config.ffn_dim), dev)
+        elif strat == "chunked":
+            rows = self._chunk_plan[(B, S, dev.index)]
+            ws = self._workspace(rt.chunked_workspace_bytes(B * S, rows, d, self.config.ffn_dim), dev)
         else:
             ws = self._workspace(256, dev)
         if _GRAPHS_ON and xin.numel() <= _GRAPH_MAX_ELEMS:

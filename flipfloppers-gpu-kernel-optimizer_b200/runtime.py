@@ -25,6 +25,7 @@ B200_OK = 0
 EPI_BIAS_F16 = 0
 EPI_BIAS_GELU_F16 = 1
 EPI_BIAS_RESID_F32 = 2
+EPI_BIAS_F32 = 3
 
 _lib = None
 _lock = threading.Lock()
@@ -100,6 +101,8 @@ EXPORTS = [
     ("b200_device_error", ctypes.c_int, [ctypes.c_int]),
     ("b200_layernorm_launch", ctypes.c_int,
      [_vp, _c_ll, _vp, _vp, _vp, _c_ll, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, _vp]),
+    ("b200_add_layernorm_launch", ctypes.c_int,
+     [_vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, _vp]),
     ("b200_gemm_launch", ctypes.c_int,
      [ctypes.c_int, _vp, _c_ll, _vp, _c_ll, _vp, _vp, _c_ll, _vp, _c_ll, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
     ("b200_flash_causal_launch", ctypes.c_int, [ctypes.POINTER(AttnArgs), _vp]),
@@ -107,6 +110,8 @@ EXPORTS = [
     ("b200_block_forward", ctypes.c_int, [ctypes.POINTER(BlockArgs), _vp]),
     ("b200_block_forward_noalloc", ctypes.c_int, [ctypes.POINTER(BlockArgs), _vp]),
     ("b200_block_fused_small_launch", ctypes.c_int, [ctypes.POINTER(FusedSmallArgs), _vp]),
+    ("b200_block_chunked_workspace_bytes", ctypes.c_size_t, [_c_ll, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    ("b200_block_forward_chunked", ctypes.c_int, [ctypes.POINTER(BlockArgs), ctypes.c_int, _vp]),
 ]
 
 
@@ -177,6 +182,19 @@ def layernorm(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, out: tor
     return out
 
 
+def add_layernorm(a: torch.Tensor, b: torch.Tensor, bias: Optional[torch.Tensor], sum_out: torch.Tensor,
+                  gamma: torch.Tensor, beta: torch.Tensor, out: torch.Tensor, eps: float = 1e-5,
+                  stream=None) -> torch.Tensor:
+    """sum_out = a + b + bias; out = LayerNorm(sum_out) * gamma + beta (fp16 or fp32 out)."""
+    _require_cuda(a, b, bias, sum_out, gamma, beta, out)
+    d = a.shape[-1]
+    rows = a.numel() // d
+    rc = lib().b200_add_layernorm_launch(_p(a), _p(b), _p(bias), _p(sum_out), _p(gamma), _p(beta), _p(out),
+                                         int(out.dtype == torch.float16), rows, d, float(eps), _stream(stream))
+    check(rc, "b200_add_layernorm_launch")
+    return out
+
+
 def gemm(epilogue: int, a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor], out: torch.Tensor,
          resid: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
     """out = epilogue(a @ w.T + bias [+ resid]); a [M,K] fp16, w [N,K] fp16, bias fp32."""
@@ -221,6 +239,15 @@ def block_workspace_bytes(tokens: int, d_model: int, ffn_dim: int) -> int:
 
 def block_forward(args: BlockArgs, stream=None) -> None:
     check(lib().b200_block_forward(ctypes.byref(args), _stream(stream)), "b200_block_forward")
+
+
+def chunked_workspace_bytes(tokens: int, chunk_rows: int, d_model: int, ffn_dim: int) -> int:
+    return int(lib().b200_block_chunked_workspace_bytes(int(tokens), int(chunk_rows), int(d_model), int(ffn_dim)))
+
+
+def block_forward_chunked(args: BlockArgs, chunk_rows: int, stream=None) -> None:
+    check(lib().b200_block_forward_chunked(ctypes.byref(args), int(chunk_rows), _stream(stream)),
+          "b200_block_forward_chunked")
 
 
 def fused_small(args: FusedSmallArgs, stream=None) -> None:

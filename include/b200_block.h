@@ -64,7 +64,8 @@ enum {
 enum {
   B200_EPI_BIAS_F16 = 0,       /* out(f16) = A.W^T + bias                     */
   B200_EPI_BIAS_GELU_F16 = 1,  /* out(f16) = gelu_erf(A.W^T + bias)           */
-  B200_EPI_BIAS_RESID_F32 = 2  /* out(f32) = resid + A.W^T + bias (in place ok) */
+  B200_EPI_BIAS_RESID_F32 = 2, /* out(f32) = resid + A.W^T + bias (in place ok) */
+  B200_EPI_BIAS_F32 = 3        /* out(f32) = A.W^T + bias (bias may be null)   */
 };
 
 int b200_abi_version(void);
@@ -84,6 +85,14 @@ int b200_device_error(int clear);
  * d % 32 == 0, d <= 4096. */
 int b200_layernorm_launch(const float* x, long long ld_x, const float* gamma, const float* beta, void* out,
                           long long ld_out, int out_f16, int rows, int d, float eps, b200_stream_t stream);
+
+/* sum_out = a + b (+ bias[col]) in fp32, then out = LayerNorm(sum_out) *
+ * gamma + beta (fp16 or fp32): the residual add after a tensor-parallel
+ * all-reduce fused with the LayerNorm that follows (norm2 / final_norm of the
+ * reference, TTB:160-161, 189).  Row-major [rows, d], d % 128 == 0. */
+int b200_add_layernorm_launch(const float* a, const float* b, const float* bias, float* sum_out, const float* gamma,
+                              const float* beta, void* out, int out_f16, int rows, int d, float eps,
+                              b200_stream_t stream);
 
 /* out[M,N] = epilogue(A[M,K] . W[N,K]^T + bias[N]).  A, W fp16 row-major with
  * leading dimensions lda, ldw (elements); bias fp32 (may be null); resid fp32
@@ -149,6 +158,16 @@ typedef struct {
 
 size_t b200_block_workspace_bytes(long long tokens, int d_model, int ffn_dim);
 int b200_block_forward(const B200BlockArgs* args, b200_stream_t stream);
+
+/* The same block, sequence-chunked for problems whose full activations do
+ * not fit (the reference's _chunked_forward_causal,
+ * torch_transformer_benchmark.py:1378-1609): per sequence, query chunks of
+ * chunk_rows rows in order; each chunk appends its K/V rows to an fp16 cache
+ * [batch*seq_len, 2*d_model] and attends keys [0, chunk end) prefix-causally.
+ * workspace >= b200_block_chunked_workspace_bytes(batch*seq_len, chunk_rows,
+ * d_model, ffn_dim) = the K/V cache plus one chunk's activations. */
+size_t b200_block_chunked_workspace_bytes(long long tokens, int chunk_rows, int d_model, int ffn_dim);
+int b200_block_forward_chunked(const B200BlockArgs* args, int chunk_rows, b200_stream_t stream);
 
 /* Whole causal model (num_layers pre-LN blocks + final LayerNorm) in ONE
  * persistent kernel, for small models: d_model == 128, num_heads == 4,
