@@ -549,7 +549,9 @@ int block_chunked_impl(const B200BlockArgs* a, int chunk_rows, cudaStream_t st) 
       at.ld_q = d;
       at.ld_k = at.ld_v = 2 * d;
       at.q_rows = Rc;
-      at.kv_rows = M;
+      // the cache rows after this chunk are not written yet: end the tensor at the
+      // last valid key so the key tile that straddles it is zero-filled by TMA
+      at.kv_rows = static_cast<long long>(b) * S + c0 + Rc;
       at.batch = 1;
       at.heads = H;
       at.head_dim = hd;

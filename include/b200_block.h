@@ -107,7 +107,10 @@ int b200_gemm_launch(int epilogue, const void* A, long long lda, const void* W, 
  * sequence b at rows (row0 + b*seq_rows + position) and columns
  * (col0 + h*head_dim ...).  Query i of a sequence sits at absolute position
  * q_offset + i and attends keys 0..q_offset+i (prefix-causal).  Writes the
- * fp16 context [out_row0 + b*out_seq_rows + i, h*head_dim ...]. */
+ * fp16 context [out_row0 + b*out_seq_rows + i, h*head_dim ...].
+ * Keys are read in tiles: rows of the last tile past a sequence's kv_len but
+ * below kv_rows are read too (with probability 0) and must hold finite values;
+ * rows at or past kv_rows read as zeros. */
 typedef struct {
   const void* q;
   const void* k;
