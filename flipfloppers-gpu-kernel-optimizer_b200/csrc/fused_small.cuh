@@ -28,7 +28,8 @@
 //   accumulator.
 // Shared memory (1 CTA/SM): XA 32 KB (LN1 out -> context -> LN2 out, fp16,
 //   SW128 K-major), Q/K/V 3 x 4 heads x 8 KB (SW64; V read MN-major), P 32 KB,
-//   weight ring 48 KB, GELU chunk ping-pong aliasing the Q and K areas.
+//   weight ring 48 KB, GELU chunk ping-pong aliasing the Q and K areas, the
+//   layer's biases and LayerNorm parameters (7.5 KB, staged once per layer).
 //
 // Every wait is bounded (ptx.cuh); a worker that gives up still executes every
 // named barrier (control flow never depends on data), so the CTA always
@@ -70,7 +71,11 @@ struct SmallCfg {
   static constexpr int OFF_P = 131072;          // 32 KB
   static constexpr int OFF_W = 163840;          // WST x 16 KB
   static constexpr int OFF_STATS = OFF_W + WST * BOX;   // float [2][4][128]
-  static constexpr int OFF_BAR = OFF_STATS + 2 * 4 * 128 * 4;
+  static constexpr int OFF_VEC = OFF_STATS + 2 * 4 * 128 * 4;  // per-layer vectors, fp32
+  // float offsets inside the vector block
+  static constexpr int V_LN1W = 0, V_LN1B = 128, V_BQKV = 256, V_BO = 640, V_LN2W = 768, V_LN2B = 896,
+                       V_BIN = 1024, V_BOUT = 1536, V_LNFW = 1664, V_LNFB = 1792, V_TOTAL = 1920;
+  static constexpr int OFF_BAR = OFF_VEC + V_TOTAL * 4;
   static constexpr int TOTAL = OFF_BAR + 512 + 1024;
 };
 
@@ -304,6 +309,8 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
     const uint32_t trow = tmem + (static_cast<uint32_t>(q * 32) << 16);
     float* st0 = stats;                  // [4][128]
     float* st1 = stats + 512;
+    float* vec = reinterpret_cast<float*>(smem + C::OFF_VEC);
+    const int wtid = threadIdx.x - 64;   // 0..511 among the workers
     uint8_t* xa = smem + C::OFF_XA;
     bool ok = true;
     float v[32];
@@ -324,22 +331,22 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
       return fmaxf(fmaxf(buf[r], buf[128 + r]), fmaxf(buf[256 + r], buf[384 + r]));
     };
     // LayerNorm of v (32 columns of this row) in place, two-pass statistics
-    auto layer_norm = [&](const float* gamma, const float* beta) {
-      float s = 0.f;
+    auto layer_norm = [&](const float* gamma, const float* beta) {  // gamma/beta: shared memory
+      float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int i = 0; i < 32; ++i) s += v[i];
-      const float mean = row_sum(s, st0) * (1.f / 128.f);
-      float qq = 0.f;
+      for (int i = 0; i < 32; ++i) s4[i & 3] += v[i];
+      const float mean = row_sum((s4[0] + s4[1]) + (s4[2] + s4[3]), st0) * (1.f / 128.f);
+      float q4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         v[i] -= mean;
-        qq += v[i] * v[i];
+        q4[i & 3] += v[i] * v[i];
       }
-      const float rstd = rsqrtf(row_sum(qq, st1) * (1.f / 128.f) + p.eps);
+      const float rstd = rsqrtf(row_sum((q4[0] + q4[1]) + (q4[2] + q4[3]), st1) * (1.f / 128.f) + p.eps);
 #pragma unroll
       for (int i = 0; i < 32; i += 4) {
-        const float4 gg = __ldg(reinterpret_cast<const float4*>(gamma + c0 + i));
-        const float4 bb = __ldg(reinterpret_cast<const float4*>(beta + c0 + i));
+        const float4 gg = *reinterpret_cast<const float4*>(gamma + c0 + i);
+        const float4 bb = *reinterpret_cast<const float4*>(beta + c0 + i);
         v[i] = v[i] * rstd * gg.x + bb.x;
         v[i + 1] = v[i + 1] * rstd * gg.y + bb.y;
         v[i + 2] = v[i + 2] * rstd * gg.z + bb.z;
@@ -370,19 +377,42 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
       mbar_arrive(&bar[slot]);
     };
 
+    // copy a layer's biases and LayerNorm parameters into shared memory (all 512 workers)
+    auto stage_vectors = [&](int l) {
+      auto cp = [&](int dst, const float* src, int n) {
+        for (int i = wtid * 4; i < n; i += 512 * 4)
+          *reinterpret_cast<float4*>(vec + dst + i) = __ldg(reinterpret_cast<const float4*>(src + i));
+      };
+      cp(C::V_LN1W, p.ln1_w + l * 128, 128);
+      cp(C::V_LN1B, p.ln1_b + l * 128, 128);
+      cp(C::V_BQKV, p.b_qkv + l * 384, 384);
+      cp(C::V_BO, p.b_o + l * 128, 128);
+      cp(C::V_LN2W, p.ln2_w + l * 128, 128);
+      cp(C::V_LN2B, p.ln2_b + l * 128, 128);
+      cp(C::V_BIN, p.b_in + l * p.ffn, p.ffn);
+      cp(C::V_BOUT, p.b_out + l * 128, 128);
+      cp(C::V_LNFW, p.lnf_w, 128);
+      cp(C::V_LNFB, p.lnf_b, 128);
+    };
+
     for (int step = 0; step < nsteps; ++step) {
       const int l = step % p.layers;
       const int seq = static_cast<int>(blockIdx.x) + (step / p.layers) * static_cast<int>(gridDim.x);
       const bool row_ok = r < p.seq_len;
       const int64_t grow = static_cast<int64_t>(seq) * p.seq_len + r;
       const float* xin = (l == 0 ? p.x : p.y) + grow * C::D + c0;
-      // ---- W1: LN1 -> XA
+      // ---- W1: LN1 -> XA (x loads first, so their latency overlaps the vector staging)
 #pragma unroll
       for (int i = 0; i < 32; i += 4) {
         float4 t = row_ok ? *reinterpret_cast<const float4*>(xin + i) : make_float4(0.f, 0.f, 0.f, 0.f);
         v[i] = t.x; v[i + 1] = t.y; v[i + 2] = t.z; v[i + 3] = t.w;
       }
-      layer_norm(p.ln1_w + l * 128, p.ln1_b + l * 128);
+      if (step == 0 || p.layers > 1) {
+        named_bar(5, 32 * C::NW);  // every worker is done with the previous layer's vectors
+        stage_vectors(l);
+        named_bar(5, 32 * C::NW);
+      }
+      layer_norm(vec + C::V_LN1W, vec + C::V_LN1B);
       store_sw128(xa);
       publish(SB_N1);
       // ---- W2: QKV accumulator -> Q/K/V tiles (head g = column group g)
@@ -390,10 +420,10 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
 #pragma unroll 1
       for (int nt = 0; nt < 3; ++nt) {
         if (ok) tmem_ld32(trow + nt * 128 + c0, v);
-        const float* bq = p.b_qkv + l * 384 + nt * 128 + c0;
+        const float* bq = vec + C::V_BQKV + nt * 128 + c0;
 #pragma unroll
         for (int i = 0; i < 32; i += 4) {
-          const float4 bb = __ldg(reinterpret_cast<const float4*>(bq + i));
+          const float4 bb = *reinterpret_cast<const float4*>(bq + i);
           v[i] += bb.x; v[i + 1] += bb.y; v[i + 2] += bb.z; v[i + 3] += bb.w;
         }
         store_sw64(smem + (nt == 0 ? C::OFF_Q : nt == 1 ? C::OFF_K : C::OFF_V) + g * 8192);
@@ -413,13 +443,14 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
           mx = fmaxf(mx, t);
         }
         const float m = row_max(mx, st0);  // reductions alternate st0/st1 strictly
-        float sum = 0.f;
+        float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const float e = fast_exp2(v[i] - m);
           v[i] = e;
-          sum += e;
+          s4[i & 3] += e;
         }
+        const float sum = (s4[0] + s4[1]) + (s4[2] + s4[3]);
         // P of the previous head must have been consumed before P is overwritten
         if (h > 0) wait_w(SB_PV_DONE, par(step, 4, h - 1));
         store_sw128(smem + C::OFF_P);
@@ -438,19 +469,22 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
       store_sw128(xa);
       publish(SB_CTX);
       // ---- W5: x1 = x + ctx.Wo^T + bo (kept in TMEM) ; LN2 -> XA
-      wait_w(SB_OP_DONE, par(step, 1, 0));
-      if (ok) tmem_ld32(trow + 384 + c0, v);
-      {
-        const float* bo = p.b_o + l * 128 + c0;
 #pragma unroll
-        for (int i = 0; i < 32; i += 4) {
-          const float4 bb = __ldg(reinterpret_cast<const float4*>(bo + i));
-          const float4 xr = row_ok ? *reinterpret_cast<const float4*>(xin + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-          v[i] += bb.x + xr.x; v[i + 1] += bb.y + xr.y; v[i + 2] += bb.z + xr.z; v[i + 3] += bb.w + xr.w;
-        }
+      for (int i = 0; i < 32; i += 4) {  // residual + bias, loaded while the out_proj MMA runs
+        const float4 bb = *reinterpret_cast<const float4*>(vec + C::V_BO + c0 + i);
+        const float4 xr = row_ok ? *reinterpret_cast<const float4*>(xin + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        v[i] = bb.x + xr.x; v[i + 1] = bb.y + xr.y; v[i + 2] = bb.z + xr.z; v[i + 3] = bb.w + xr.w;
+      }
+      wait_w(SB_OP_DONE, par(step, 1, 0));
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        float t[16];
+        if (ok) tmem_ld16(trow + 384 + c0 + 16 * half, t);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[16 * half + i] += t[i];
       }
       if (ok) tmem_st32(trow + 384 + c0, v);
-      layer_norm(p.ln2_w + l * 128, p.ln2_b + l * 128);
+      layer_norm(vec + C::V_LN2W, vec + C::V_LN2B);
       store_sw128(xa);
       publish(SB_N2);
       // ---- W6: GELU chunks -> H ping-pong
@@ -459,10 +493,18 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
         const int b = c & 1;
         wait_w(SB_FIN + b, par(step, b ? per_b1 : per_b0, c >> 1));
         if (ok) tmem_ld32(trow + b * 128 + c0, v);
-        const float* b1 = p.b_in + l * p.ffn + c * 128 + c0;
+        if (c == 0 && l == p.layers - 1) {
+          // pull the next sequence's rows toward L2 while the FFN runs
+          const int nseq = seq + static_cast<int>(gridDim.x);
+          if (nseq < p.num_seq && row_ok) {
+            const float* nx = p.x + (static_cast<int64_t>(nseq) * p.seq_len + r) * C::D + c0;
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(nx) : "memory");
+          }
+        }
+        const float* b1 = vec + C::V_BIN + c * 128 + c0;
 #pragma unroll
         for (int i = 0; i < 32; i += 4) {
-          const float4 bb = __ldg(reinterpret_cast<const float4*>(b1 + i));
+          const float4 bb = *reinterpret_cast<const float4*>(b1 + i);
           v[i] = gelu_erf(v[i] + bb.x);
           v[i + 1] = gelu_erf(v[i + 1] + bb.y);
           v[i + 2] = gelu_erf(v[i + 2] + bb.z);
@@ -480,15 +522,15 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
       for (int half = 0; half < 2; ++half) {
         float x1[16];
         if (ok) tmem_ld16(trow + 384 + c0 + 16 * half, x1);
-        const float* b2 = p.b_out + l * 128 + c0 + 16 * half;
+        const float* b2 = vec + C::V_BOUT + c0 + 16 * half;
 #pragma unroll
         for (int i = 0; i < 16; i += 4) {
-          const float4 bb = __ldg(reinterpret_cast<const float4*>(b2 + i));
+          const float4 bb = *reinterpret_cast<const float4*>(b2 + i);
           float* w = v + 16 * half + i;
           w[0] += bb.x + x1[i]; w[1] += bb.y + x1[i + 1]; w[2] += bb.z + x1[i + 2]; w[3] += bb.w + x1[i + 3];
         }
       }
-      if (l == p.layers - 1) layer_norm(p.lnf_w, p.lnf_b);
+      if (l == p.layers - 1) layer_norm(vec + C::V_LNFW, vec + C::V_LNFB);
       if (row_ok && ok) {
         float* yo = p.y + grow * C::D + c0;
 #pragma unroll
