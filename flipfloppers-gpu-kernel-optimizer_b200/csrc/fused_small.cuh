@@ -505,10 +505,10 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
 #pragma unroll
         for (int i = 0; i < 32; i += 4) {
           const float4 bb = *reinterpret_cast<const float4*>(b1 + i);
-          v[i] = gelu_erf(v[i] + bb.x);
-          v[i + 1] = gelu_erf(v[i + 1] + bb.y);
-          v[i + 2] = gelu_erf(v[i + 2] + bb.z);
-          v[i + 3] = gelu_erf(v[i + 3] + bb.w);
+          v[i] = gelu_as(v[i] + bb.x);
+          v[i + 1] = gelu_as(v[i + 1] + bb.y);
+          v[i + 2] = gelu_as(v[i + 2] + bb.z);
+          v[i + 3] = gelu_as(v[i + 3] + bb.w);
         }
         // the buffer's previous chunk (c-2) must have been consumed by ffn_out
         if (c >= 2) wait_w(SB_HFREE + b, par(step, b ? per_b1 : per_b0, (c >> 1) - 1));

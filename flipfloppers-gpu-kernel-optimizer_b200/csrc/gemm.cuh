@@ -3,7 +3,7 @@
 // A, W fp16 row-major (K contiguous, "K-major" for UMMA); fp32 accumulation in
 // TMEM; fp32 bias.  Epilogues:
 //   EPI_BIAS_F16       fp16 out            (QKV projection, reference TTB:1303)
-//   EPI_BIAS_GELU_F16  fp16 gelu_erf(.)    (ffn_in + exact GELU, TTB:1350-1354)
+//   EPI_BIAS_GELU_F16  fp16 gelu_as(.)    (ffn_in + exact GELU, TTB:1350-1354)
 //   EPI_BIAS_RESID_F32 fp32 out = resid+.  (out_proj / ffn_out + residual,
 //                                           TTB:1333-1339, 1368-1369)
 //   EPI_BIAS_F32       fp32 out            (row-parallel partial sums before
@@ -158,7 +158,7 @@ __global__ void __launch_bounds__(192, 1)
           } else {
             if constexpr (EPI == EPI_BIAS_GELU_F16) {
 #pragma unroll
-              for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
+              for (int i = 0; i < 32; ++i) v[i] = gelu_as(v[i]);
             }
             uint4* o4 = reinterpret_cast<uint4*>(static_cast<__half*>(p.out) + static_cast<int64_t>(row) * p.ld_out + col);
 #pragma unroll

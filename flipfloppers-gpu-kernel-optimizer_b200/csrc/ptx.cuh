@@ -255,6 +255,37 @@ __device__ __forceinline__ float gelu_erf(float v) {
   return 0.5f * v * (1.0f + erff(v * 0.70710678118654752440f));
 }
 
+__device__ __forceinline__ float fast_rcp(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// The same GELU with erf from Abramowitz & Stegun, Handbook of Mathematical
+// Functions (1964), eq. 7.1.28:  erf(u) = 1 - (1 + a1 u + ... + a6 u^6)^-16,
+// |error| <= 3e-7 for u >= 0, extended as an odd function.  Branch-free: six
+// FMAs, four squarings and one reciprocal.  Evaluated in fp32 the GELU stays
+// within 2e-6 (absolute) of the exact one on [-12, 12] (checked on the CPU in
+// tests/test_gelu_cpu.py and against torch's GELU on the GPU); it feeds fp16
+// activations, whose rounding is ~250x larger.
+__device__ __forceinline__ float gelu_as(float v) {
+  const float u = fabsf(v) * 0.70710678118654752440f;
+  float q = 4.30638e-5f;
+  q = fmaf(q, u, 2.765672e-4f);
+  q = fmaf(q, u, 1.520143e-4f);
+  q = fmaf(q, u, 9.2705272e-3f);
+  q = fmaf(q, u, 4.22820123e-2f);
+  q = fmaf(q, u, 7.05230784e-2f);
+  q = fmaf(q, u, 1.0f);
+  q = q * q;
+  q = q * q;
+  q = q * q;
+  q = q * q;  // (1 + a1 u + ... )^16; overflows to inf for large u -> erf = 1
+  const float e = copysignf(1.0f - fast_rcp(q), v);  // erf(v / sqrt(2))
+  const float hv = 0.5f * v;
+  return fmaf(hv, e, hv);
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
