@@ -88,6 +88,12 @@ int set_smem(const void* fn, int bytes) {
   return B200_OK;
 }
 
+int num_sms() {
+  int dev = current_device(), n = 0;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
 int launch_status() {
   const cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess) return B200_OK;
@@ -133,8 +139,9 @@ int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams
   auto kern = k_gemm_tn<BN, STAGES, EPI>;
   const int smem = GemmSmem<BN, STAGES>::TOTAL;
   if (int rc = set_smem(reinterpret_cast<const void*>(kern), smem)) return rc;
-  dim3 grid((p.N + BN - 1) / BN, (p.M + 127) / 128);
-  kern<<<grid, 192, smem, st>>>(ta, tw, p);
+  const long long tiles = static_cast<long long>((p.M + 127) / 128) * ((p.N + BN - 1) / BN);
+  const int grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
+  kern<<<grid, GEMM_THREADS, smem, st>>>(ta, tw, p);
   return launch_status();
 }
 
@@ -167,7 +174,6 @@ int gemm_impl(int epi, const void* A, long long lda, const void* W, long long ld
   if (ld_out < N || ld_out % (f32_out ? 4 : 8)) return B200_ERR_ALIGN;
   if (!al16(A) || !al16(W) || !al16(out) || (bias && !al16(bias))) return B200_ERR_ALIGN;
   if (epi == EPI_BIAS_RESID_F32 && (!al16(resid) || ld_resid % 4 || ld_resid < N)) return B200_ERR_ALIGN;
-  if ((M + 127) / 128 > 65535) return B200_ERR_TILE;
   if (int rc = check_arch()) return rc;
   const int BN = pick_bn(M, N);
   CUtensorMap ta, tw;
@@ -328,12 +334,6 @@ int attn_impl(const B200AttnArgs* a, cudaStream_t st) {
 }
 
 // ------------------------------------------------------------------ fused small-model kernel
-int num_sms() {
-  int dev = current_device(), n = 0;
-  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  return n > 0 ? n : 148;
-}
-
 int fused_small_impl(const B200FusedSmallArgs* a, cudaStream_t st) {
   if (!a || !a->x || !a->y || !a->w_qkv || !a->w_o || !a->w_in || !a->w_out) return B200_ERR_ARG;
   if (!a->ln1_w || !a->ln1_b || !a->ln2_w || !a->ln2_b || !a->lnf_w || !a->lnf_b || !a->b_qkv || !a->b_o ||
