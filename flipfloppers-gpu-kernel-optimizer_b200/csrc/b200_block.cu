@@ -156,10 +156,12 @@ int launch_gemm_bn(int epi, const CUtensorMap& ta, const CUtensorMap& tw, const 
   }
 }
 
+// 128x256 tiles keep 192 KB of operands in flight (4 stages), enough to cover
+// the L2 round trip at full MMA rate; 128x128 tiles (6 x 32 KB) are not, so
+// they are used only when N is not a multiple of 256.
 int pick_bn(long long M, int N) {
-  const long long mt = (M + 127) / 128;
-  if (N % 256 == 0 && mt * (N / 256) >= 2 * 148) return 256;
-  return 128;
+  (void)M;
+  return N % 256 == 0 ? 256 : 128;
 }
 
 int gemm_impl(int epi, const void* A, long long lda, const void* W, long long ldw, const float* bias,
