@@ -1,0 +1,299 @@
+// Causal flash attention, two query tiles per CTA (head_dim 32 or 64).
+//
+// Same semantics and argument block as k_flash_causal (attn.cuh): the
+// reference's causal attention (TTB:117-132) with the prefix offset of its
+// chunked forward (TTB:1491-1500).  Structure:
+//   warp 0      TMA producer: Q tiles t=0,1 (rows qp*256 + t*128 ...), then K_j / V_j
+//               into a 3-deep ring shared by both query tiles;
+//   warp 1      TMEM owner and MMA issuer, ping-ponging the two tiles:
+//               S_t,j = Q_t.K_j^T into TMEM columns [128t, 128t+128) and
+//               O_t += P_t,j.V_j into [256 + t*HD, ...), so tile 1's QK^T and
+//               tile 0's PV run while the other tile's softmax runs;
+//   warps 2-5   softmax of query tile 0, warps 6-9 of tile 1: one row per
+//               thread, log2-domain running max with lazy rescaling (the max
+//               used for the exponentials moves only when a new tile raises it
+//               by more than 8, i.e. P <= 2^8; only then is O rescaled in TMEM),
+//               P in fp16 to shared memory (128B-swizzled K-major).
+// Key tiles past a query tile's diagonal are skipped; query tile 1 may need
+// one more key tile than tile 0.
+#pragma once
+
+#include "attn.cuh"
+
+namespace b200 {
+
+template <int HD>
+struct Attn2Cfg {
+  static constexpr int BN = 128;
+  static constexpr int ATOM_E = HD;                     // 32 -> SW64, 64 -> SW128 (one box per tile)
+  static constexpr int ROWB = HD * 2;
+  static constexpr uint32_t SWZ = HD == 64 ? UMMA_SW128 : UMMA_SW64;
+  static constexpr int ST = 3;                          // K/V ring depth
+  static constexpr int Q_BYTES = 128 * HD * 2;
+  static constexpr int KV_BYTES = BN * HD * 2;
+  static constexpr int P_BYTES = 128 * BN * 2;
+  static constexpr int OFF_Q = 0;                       // [2]
+  static constexpr int OFF_K = 2 * Q_BYTES;             // [ST] K, then [ST] V
+  static constexpr int OFF_V = OFF_K + ST * KV_BYTES;
+  static constexpr int OFF_P = OFF_V + ST * KV_BYTES;   // [2]
+  static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
+  static constexpr int TOTAL = OFF_BAR + 256 + 1024;
+  static constexpr float RESCALE_THRESHOLD = 8.0f;      // log2 units
+  static_assert(HD == 32 || HD == 64, "two-tile kernel covers head_dim 32 and 64");
+};
+
+template <int HD>
+__global__ void __launch_bounds__(320, 1)
+    k_flash_causal2(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
+  using C = Attn2Cfg<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;            // [ST]
+  uint64_t* kv_empty = kv_full + C::ST;    // [ST]
+  uint64_t* s_full = kv_empty + C::ST;     // [2]
+  uint64_t* p_full = s_full + 2;           // [2]
+  uint64_t* pv_done = p_full + 2;          // [2]
+  uint64_t* drain = pv_done + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int npair = (p.q_len + 255) / 256;
+  const int qp = npair - 1 - static_cast<int>(blockIdx.x);  // latest query rows first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int kv_tiles = (p.kv_len + C::BN - 1) / C::BN;
+  // key tiles each query tile needs (0 if the tile holds no query row)
+  int ntile[2];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int r0 = qp * 256 + t * 128;
+    if (r0 >= p.q_len) {
+      ntile[t] = 0;
+    } else {
+      const int q_last = p.q_offset + min(p.q_len, r0 + 128) - 1;
+      ntile[t] = min(q_last / C::BN + 1, kv_tiles);
+    }
+  }
+  const int n_all = max(ntile[0], ntile[1]);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < C::ST; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 128);
+      mbar_init(&pv_done[t], 1);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      const int qrow = p.q_row0 + b * p.q_seq_rows + qp * 256;
+      mbar_arrive_expect_tx(q_full, 2 * C::Q_BYTES);
+      tma_load_2d(smem + C::OFF_Q, &tmQ, q_full, p.q_col0 + h * HD, qrow);
+      tma_load_2d(smem + C::OFF_Q + C::Q_BYTES, &tmQ, q_full, p.q_col0 + h * HD, qrow + 128);
+      int issued = 0;
+      for (int j = 0; j < n_all; ++j) {
+        const int s = j % C::ST;
+        if (j >= C::ST && !mbar_wait(&kv_empty[s], ((j / C::ST) - 1) & 1, abort_flag, DERR_WAIT_SLOT)) break;
+        const int krow = p.kv_row0 + b * p.kv_seq_rows + j * C::BN;
+        mbar_arrive_expect_tx(&kv_full[s], 2 * C::KV_BYTES);
+        tma_load_2d(smem + C::OFF_K + s * C::KV_BYTES, &tmK, &kv_full[s], p.k_col0 + h * HD, krow);
+        tma_load_2d(smem + C::OFF_V + s * C::KV_BYTES, &tmV, &kv_full[s], p.v_col0 + h * HD, krow);
+        issued = j + 1;
+      }
+      if (*abort_flag) {
+        mbar_wait_drain(q_full, 0);
+        for (int j = (issued > C::ST ? issued - C::ST : 0); j < issued; ++j)
+          mbar_wait_drain(&kv_full[j % C::ST], (j / C::ST) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = make_idesc_f16(128, C::BN, false);
+      constexpr uint32_t idesc_o = make_idesc_f16(128, HD, true);
+      const uint32_t q_addr = smem_u32(smem + C::OFF_Q);
+      const uint32_t k_addr = smem_u32(smem + C::OFF_K);
+      const uint32_t v_addr = smem_u32(smem + C::OFF_V);
+      const uint32_t p_addr = smem_u32(smem + C::OFF_P);
+      int kv_seen = 0;  // key tiles whose TMA load has been waited for
+      bool ok = mbar_wait(q_full, 0, abort_flag, DERR_WAIT_TMA);
+      auto need_kv = [&](int j) {
+        while (ok && kv_seen <= j) {
+          if (!mbar_wait(&kv_full[kv_seen % C::ST], (kv_seen / C::ST) & 1, abort_flag, DERR_WAIT_TMA)) ok = false;
+          ++kv_seen;
+        }
+        if (ok) tc_fence_after();
+        return ok;
+      };
+      auto issue_s = [&](int t, int j) {
+        const uint32_t kk_base = k_addr + (j % C::ST) * C::KV_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk)
+          umma_f16_ss(tmem + t * 128, make_sdesc(q_addr + t * C::Q_BYTES + kk * 32, 16, 8 * C::ROWB, C::SWZ),
+                      make_sdesc(kk_base + kk * 32, 16, 8 * C::ROWB, C::SWZ), idesc_s, kk > 0 ? 1u : 0u);
+        tc_commit(&s_full[t]);
+      };
+      if (ok && n_all > 0 && need_kv(0)) {
+        if (ntile[0] > 0) issue_s(0, 0);
+        if (ntile[1] > 0) issue_s(1, 0);
+      }
+      for (int j = 0; ok && j < n_all; ++j) {
+        const uint32_t vb = v_addr + (j % C::ST) * C::KV_BYTES;
+        for (int t = 0; t < 2; ++t) {
+          if (j >= ntile[t]) continue;
+          if (!mbar_wait(&p_full[t], j & 1, abort_flag, DERR_WAIT_SOFTMAX)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t pb = p_addr + t * C::P_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < C::BN / 16; ++kk)
+            umma_f16_ss(tmem + 256 + t * HD, make_sdesc(pb + (kk >> 2) * (128 * 128) + (kk & 3) * 32, 16, 1024, UMMA_SW128),
+                        make_sdesc(vb + kk * 16 * C::ROWB, C::BN * C::ROWB, 8 * C::ROWB, C::SWZ), idesc_o,
+                        (j > 0 || kk > 0) ? 1u : 0u);
+          tc_commit(&pv_done[t]);
+          if (j + 1 < ntile[t]) {
+            if (!need_kv(j + 1)) break;
+            issue_s(t, j + 1);
+          }
+        }
+        if (!ok) break;
+        tc_commit(&kv_empty[j % C::ST]);
+      }
+      if (*abort_flag) {
+        tc_commit(drain);
+        mbar_wait_drain(drain, 0);
+      }
+    }
+  } else {
+    // softmax warpgroup t = 0 (warps 2-5) or 1 (warps 6-9)
+    const int t = (warp - 2) >> 2;
+    const int qd = warp & 3;
+    const int rl = qd * 32 + lane;
+    const int row_in_seq = qp * 256 + t * 128 + rl;
+    const int qpos = p.q_offset + row_in_seq;
+    const int q_first = p.q_offset + qp * 256 + t * 128;
+    const uint32_t trow = tmem + (static_cast<uint32_t>(qd * 32) << 16);
+    uint8_t* ps = smem + C::OFF_P + t * C::P_BYTES;
+    const int nt = ntile[t];
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nt; ++j) {
+      ok = mbar_wait_warp(&s_full[t], j & 1, abort_flag, DERR_WAIT_MMA);
+      if (!ok) break;
+      tc_fence_after();
+      float s[C::BN];
+#pragma unroll
+      for (int c = 0; c < C::BN; c += 32) {
+        float tt[32];
+        tmem_ld32(trow + t * 128 + c, tt);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[c + i] = tt[i];
+      }
+      const int k0 = j * C::BN;
+      const bool need_mask = (k0 + C::BN - 1) > q_first;
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < C::BN; c += 2) {
+        float a = s[c] * p.scale_log2, bb = s[c + 1] * p.scale_log2;
+        if (need_mask) {
+          if (k0 + c > qpos) a = -INFINITY;
+          if (k0 + c + 1 > qpos) bb = -INFINITY;
+        }
+        s[c] = a;
+        s[c + 1] = bb;
+        mx0 = fmaxf(mx0, a);
+        mx1 = fmaxf(mx1, bb);
+      }
+      const float mx = fmaxf(mx0, mx1);
+      // lazy rescale: move the reference max only when this tile raises it by more than the threshold
+      const bool grow = mx > m_used + C::RESCALE_THRESHOLD;
+      const float m_new = grow ? mx : m_used;
+      const float alpha = grow ? fast_exp2(m_used - m_new) : 1.f;  // 0 on the first tile
+      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+      float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < C::BN; ++c) {
+        const float e = fast_exp2(s[c] - m_use);
+        s[c] = e;
+        s4[c & 3] += e;
+      }
+      l = l * alpha + ((s4[0] + s4[1]) + (s4[2] + s4[3]));
+      m_used = m_new;
+      if (j > 0) {
+        ok = mbar_wait_warp(&pv_done[t], (j - 1) & 1, abort_flag, DERR_WAIT_MMA);
+        if (!ok) break;
+        tc_fence_after();
+      }
+#pragma unroll
+      for (int ch = 0; ch < C::BN / 8; ++ch) {
+        const uint4 v = make_uint4(pack_half2(s[8 * ch + 0], s[8 * ch + 1]), pack_half2(s[8 * ch + 2], s[8 * ch + 3]),
+                                   pack_half2(s[8 * ch + 4], s[8 * ch + 5]), pack_half2(s[8 * ch + 6], s[8 * ch + 7]));
+        *reinterpret_cast<uint4*>(ps + (ch >> 3) * (128 * 128) + sw128_off(rl, ch & 7)) = v;
+      }
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll 1
+        for (int c = 0; c < HD; c += 32) {
+          float o[32];
+          tmem_ld32(trow + 256 + t * HD + c, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tmem_st32(trow + 256 + t * HD + c, o);
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full[t]);
+    }
+    if (ok && nt > 0) ok = mbar_wait_warp(&pv_done[t], (nt - 1) & 1, abort_flag, DERR_WAIT_MMA);
+    if (ok && nt > 0 && !*abort_flag) {
+      tc_fence_after();
+      const float inv_l = 1.f / l;
+      __half* orow = p.out + (static_cast<int64_t>(b) * p.out_seq_rows + row_in_seq) * p.ld_out + h * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD; c += 32) {
+        float o[32];
+        tmem_ld32(trow + 256 + t * HD + c, o);
+        if (row_in_seq < p.q_len) {
+          uint4* o4 = reinterpret_cast<uint4*>(orow + c);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            o4[i] = make_uint4(pack_half2(o[8 * i + 0] * inv_l, o[8 * i + 1] * inv_l),
+                               pack_half2(o[8 * i + 2] * inv_l, o[8 * i + 3] * inv_l),
+                               pack_half2(o[8 * i + 4] * inv_l, o[8 * i + 5] * inv_l),
+                               pack_half2(o[8 * i + 6] * inv_l, o[8 * i + 7] * inv_l));
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace b200

@@ -7,6 +7,7 @@
 
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <set>
@@ -17,6 +18,7 @@
 #include "ln.cuh"
 #include "gemm.cuh"
 #include "attn.cuh"
+#include "attn2.cuh"
 #include "fused_small.cuh"
 
 using namespace b200;
@@ -306,6 +308,47 @@ int launch_attn_t(const B200AttnArgs& a, cudaStream_t st) {
   return launch_status();
 }
 
+template <int HD>
+int launch_attn2_t(const B200AttnArgs& a, cudaStream_t st) {
+  using C = Attn2Cfg<HD>;
+  constexpr CUtensorMapSwizzle SW = HD == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  CUtensorMap tq, tk, tv;
+  if (int rc = make_map_f16(&tq, a.q, a.q_rows, a.ld_q, a.ld_q, HD, 128, SW)) return rc;
+  if (int rc = make_map_f16(&tk, a.k, a.kv_rows, a.ld_k, a.ld_k, HD, C::BN, SW)) return rc;
+  if (int rc = make_map_f16(&tv, a.v, a.kv_rows, a.ld_v, a.ld_v, HD, C::BN, SW)) return rc;
+  AttnParams p{};
+  p.H = a.heads;
+  p.q_len = a.q_len;
+  p.q_offset = a.q_offset;
+  p.kv_len = a.kv_len;
+  p.q_seq_rows = a.q_seq_rows;
+  p.kv_seq_rows = a.kv_seq_rows;
+  p.q_row0 = a.q_row0;
+  p.kv_row0 = a.kv_row0;
+  p.q_col0 = a.q_col0;
+  p.k_col0 = a.k_col0;
+  p.v_col0 = a.v_col0;
+  p.out = static_cast<__half*>(a.out) + static_cast<int64_t>(a.out_row0) * a.ld_out;
+  p.ld_out = a.ld_out;
+  p.out_seq_rows = a.out_seq_rows;
+  p.scale_log2 = static_cast<float>(1.4426950408889634 / __builtin_sqrt(static_cast<double>(HD)));
+  auto kern = k_flash_causal2<HD>;
+  const int smem = C::TOTAL;
+  if (int rc = set_smem(reinterpret_cast<const void*>(kern), smem)) return rc;
+  dim3 grid((a.q_len + 255) / 256, a.heads, a.batch);
+  kern<<<grid, 320, smem, st>>>(tq, tk, tv, p);
+  return launch_status();
+}
+
+// B200_ATTN_ONE_TILE=1 selects the one-query-tile kernel for every head_dim (A/B comparisons).
+bool attn_one_tile_forced() {
+  static const bool forced = [] {
+    const char* e = getenv("B200_ATTN_ONE_TILE");
+    return e != nullptr && e[0] == '1';
+  }();
+  return forced;
+}
+
 int attn_impl(const B200AttnArgs* a, cudaStream_t st) {
   if (!a || !a->q || !a->k || !a->v || !a->out) return B200_ERR_ARG;
   if (a->batch <= 0 || a->heads <= 0 || a->q_len < 0 || a->q_offset < 0 || a->kv_len <= 0) return B200_ERR_ARG;
@@ -326,6 +369,10 @@ int attn_impl(const B200AttnArgs* a, cudaStream_t st) {
     return B200_ERR_ARG;
   if (a->heads > 65535 || a->batch > 65535) return B200_ERR_TILE;
   if (int rc = check_arch()) return rc;
+  if (!attn_one_tile_forced()) {
+    if (hd == 32) return launch_attn2_t<32>(*a, st);
+    if (hd == 64) return launch_attn2_t<64>(*a, st);
+  }
   switch (hd) {
     case 32: return launch_attn_t<32, 128>(*a, st);
     case 64: return launch_attn_t<64, 128>(*a, st);
