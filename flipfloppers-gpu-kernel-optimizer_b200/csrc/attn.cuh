@@ -64,7 +64,7 @@ struct AttnCfg {
 };
 
 template <int HD, int BN>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(192, 2)  // two CTAs per SM (registers <= 170)
     k_flash_causal(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
   using C = AttnCfg<HD, BN>;
@@ -211,25 +211,28 @@ __global__ void __launch_bounds__(192, 1)
       }
       const int k0 = j * BN;
       const bool need_mask = (k0 + BN - 1) > q_first;
-      float mx = -INFINITY;
+      float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < BN; ++c) {
-        float t = s[c] * p.scale_log2;
-        if (need_mask && (k0 + c) > qpos) t = -INFINITY;
-        s[c] = t;
-        mx = fmaxf(mx, t);
+      for (int c = 0; c < BN; c += 2) {  // raw scores; the positive scale is applied in the exponent
+        if (need_mask && (k0 + c) > qpos) s[c] = -INFINITY;
+        if (need_mask && (k0 + c + 1) > qpos) s[c + 1] = -INFINITY;
+        mx0 = fmaxf(mx0, s[c]);
+        mx1 = fmaxf(mx1, s[c + 1]);
       }
-      const float m_new = fmaxf(m, mx);
+      const float m_new = fmaxf(m, fmaxf(mx0, mx1) * p.scale_log2);
       // rows with nothing visible yet keep p = 0 (cannot happen for real rows: key 0 is always visible)
       const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
       const float alpha = fast_exp2(m - m_use);  // m = -inf on the first tile -> 0
-      float sum = 0.f;
+      float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < BN; ++c) {
-        const float e = fast_exp2(s[c] - m_use);
+        float e;
+        if ((c & 3) == 3) e = exp2_poly(fmaf(s[c], p.scale_log2, -m_use));
+        else e = fast_exp2(fmaf(s[c], p.scale_log2, -m_use));
         s[c] = e;
-        sum += e;
+        s4[c & 3] += e;
       }
+      const float sum = (s4[0] + s4[1]) + (s4[2] + s4[3]);
       l = l * alpha + sum;
       m = m_new;
       if (j > 0) {

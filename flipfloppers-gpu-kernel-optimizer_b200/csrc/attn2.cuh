@@ -216,18 +216,15 @@ __global__ void __launch_bounds__(320, 1)
       const bool need_mask = (k0 + C::BN - 1) > q_first;
       float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < C::BN; c += 2) {
-        float a = s[c] * p.scale_log2, bb = s[c + 1] * p.scale_log2;
+      for (int c = 0; c < C::BN; c += 2) {  // raw scores; the positive scale is applied in the exponent
         if (need_mask) {
-          if (k0 + c > qpos) a = -INFINITY;
-          if (k0 + c + 1 > qpos) bb = -INFINITY;
+          if (k0 + c > qpos) s[c] = -INFINITY;
+          if (k0 + c + 1 > qpos) s[c + 1] = -INFINITY;
         }
-        s[c] = a;
-        s[c + 1] = bb;
-        mx0 = fmaxf(mx0, a);
-        mx1 = fmaxf(mx1, bb);
+        mx0 = fmaxf(mx0, s[c]);
+        mx1 = fmaxf(mx1, s[c + 1]);
       }
-      const float mx = fmaxf(mx0, mx1);
+      const float mx = fmaxf(mx0, mx1) * p.scale_log2;
       // lazy rescale: move the reference max only when this tile raises it by more than the threshold
       const bool grow = mx > m_used + C::RESCALE_THRESHOLD;
       const float m_new = grow ? mx : m_used;
@@ -236,7 +233,9 @@ __global__ void __launch_bounds__(320, 1)
       float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < C::BN; ++c) {
-        const float e = fast_exp2(s[c] - m_use);
+        float e;
+        if ((c & 3) == 3) e = exp2_poly(fmaf(s[c], p.scale_log2, -m_use));
+        else e = fast_exp2(fmaf(s[c], p.scale_log2, -m_use));
         s[c] = e;
         s4[c & 3] += e;
       }

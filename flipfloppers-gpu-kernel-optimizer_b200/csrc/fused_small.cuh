@@ -437,16 +437,17 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
         if (ok) tmem_ld32(trow + (h & 1) * 128 + c0, v);
         float mx = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float t = (c0 + i <= r) ? v[i] * p.scale_log2 : -INFINITY;
-          v[i] = t;
-          mx = fmaxf(mx, t);
+        for (int i = 0; i < 32; ++i) {  // raw scores; the positive scale is applied in the exponent
+          if (c0 + i > r) v[i] = -INFINITY;
+          mx = fmaxf(mx, v[i]);
         }
-        const float m = row_max(mx, st0);  // reductions alternate st0/st1 strictly
+        const float m = row_max(mx, st0) * p.scale_log2;  // reductions alternate st0/st1 strictly
         float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const float e = fast_exp2(v[i] - m);
+          float e;
+          if ((i & 3) == 3) e = exp2_poly(fmaf(v[i], p.scale_log2, -m));
+          else e = fast_exp2(fmaf(v[i], p.scale_log2, -m));
           v[i] = e;
           s4[i & 3] += e;
         }
