@@ -233,9 +233,7 @@ __global__ void __launch_bounds__(320, 1)
       float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < C::BN; ++c) {
-        float e;
-        if ((c & 3) == 3) e = exp2_poly(fmaf(s[c], p.scale_log2, -m_use));
-        else e = fast_exp2(fmaf(s[c], p.scale_log2, -m_use));
+        const float e = fast_exp2(fmaf(s[c], p.scale_log2, -m_use));
         s[c] = e;
         s4[c & 3] += e;
       }

@@ -445,9 +445,7 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
         float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          float e;
-          if ((i & 3) == 3) e = exp2_poly(fmaf(v[i], p.scale_log2, -m));
-          else e = fast_exp2(fmaf(v[i], p.scale_log2, -m));
+          const float e = fast_exp2(fmaf(v[i], p.scale_log2, -m));
           v[i] = e;
           s4[i & 3] += e;
         }

@@ -255,26 +255,6 @@ __device__ __forceinline__ float gelu_erf(float v) {
   return 0.5f * v * (1.0f + erff(v * 0.70710678118654752440f));
 }
 
-// 2^x without the MUFU unit, for part of the softmax exponentials so that the
-// FMA pipe shares the load with ex2: x = n + f with n = round(x) (magic-number
-// rounding: adding 1.5*2^23 leaves round(x) in the low mantissa bits), 2^f from
-// a degree-4 polynomial fitted in this project for minimal relative error on
-// [-0.5, 0.5] (max relative error 2.9e-6 evaluated in fp32; tests/test_gelu_cpu.py),
-// 2^n by adding n to the exponent field.  x is clamped to -120 (2^-120 stands
-// in for 0 after the fp16 cast of P).
-__device__ __forceinline__ float exp2_poly(float x) {
-  x = fmaxf(x, -120.f);
-  const float t = x + 12582912.f;
-  const float n = t - 12582912.f;
-  const float f = x - n;
-  float q = fmaf(9.582852944731712e-3f, f, 5.5906426161527634e-2f);
-  q = fmaf(q, f, 0.24024099111557007f);
-  q = fmaf(q, f, 0.6931241750717163f);
-  q = fmaf(q, f, 1.0f);
-  const int e = __float_as_int(t) - 0x4B400000;  // round(x)
-  return __int_as_float(__float_as_int(q) + (e << 23));
-}
-
 __device__ __forceinline__ float fast_rcp(float x) {
   float y;
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

@@ -140,6 +140,7 @@ def _attn_ref(q, k, v, q_offset):
 ATTN_CASES = [  # B, H, S, hd
     (2, 4, 128, 32), (3, 2, 100, 32), (2, 4, 384, 64), (1, 2, 300, 128), (2, 4, 128, 256), (1, 2, 200, 256),
     (2, 4, 1024, 32),
+    (1, 2, 2304, 64), (2, 2, 2100, 32),  # q_len >= 2048: two query tiles per CTA
 ]
 
 
@@ -157,11 +158,12 @@ def test_flash_causal_vs_torch(rt, B, H, S, hd):
     assert err < 4e-3, err
 
 
-@pytest.mark.parametrize("hd,chunk", [(64, 256), (32, 128), (64, 192), (256, 128)])
-def test_flash_prefix_chunks_equal_full(rt, hd, chunk):
+@pytest.mark.parametrize("hd,chunk,S", [(64, 256, 640), (32, 128, 640), (64, 192, 640), (256, 128, 640),
+                                        (64, 2048, 4352), (32, 2176, 4352)])
+def test_flash_prefix_chunks_equal_full(rt, hd, chunk, S):
     """Query chunks [c0:c1) over the K/V prefix [0:c1) (q_offset=c0) reproduce
     full causal attention row for row -- the chunked forward's identity."""
-    B, H, S = 2, 2, 640
+    B, H = 2, 2
     d = H * hd
     g = torch.Generator().manual_seed(hd + chunk)
     q = torch.randn(B * S, d, generator=g).to(torch.float16).to(DEV)
