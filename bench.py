@@ -42,12 +42,15 @@ sys.path.insert(0, REPO)
 
 METRIC = "block forward latency (ms) & tokens/s per shape at 1/2/4/8 B200; % of tensor/HBM roofline"
 CONFIGS = {
-    # name: (B per rank, S, d, H, ffn, L)
+    # name: (B, S, d, H, ffn, L) -- B per rank (weak scaling) except C5
     "C2": (64, 128, 128, 4, 512, 1),
     "C3": (10000, 128, 128, 4, 512, 1),
     "C4a": (64, 1024, 128, 4, 512, 1),
     "C4b": (64, 128, 1024, 4, 4096, 1),
+    "C5": (32, 100000, 1024, 16, 4096, 1),
 }
+# C5 keeps the global batch (B=32) fixed and splits it across the ranks (strong scaling)
+STRONG = {"C5"}
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 
 
@@ -62,17 +65,35 @@ def parse():
     return ap.parse_args()
 
 
+def rank_batch(cfg_name, rank, world):
+    B = CONFIGS[cfg_name][0]
+    if cfg_name in STRONG:
+        base, extra = divmod(B, world)
+        return base + (1 if rank < extra else 0)
+    return B
+
+
+def flushes(cfg_name):
+    """Flush L2 between steps unless one step's input alone is several times the 126 MB L2."""
+    B, S, d = CONFIGS[cfg_name][:3]
+    return B * S * d * 4 < (512 << 20)
+
+
 def workload_name(cfg_name):
     B, S, d, H, F, L = CONFIGS[cfg_name]
-    return f"{cfg_name}: causal pre-LN block B={B}/rank S={S} d={d} H={H} ffn={F} L={L}"
+    per = "" if cfg_name in STRONG else "/rank"
+    return f"{cfg_name}: causal pre-LN block B={B}{per} S={S} d={d} H={H} ffn={F} L={L}"
 
 
 def config_dict(cfg_name, n):
     B, S, d, H, F, L = CONFIGS[cfg_name]
-    return {"workload": workload_name(cfg_name), "batch_per_rank": B, "global_batch": B * n, "seq_len": S,
+    strong = cfg_name in STRONG
+    return {"workload": workload_name(cfg_name), "batch_per_rank": (B + n - 1) // n if strong else B,
+            "global_batch": B if strong else B * n, "seq_len": S,
             "d_model": d, "heads": H, "head_dim": d // H, "ffn_dim": F, "layers": L, "causal": True,
             "parallelism": f"batch-sharded x{n} (no data-path collective)" if n > 1 else "single GPU",
-            "l2": "flushed between timed steps (256 MiB write)", "seed": 1234}
+            "l2": ("flushed between timed steps (256 MiB write)" if flushes(cfg_name)
+                   else "inputs larger than L2 (no flush)"), "seed": 1234}
 
 
 def load_peaks():
@@ -158,10 +179,44 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- CPU baseline (oracle port)
+def cpu_sampled_rows_estimate(cfg_name):
+    """C5 cannot run on the CPU unchunked (its score tensor alone is ~20 TB): time the exact
+    sampled-row restatement (oracle.sampled_rows_forward) on one sequence and extrapolate a
+    full forward as B x (K/V-prefix projection + sum over rows of the per-row cost, which
+    grows linearly with the row's prefix length)."""
+    import numpy as np
+    import oracle
+    try:
+        from threadpoolctl import threadpool_info
+        cores = max([i.get("num_threads", 1) for i in threadpool_info()] or [os.cpu_count() or 1])
+    except Exception:  # noqa: BLE001
+        cores = os.cpu_count() or 1
+    B, S, d, H, F, L = CONFIGS[cfg_name]
+    T = 16384  # prefix sampled
+    params = oracle.params_from_state_dict(oracle.init_state_dict(1, d, F, 1234))
+    x = oracle.generate_chunked_input(1, S, d, seed=1234, rows=T)[0].numpy()
+    t0 = time.perf_counter()
+    oracle.sampled_rows_forward(params, H, x, [T - 1], key_block=8192)
+    t_one = time.perf_counter() - t0             # K/V prefix of T rows + one row at position T-1
+    t0 = time.perf_counter()
+    oracle.sampled_rows_forward(params, H, x, [T - 1 - i for i in range(8)], key_block=8192)
+    t_nine = time.perf_counter() - t0
+    per_row_at_T = max((t_nine - t_one) / 7, 1e-6)  # marginal cost of a row with a T-key prefix
+    kv = max(t_one - per_row_at_T, 1e-6) * S / T     # K/V projections scale with the prefix length
+    rows = per_row_at_T * (S / 2) / T * S          # per-row cost ~ linear in its prefix; mean prefix S/2
+    est = B * (kv + rows)
+    return {"value": B * S / est, "unit": "tokens/s", "cores": int(cores), "kind": "port",
+            "sample": f"ESTIMATE: oracle.sampled_rows_forward on one sequence prefix of {T} rows "
+                      f"(K/V prefix {t_one:.1f} s, marginal row {per_row_at_T * 1e3:.1f} ms at {T} keys), "
+                      f"extrapolated to B={B} x S={S}: {est / 60:.1f} min per forward"}, est, 1
+
+
 def cpu_forward_rate(cfg_name, budget_s=12.0, min_reps=1):
     """tokens/s of the NumPy restatement of the reference module on this host (all BLAS threads)."""
     import numpy as np
     import oracle
+    if cfg_name in STRONG:
+        return cpu_sampled_rows_estimate(cfg_name)
     try:
         from threadpoolctl import threadpool_info
         cores = max([i.get("num_threads", 1) for i in threadpool_info()] or [os.cpu_count() or 1])
@@ -194,6 +249,16 @@ def run_reference(args, rank, world):
     B, S, d, H, F, L = CONFIGS[args.config]
     import numpy as np
     import oracle
+    if args.config in STRONG:
+        base, est, _ = cpu_sampled_rows_estimate(args.config)
+        line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": "tokens/s",
+                "n_gpus": args.gpus, "steps": 1, "warmup": 0, "ms_per_step": est * 1e3, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded N(0,1) input, seeded default init)", "config": config_dict(args.config, 1),
+                "cpu_baseline": base,
+                "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return 0
     base, med, Bs = cpu_forward_rate(args.config, budget_s=0.0, min_reps=1)
     params = oracle.params_from_state_dict(oracle.init_state_dict(L, d, F, 1234))
     x, _ = oracle.generate_random_case(Bs, S, d, 1234 + 100000)
@@ -237,16 +302,23 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
-    B, S, d, H, F, L = CONFIGS[args.config]
+    _, S, d, H, F, L = CONFIGS[args.config]
+    B = rank_batch(args.config, rank, world)
     cfg = T.TransformerConfig(B, S, d, H, F, L, True)
     torch.manual_seed(1234)
     model = T.UserOptimizedTransformer(cfg).to(dev).eval()
-    gen = torch.Generator(device="cpu").manual_seed(1234 + 100000 + 7919 * rank)
-    x_host = torch.randn(B, S, d, generator=gen).pin_memory()
+    if B * S * d * 4 <= (1 << 30):
+        gen = torch.Generator(device="cpu").manual_seed(1234 + 100000 + 7919 * rank)
+        x_host = torch.randn(B, S, d, generator=gen).pin_memory()
+        x = x_host.to(dev)
+    else:  # multi-GB inputs: draw on the device, keep a pinned host copy for the end-to-end leg
+        gen = torch.Generator(device=dev).manual_seed(1234 + 100000 + 7919 * rank)
+        x = torch.randn(B, S, d, generator=gen, device=dev)
+        x_host = torch.empty(B, S, d).pin_memory()
+        x_host.copy_(x)
     y_host = torch.empty(B, S, d).pin_memory()
-    x = x_host.to(dev)
     mask = torch.ones(B, S, dtype=torch.bool, device=dev)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush = torch.empty((256 << 20) if flushes(args.config) else 16, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream()
     tokens_rank = B * S
 
@@ -301,7 +373,7 @@ def main():
         # ---- end to end, pipelined (UserOptimizedTransformer.forward_host): every step still
         # uploads its x and downloads its y, but step i's download, step i+1's forward and
         # step i+2's upload overlap; L2 flushed before every forward
-        y_hosts = [torch.empty(B, S, d).pin_memory() for _ in range(2)]
+        y_hosts = [y_host, torch.empty(B, S, d).pin_memory()]
         for i in range(4):
             model.forward_host(x_host, out=y_hosts[i % 2], wait=False, flush=flush)
         model.synchronize_host()
@@ -317,23 +389,26 @@ def main():
         torch.cuda.synchronize()
         barrier()
         e2e_ms = max_over_ranks(t0.elapsed_time(t1))
-        ok_e2e = torch.allclose(y_hosts[0], y_host) and torch.allclose(y_hosts[1], y_host)
+        ok_e2e = bool(torch.equal(y_hosts[0], y_hosts[1]))
     clocks = clk.stop()
 
-    value = world * tokens_rank * args.steps / (ms_total / 1e3)
-    e2e_value = world * tokens_rank * args.steps / (e2e_ms / 1e3)
+    tokens_all = (CONFIGS[args.config][0] * S) if args.config in STRONG else world * tokens_rank
+    value = tokens_all * args.steps / (ms_total / 1e3)
+    e2e_value = tokens_all * args.steps / (e2e_ms / 1e3)
     launches_per_step = kernels_per_forward(model)
 
     roof = None
     cpu = None
     if rank == 0:
-        roof = roofline_pass(model, x, mask, flush, cfg, steps=max(20, min(args.steps, 200)))
+        roof = roofline_pass(model, x, mask, flush if flushes(args.config) else None, cfg,
+                             steps=max(3, min(args.steps, 200)) if args.config in STRONG else max(20, min(args.steps, 200)))
         if world == 1 and not args.no_cpu_baseline:
             cpu = cpu_forward_rate(args.config)[0]
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_total / args.steps, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "f16 operands / f32 accumulate, f32 in-out",
+                "scaling": "strong" if args.config in STRONG else "weak", "vs_baseline": None,
+                "dtype": "f16 operands / f32 accumulate, f32 in-out",
                 "data": "synthetic (seeded N(0,1) input, seeded default init)",
                 "config": dict(config_dict(args.config, world), strategy=model.last_strategy),
                 "e2e": {"value": e2e_value, "unit": "tokens/s", "ms_per_step": e2e_ms / args.steps,
@@ -341,7 +416,7 @@ def main():
                         "api": "UserOptimizedTransformer.forward_host (pinned host in/out, upload/forward/"
                                "download overlapped across steps, L2 flushed before each forward)",
                         "outputs_match_device_path": bool(ok_e2e),
-                        "serial": {"value": world * tokens_rank * args.steps / (e2e_serial_ms / 1e3),
+                        "serial": {"value": tokens_all * args.steps / (e2e_serial_ms / 1e3),
                                    "ms_per_step": e2e_serial_ms / args.steps,
                                    "api": "UserOptimizedTransformer.__call__ with H2D/D2H on one stream"}},
                 "roofline": roof, "cpu_baseline": cpu, "clocks": clocks,
