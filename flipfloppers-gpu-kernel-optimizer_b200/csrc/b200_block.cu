@@ -428,6 +428,7 @@ int fused_small_impl(const B200FusedSmallArgs* a, cudaStream_t st) {
   p.lnf_b = a->lnf_b;
   p.eps = a->eps;
   p.scale_log2 = static_cast<float>(1.4426950408889634 / __builtin_sqrt(32.0));
+  p.row_valid = static_cast<const unsigned char*>(a->row_valid);
   const int smem = SmallCfg::TOTAL;
   if (int rc = set_smem(reinterpret_cast<const void*>(k_block_small), smem)) return rc;
   if (int rc = check_block_fits(reinterpret_cast<const void*>(k_block_small), SmallCfg::THREADS)) return rc;
@@ -687,6 +688,15 @@ int b200_add_layernorm_launch(const float* a, const float* b, const float* bias,
                               const float* beta, void* out, int out_f16, int rows, int d, float eps,
                               b200_stream_t stream) {
   return add_ln_impl(a, b, bias, sum_out, gamma, beta, out, out_f16, rows, d, eps, static_cast<cudaStream_t>(stream));
+}
+
+int b200_zero_masked_rows(float* y, const unsigned char* row_valid, long long rows, int d, b200_stream_t stream) {
+  if (!y || !row_valid || rows < 0 || d <= 0) return B200_ERR_ARG;
+  if (rows == 0) return B200_OK;
+  if (int rc = check_arch()) return rc;
+  k_zero_masked_rows<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      y, row_valid, rows, d);
+  return launch_status();
 }
 
 int b200_gemm_launch(int epilogue, const void* A, long long lda, const void* W, long long ldw, const float* bias,

@@ -56,6 +56,7 @@ struct SmallParams {
   const float* lnf_w; const float* lnf_b;   // [128]
   float eps;
   float scale_log2;   // 32^-0.5 * log2(e)
+  const unsigned char* row_valid;  // [num_seq*seq_len] key-padding mask (0 = padded row), may be null
 };
 
 struct SmallCfg {
@@ -531,9 +532,14 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
       }
       if (l == p.layers - 1) layer_norm(vec + C::V_LNFW, vec + C::V_LNFB);
       if (row_ok && ok) {
+        // padded rows of the model output are zero (with causal attention and prefix-valid
+        // padding the valid rows never see a padded key, so only the output needs masking)
+        const bool zero = l == p.layers - 1 && p.row_valid != nullptr && p.row_valid[grow] == 0;
         float* yo = p.y + grow * C::D + c0;
 #pragma unroll
-        for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(yo + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+        for (int i = 0; i < 32; i += 4)
+          *reinterpret_cast<float4*>(yo + i) =
+              zero ? make_float4(0.f, 0.f, 0.f, 0.f) : make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
       }
       // the next step's LN1 (which reuses the statistics buffers) must not race
       // this step's final row reduction

@@ -130,4 +130,15 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// y[r, :] = 0 for every row whose valid flag is 0 (the reference zeroes padded
+// query rows of the model output, TTB:190-191).  One warp per row.
+__global__ void __launch_bounds__(256)
+    k_zero_masked_rows(float* __restrict__ y, const unsigned char* __restrict__ valid, long long rows, int d) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long row = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + warp;
+  if (row >= rows || valid[row]) return;
+  float* yr = y + row * d;
+  for (int c = lane; c < d; c += 32) yr[c] = 0.f;
+}
+
 }  // namespace b200

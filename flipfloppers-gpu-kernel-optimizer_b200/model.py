@@ -194,14 +194,43 @@ class UserOptimizedTransformer(nn.Module):
     # ------------------------------------------------------------------ arbiter
     def _mask_is_all_ones(self, m: Optional[torch.Tensor]) -> bool:
         """Cached ``mask.all()``, keyed by (data_ptr, shape) as in TTB:1011-1025."""
+        return self._padding_rows(m, None) is None
+
+    def _padding_rows(self, m: Optional[torch.Tensor], device) -> Optional[torch.Tensor]:
+        """Per-row valid flags (uint8 [B*S] on ``device``) of a key-padding mask, or None if
+        there is no padding.  A property of the mask, cached by (data_ptr, shape) like the
+        reference's ``_mask_is_all_ones`` (TTB:1011-1025).
+
+        The reference masks padded keys in attention and zeroes padded rows after each
+        block and after the final norm (TTB:125-128, 140-141, 163-164, 190-191).  With
+        causal attention and a prefix-valid mask (``True`` then ``False`` along each
+        sequence, what ``generate_random_case`` produces, TTB:1793-1803) a valid query
+        only ever attends valid keys, so valid rows equal the unmasked computation and
+        the output's padded rows are zero: the kernels implement exactly that.  Masks
+        with interior holes would change valid rows and are rejected."""
         if m is None:
-            return True
-        key = (m.data_ptr(), tuple(m.shape))
+            return None
+        key = (m.data_ptr(), tuple(m.shape), str(m.device))
         hit = self._mask_cache.get(key)
         if hit is None:
-            hit = bool(m.all())
+            mb = m.to(torch.bool)
+            if bool(mb.all()):
+                hit = ("ones", None)
+            else:
+                if mb.dim() != 2:
+                    raise ValueError("valid_token_mask must be [batch, seq_len]")
+                mi = mb.to(torch.int8)
+                if mi.shape[1] > 1 and bool((mi[:, 1:] > mi[:, :-1]).any()):
+                    raise NotImplementedError(
+                        "valid_token_mask must be prefix-valid per sequence (valid tokens first, padding last); "
+                        "masks with interior holes are not supported")
+                hit = ("pad", mb.to(torch.uint8).contiguous().reshape(-1))
             self._mask_cache[key] = hit
-        return hit
+        rows = hit[1]
+        if rows is not None and device is not None and rows.device != device:
+            rows = rows.to(device)
+            self._mask_cache[key] = ("pad", rows)
+        return rows
 
     def _fused_small_eligible(self) -> bool:
         c = self.config
@@ -286,37 +315,40 @@ class UserOptimizedTransformer(nn.Module):
                                "there is no CPU fallback")
         if x.dim() != 3 or x.shape[-1] != cfg.d_model:
             raise ValueError(f"expected x of shape [B, S, {cfg.d_model}], got {tuple(x.shape)}")
-        if not self._mask_is_all_ones(valid_token_mask):
-            raise NotImplementedError("key-padding masks (valid_token_mask with False entries) are not supported yet")
         B, S, d = x.shape
+        if valid_token_mask is not None and tuple(valid_token_mask.shape) != (B, S):
+            raise ValueError(f"valid_token_mask must be [{B}, {S}], got {tuple(valid_token_mask.shape)}")
+        rows_valid = self._padding_rows(valid_token_mask, x.device)
         out_dtype = x.dtype
         xin = x if (x.dtype == torch.float32 and x.is_contiguous()) else x.to(torch.float32).contiguous()
         dev = xin.device
         with torch.cuda.device(dev):
             y = torch.empty_like(xin)
-            self._forward_into(xin, y)
+            self._forward_into(xin, y, rows_valid)
         return y if out_dtype == torch.float32 else y.to(out_dtype)
 
-    def _run_graphed(self, x: torch.Tensor, y: torch.Tensor, ws: torch.Tensor, strat: str) -> None:
+    def _run_graphed(self, x: torch.Tensor, y: torch.Tensor, ws: torch.Tensor, strat: str,
+                     rows_valid: Optional[torch.Tensor] = None) -> None:
         """Replay (or capture) the forward as one CUDA graph keyed by shape and pointers.
 
-        The graph reads x and writes y at the addresses it was captured with;
-        keying on both pointers keeps that correct for any caller, and the
-        caching allocator hands the same output block back to a loop that drops
-        its previous result, so steady-state calls replay without copies."""
-        key = (tuple(x.shape), x.data_ptr(), y.data_ptr(), ws.data_ptr(), strat)
+        The graph reads x (and the padding flags) and writes y at the addresses it was
+        captured with; keying on every pointer keeps that correct for any caller, and
+        the caching allocator hands the same output block back to a loop that drops its
+        previous result, so steady-state calls replay without copies."""
+        rv = 0 if rows_valid is None else rows_valid.data_ptr()
+        key = (tuple(x.shape), x.data_ptr(), y.data_ptr(), ws.data_ptr(), strat, rv)
         g = self._graphs.get(key)
         if g is None:
             shape_key = (tuple(x.shape), strat)
             if shape_key not in self._warm:
                 # first call at this shape: launch eagerly (sets kernel attributes, validates arguments)
-                self._launch(x, y, ws, strat)
+                self._launch(x, y, ws, strat, rows_valid)
                 torch.cuda.current_stream().synchronize()
                 self._warm.add(shape_key)
                 return
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
-                self._launch(x, y, ws, strat)
+                self._launch(x, y, ws, strat, rows_valid)
             self._graphs[key] = g
             while len(self._graphs) > _GRAPH_CACHE:
                 self._graphs.popitem(last=False)
@@ -324,16 +356,21 @@ class UserOptimizedTransformer(nn.Module):
             self._graphs.move_to_end(key)
         g.replay()
 
-    def _launch(self, x: torch.Tensor, y: torch.Tensor, ws: torch.Tensor, strat: str) -> None:
+    def _launch(self, x: torch.Tensor, y: torch.Tensor, ws: torch.Tensor, strat: str,
+                rows_valid: Optional[torch.Tensor] = None) -> None:
         if strat == "fused_small":
-            self._forward_fused_small(x, y)
-        elif strat == "chunked":
+            self._forward_fused_small(x, y, rows_valid)
+            return
+        if strat == "chunked":
             B, S, _ = x.shape
             self._forward_chain(x, y, ws, chunk_rows=self._chunk_plan[(B, S, x.device.index)])
         else:
             self._forward_chain(x, y, ws)
+        if rows_valid is not None:
+            rt.zero_masked_rows(y, rows_valid)
 
-    def _forward_fused_small(self, x: torch.Tensor, y: torch.Tensor) -> None:
+    def _forward_fused_small(self, x: torch.Tensor, y: torch.Tensor,
+                             rows_valid: Optional[torch.Tensor] = None) -> None:
         cfg = self.config
         B, S, d = x.shape
         st = self._stack
@@ -346,6 +383,7 @@ class UserOptimizedTransformer(nn.Module):
             setattr(a, name, st[name].data_ptr())
         a.lnf_w, a.lnf_b = self._lnf[0].data_ptr(), self._lnf[1].data_ptr()
         a.eps = float(self.layers[0].norm1.eps)
+        a.row_valid = None if rows_valid is None else rows_valid.data_ptr()
         rt.fused_small(a)
 
     def _forward_chain(self, x: torch.Tensor, y: torch.Tensor, ws: torch.Tensor,
@@ -455,8 +493,9 @@ class UserOptimizedTransformer(nn.Module):
             pipes[key] = pipe
         return pipe
 
-    def _forward_into(self, xin: torch.Tensor, y: torch.Tensor) -> None:
-        """Forward of a contiguous fp32 CUDA tensor into a preallocated ``y`` (current stream)."""
+    def _forward_into(self, xin: torch.Tensor, y: torch.Tensor, rows_valid: Optional[torch.Tensor] = None) -> None:
+        """Forward of a contiguous fp32 CUDA tensor into a preallocated ``y`` (current stream);
+        ``rows_valid`` (uint8 [B*S], optional) zeroes padded output rows."""
         B, S, d = xin.shape
         dev = xin.device
         self._ensure_packs(dev)
@@ -470,9 +509,9 @@ class UserOptimizedTransformer(nn.Module):
         else:
             ws = self._workspace(256, dev)
         if _GRAPHS_ON and xin.numel() <= _GRAPH_MAX_ELEMS:
-            self._run_graphed(xin, y, ws, strat)
+            self._run_graphed(xin, y, ws, strat, rows_valid)
         else:
-            self._launch(xin, y, ws, strat)
+            self._launch(xin, y, ws, strat, rows_valid)
 
     # ------------------------------------------------------------------ profiling helper
     @torch.no_grad()

@@ -90,6 +90,7 @@ class FusedSmallArgs(ctypes.Structure):
         ("w_out", _vp), ("b_out", _vp),
         ("lnf_w", _vp), ("lnf_b", _vp),
         ("eps", ctypes.c_float),
+        ("row_valid", _vp),
     ]
 
 
@@ -103,6 +104,7 @@ EXPORTS = [
      [_vp, _c_ll, _vp, _vp, _vp, _c_ll, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, _vp]),
     ("b200_add_layernorm_launch", ctypes.c_int,
      [_vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, _vp]),
+    ("b200_zero_masked_rows", ctypes.c_int, [_vp, _vp, _c_ll, ctypes.c_int, _vp]),
     ("b200_gemm_launch", ctypes.c_int,
      [ctypes.c_int, _vp, _c_ll, _vp, _c_ll, _vp, _vp, _c_ll, _vp, _c_ll, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
     ("b200_flash_causal_launch", ctypes.c_int, [ctypes.POINTER(AttnArgs), _vp]),
@@ -193,6 +195,15 @@ def add_layernorm(a: torch.Tensor, b: torch.Tensor, bias: Optional[torch.Tensor]
                                          int(out.dtype == torch.float16), rows, d, float(eps), _stream(stream))
     check(rc, "b200_add_layernorm_launch")
     return out
+
+
+def zero_masked_rows(y: torch.Tensor, row_valid: torch.Tensor, stream=None) -> torch.Tensor:
+    """Zero the rows of y (fp32 [..., d]) whose flag in row_valid (bool/uint8, one per row) is 0."""
+    _require_cuda(y, row_valid)
+    d = y.shape[-1]
+    rc = lib().b200_zero_masked_rows(_p(y), _p(row_valid), y.numel() // d, d, _stream(stream))
+    check(rc, "b200_zero_masked_rows")
+    return y
 
 
 def gemm(epilogue: int, a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor], out: torch.Tensor,

@@ -94,6 +94,13 @@ int b200_add_layernorm_launch(const float* a, const float* b, const float* bias,
                               const float* beta, void* out, int out_f16, int rows, int d, float eps,
                               b200_stream_t stream);
 
+/* y[r, :] = 0 for every row r with row_valid[r] == 0: the reference zeroes
+ * padded query rows of the model output (torch_transformer_benchmark.py:190-191).
+ * With causal attention and a prefix-valid padding mask, valid rows never
+ * attend a padded key, so masking the output is the whole of the padding
+ * semantics.  y fp32 [rows, d], row_valid uint8 [rows]. */
+int b200_zero_masked_rows(float* y, const unsigned char* row_valid, long long rows, int d, b200_stream_t stream);
+
 /* out[M,N] = epilogue(A[M,K] . W[N,K]^T + bias[N]).  A, W fp16 row-major with
  * leading dimensions lda, ldw (elements); bias fp32 (may be null); resid fp32
  * [M, ld_resid] for B200_EPI_BIAS_RESID_F32 (may equal out).  Requires
@@ -198,6 +205,8 @@ typedef struct {
   const float* lnf_w;
   const float* lnf_b;
   float eps;
+  const void* row_valid;   /* [batch*seq_len] uint8 key-padding mask (0 = padded row; prefix-valid per
+                              sequence); padded rows of y are written as 0.  NULL = no padding. */
 } B200FusedSmallArgs;
 
 int b200_block_fused_small_launch(const B200FusedSmallArgs* args, b200_stream_t stream);

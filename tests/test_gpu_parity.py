@@ -47,13 +47,13 @@ def _clean_device_errors(pkg):
     assert rt.device_error(clear=True) == 0
 
 
-@pytest.mark.parametrize("case", [c for c in golden_cases() if c["padding_ratio"] == 0],
-                         ids=lambda c: c["name"])
+@pytest.mark.parametrize("case", golden_cases(), ids=lambda c: c["name"])
 def test_golden_cases(tt, case):
     g = load_golden(case["name"])
-    x, _ = oracle.generate_random_case(case["B"], case["S"], case["d"], case["x_seed"])
+    x, mask = oracle.generate_random_case(case["B"], case["S"], case["d"], case["x_seed"], case["padding_ratio"])
     model, _ = _model(tt, case["B"], case["S"], case["d"], case["H"], case["ffn"], case["L"], case["seed"])
-    y = _run(model, x)
+    with torch.inference_mode():
+        y = model(x.to(DEV), mask.to(DEV)).cpu()
     res = oracle.compare_outputs(g["y"], y, rtol=RTOL, atol=ATOL)
     print(f"{case['name']}: max_abs={res.max_abs_error:.3g} failed={res.failed_elements}")
     assert res.passed, res
@@ -175,3 +175,29 @@ def test_forward_host_pipeline_matches_device_path(tt, d, H, F):
         for x, o in zip(xs, outs):
             ref = model(x.to(DEV)).cpu()
             assert torch.equal(o, ref)
+
+
+@pytest.mark.parametrize("B,S,d,H,F,L", [(8, 128, 128, 4, 512, 1), (6, 96, 128, 4, 256, 2), (5, 200, 256, 4, 1024, 1)])
+def test_padding_masks_against_oracle(tt, B, S, d, H, F, L):
+    """Prefix-valid key-padding masks (generate_random_case with padding_ratio > 0):
+    valid rows match the reference's masked forward, padded rows are exactly 0 --
+    on the fused small-model kernel (d=128) and on the chain."""
+    model, _ = _model(tt, B, S, d, H, F, L, seed=31)
+    x, mask = oracle.generate_random_case(B, S, d, 32, padding_ratio=0.5)
+    assert not bool(mask.all())
+    with torch.inference_mode():
+        y = model(x.to(DEV), mask.to(DEV)).cpu()
+    ref = oracle.model_forward(oracle.params_from_state_dict(model.state_dict()),
+                               oracle.OracleConfig(B, S, d, H, F, L, True), x.numpy(), mask.numpy())
+    res = oracle.compare_outputs(ref, y, rtol=RTOL, atol=ATOL)
+    assert res.passed, res
+    assert torch.all(y[~mask] == 0)
+
+
+def test_mask_with_holes_is_rejected(tt):
+    model, _ = _model(tt, 2, 64, 128, 4, 512, 1)
+    x, _ = oracle.generate_random_case(2, 64, 128, 1)
+    mask = torch.ones(2, 64, dtype=torch.bool)
+    mask[0, 10] = False
+    with pytest.raises(NotImplementedError, match="prefix-valid"):
+        model(x.to(DEV), mask.to(DEV))

@@ -53,3 +53,19 @@ def test_batch_independence_of_oracle():
     y = oracle.model_forward(sd, cfg, x.numpy())
     y2 = oracle.model_forward(sd, oracle.OracleConfig(2, 40, 64, 2, 256, 1, True), x[1:3].numpy())
     assert np.abs(y[1:3] - y2).max() < 1e-6
+
+
+@pytest.mark.parametrize("L", [1, 2])
+def test_prefix_padding_only_zeroes_padded_rows(L):
+    """The padding design argument, on the oracle: with causal attention and a
+    prefix-valid mask, the reference's masked forward equals the unmasked forward
+    on valid rows and is 0 on padded rows (so the kernels only mask the output)."""
+    B, S, d, H, F = 4, 48, 64, 2, 256
+    sd = oracle.params_from_state_dict(oracle.init_state_dict(L, d, F, 8))
+    x, mask = oracle.generate_random_case(B, S, d, 9, padding_ratio=0.6)
+    cfg = oracle.OracleConfig(B, S, d, H, F, L, True)
+    masked = oracle.model_forward(sd, cfg, x.numpy(), mask.numpy())
+    plain = oracle.model_forward(sd, cfg, x.numpy())
+    m = mask.numpy()
+    assert np.abs(masked[m] - plain[m]).max() < 1e-5
+    assert np.all(masked[~m] == 0)
