@@ -39,7 +39,15 @@ struct AttnParams {
   int64_t ld_out;
   int out_seq_rows;      // rows between consecutive sequences in out
   float scale_log2;      // head_dim^-0.5 * log2(e)
+  int non_causal;        // 1: every query sees every valid key (the reference without --causal)
+  const int* kv_lens;    // per-sequence count of valid keys (key-padding mask), may be null
 };
+
+// Keys [0, kv_eff) of sequence b are valid (at least one, so a row is never empty).
+__device__ __forceinline__ int attn_kv_eff(const AttnParams& p, int b) {
+  const int l = p.kv_lens ? min(p.kv_len, p.kv_lens[b]) : p.kv_len;
+  return l > 0 ? l : 1;
+}
 
 template <int HD, int BN>
 struct AttnCfg {
@@ -87,7 +95,8 @@ __global__ void __launch_bounds__(192, 2)  // two CTAs per SM (registers <= 170)
   const int h = blockIdx.y, b = blockIdx.z;
   const int q_first = p.q_offset + qt * 128;
   const int q_last = p.q_offset + min(p.q_len, (qt + 1) * 128) - 1;
-  const int nkt = min(q_last / BN + 1, (p.kv_len + BN - 1) / BN);
+  const int kv_eff = attn_kv_eff(p, b);
+  const int nkt = p.non_causal ? (kv_eff + BN - 1) / BN : min(q_last / BN + 1, (kv_eff + BN - 1) / BN);
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -210,12 +219,13 @@ __global__ void __launch_bounds__(192, 2)  // two CTAs per SM (registers <= 170)
         for (int i = 0; i < 32; ++i) s[c + i] = t[i];
       }
       const int k0 = j * BN;
-      const bool need_mask = (k0 + BN - 1) > q_first;
+      const int klim = p.non_causal ? kv_eff - 1 : min(qpos, kv_eff - 1);  // last visible key of this row
+      const bool need_mask = (k0 + BN - 1) > (p.non_causal ? kv_eff - 1 : min(q_first, kv_eff - 1));
       float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
       for (int c = 0; c < BN; c += 2) {  // raw scores; the positive scale is applied in the exponent
-        if (need_mask && (k0 + c) > qpos) s[c] = -INFINITY;
-        if (need_mask && (k0 + c + 1) > qpos) s[c + 1] = -INFINITY;
+        if (need_mask && (k0 + c) > klim) s[c] = -INFINITY;
+        if (need_mask && (k0 + c + 1) > klim) s[c + 1] = -INFINITY;
         mx0 = fmaxf(mx0, s[c]);
         mx1 = fmaxf(mx1, s[c + 1]);
       }

@@ -64,7 +64,8 @@ __global__ void __launch_bounds__(320, 1)
   const int npair = (p.q_len + 255) / 256;
   const int qp = npair - 1 - static_cast<int>(blockIdx.x);  // latest query rows first
   const int h = blockIdx.y, b = blockIdx.z;
-  const int kv_tiles = (p.kv_len + C::BN - 1) / C::BN;
+  const int kv_eff = attn_kv_eff(p, b);
+  const int kv_tiles = (kv_eff + C::BN - 1) / C::BN;
   // key tiles each query tile needs (0 if the tile holds no query row)
   int ntile[2];
 #pragma unroll
@@ -74,7 +75,7 @@ __global__ void __launch_bounds__(320, 1)
       ntile[t] = 0;
     } else {
       const int q_last = p.q_offset + min(p.q_len, r0 + 128) - 1;
-      ntile[t] = min(q_last / C::BN + 1, kv_tiles);
+      ntile[t] = p.non_causal ? kv_tiles : min(q_last / C::BN + 1, kv_tiles);
     }
   }
   const int n_all = max(ntile[0], ntile[1]);
@@ -213,13 +214,14 @@ __global__ void __launch_bounds__(320, 1)
         for (int i = 0; i < 32; ++i) s[c + i] = tt[i];
       }
       const int k0 = j * C::BN;
-      const bool need_mask = (k0 + C::BN - 1) > q_first;
+      const int klim = p.non_causal ? kv_eff - 1 : min(qpos, kv_eff - 1);  // last visible key of this row
+      const bool need_mask = (k0 + C::BN - 1) > (p.non_causal ? kv_eff - 1 : min(q_first, kv_eff - 1));
       float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
       for (int c = 0; c < C::BN; c += 2) {  // raw scores; the positive scale is applied in the exponent
         if (need_mask) {
-          if (k0 + c > qpos) s[c] = -INFINITY;
-          if (k0 + c + 1 > qpos) s[c + 1] = -INFINITY;
+          if (k0 + c > klim) s[c] = -INFINITY;
+          if (k0 + c + 1 > klim) s[c + 1] = -INFINITY;
         }
         mx0 = fmaxf(mx0, s[c]);
         mx1 = fmaxf(mx1, s[c + 1]);

@@ -297,6 +297,8 @@ int launch_attn_t(const B200AttnArgs& a, cudaStream_t st) {
   p.ld_out = a.ld_out;
   p.out_seq_rows = a.out_seq_rows;
   p.scale_log2 = static_cast<float>(1.4426950408889634 / __builtin_sqrt(static_cast<double>(HD)));
+  p.non_causal = a.non_causal;
+  p.kv_lens = a.kv_lens;
   // TMEM: at most two 256-column CTAs per SM, so request enough shared memory
   // that a third cannot be co-resident and block in tcgen05.alloc.
   int smem = C::TOTAL;
@@ -332,6 +334,8 @@ int launch_attn2_t(const B200AttnArgs& a, cudaStream_t st) {
   p.ld_out = a.ld_out;
   p.out_seq_rows = a.out_seq_rows;
   p.scale_log2 = static_cast<float>(1.4426950408889634 / __builtin_sqrt(static_cast<double>(HD)));
+  p.non_causal = a.non_causal;
+  p.kv_lens = a.kv_lens;
   auto kern = k_flash_causal2<HD>;
   const int smem = C::TOTAL;
   if (int rc = set_smem(reinterpret_cast<const void*>(kern), smem)) return rc;
@@ -429,6 +433,7 @@ int fused_small_impl(const B200FusedSmallArgs* a, cudaStream_t st) {
   p.eps = a->eps;
   p.scale_log2 = static_cast<float>(1.4426950408889634 / __builtin_sqrt(32.0));
   p.row_valid = static_cast<const unsigned char*>(a->row_valid);
+  p.non_causal = a->non_causal;
   const int smem = SmallCfg::TOTAL;
   if (int rc = set_smem(reinterpret_cast<const void*>(k_block_small), smem)) return rc;
   if (int rc = check_block_fits(reinterpret_cast<const void*>(k_block_small), SmallCfg::THREADS)) return rc;
@@ -507,6 +512,8 @@ int block_impl(const B200BlockArgs* a, cudaStream_t st) {
   at.ld_out = d;
   at.out_seq_rows = a->seq_len;
   at.out_row0 = 0;
+  at.non_causal = a->non_causal;
+  at.kv_lens = a->kv_lens;
   if ((rc = attn_impl(&at, st))) return rc;
   // 4. x1 = x + ctx . Wo^T + bo
   if ((rc = gemm_impl(EPI_BIAS_RESID_F32, w.ctx, d, a->w_o, d, a->b_o, a->x, d, w.x1, d, static_cast<int>(M), d, d,
@@ -574,6 +581,7 @@ int block_chunked_impl(const B200BlockArgs* a, int chunk_rows, cudaStream_t st) 
   if (a->batch <= 0 || a->seq_len <= 0 || a->d_model <= 0 || a->num_heads <= 0 || a->ffn_dim <= 0 || chunk_rows <= 0)
     return B200_ERR_ARG;
   if (a->d_model % a->num_heads || a->x == a->y) return B200_ERR_ARG;
+  if (a->non_causal) return B200_ERR_CONFIG;  // prefix chunking is a causal construction
   const long long M = static_cast<long long>(a->batch) * a->seq_len;
   const int d = a->d_model, F = a->ffn_dim, H = a->num_heads, hd = d / H, S = a->seq_len;
   if (hd != 32 && hd != 64 && hd != 128 && hd != 256) return B200_ERR_HEAD_DIM;

@@ -57,6 +57,7 @@ struct SmallParams {
   float eps;
   float scale_log2;   // 32^-0.5 * log2(e)
   const unsigned char* row_valid;  // [num_seq*seq_len] key-padding mask (0 = padded row), may be null
+  int non_causal;                  // 1: every query sees every valid key
 };
 
 struct SmallCfg {
@@ -430,7 +431,17 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
         store_sw64(smem + (nt == 0 ? C::OFF_Q : nt == 1 ? C::OFF_K : C::OFF_V) + g * 8192);
       }
       publish(SB_QKV_SMEM);
-      // ---- W3: causal softmax per head (this thread: row r, keys c0..c0+31)
+      // ---- W3: softmax per head (this thread: row r, keys c0..c0+31)
+      // bit i: key c0+i exists and is not padding (the causal bound is applied per row below)
+      uint32_t kvalid = 0;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int k = c0 + i;
+        const bool v_ok = k < p.seq_len &&
+                          (p.row_valid == nullptr || p.row_valid[static_cast<int64_t>(seq) * p.seq_len + k] != 0);
+        kvalid |= (v_ok ? 1u : 0u) << i;
+      }
+      if (!p.non_causal) kvalid &= (r >= c0 + 31) ? 0xffffffffu : (r < c0 ? 0u : (0xffffffffu >> (31 - (r - c0))));
       float my_l = 1.f;  // softmax denominator of head g (this thread's head in the context step)
 #pragma unroll 1
       for (int h = 0; h < 4; ++h) {
@@ -439,7 +450,7 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
         float mx = -INFINITY;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {  // raw scores; the positive scale is applied in the exponent
-          if (c0 + i > r) v[i] = -INFINITY;
+          if (!((kvalid >> i) & 1u)) v[i] = -INFINITY;
           mx = fmaxf(mx, v[i]);
         }
         const float m = row_max(mx, st0) * p.scale_log2;  // reductions alternate st0/st1 strictly

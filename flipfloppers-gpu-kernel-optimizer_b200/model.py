@@ -14,6 +14,9 @@ Surface and behaviour follow the reference's drop-in class
 * derived device weights (fused fp16 QKV, fp16 projections, fp32 biases) are
   plain attributes rebuilt when a parameter changes, never Parameters or
   buffers (TTB:624-630, 706-796);
+* causal and non-causal forwards (``config.causal``; the reference harness runs
+  non-causal without ``--causal``, TTB:115-123), with prefix-valid key-padding
+  masks (TTB:125-128, 1793-1803);
 * a per-shape strategy arbiter decided eagerly and keyed by shape only
   (TTB:864-987, 1118-1215), with the reference's memory gate
   (``_would_oom_causal``, TTB:1036-1116) restated for HBM;
@@ -203,11 +206,13 @@ class UserOptimizedTransformer(nn.Module):
 
         The reference masks padded keys in attention and zeroes padded rows after each
         block and after the final norm (TTB:125-128, 140-141, 163-164, 190-191).  With
-        causal attention and a prefix-valid mask (``True`` then ``False`` along each
-        sequence, what ``generate_random_case`` produces, TTB:1793-1803) a valid query
-        only ever attends valid keys, so valid rows equal the unmasked computation and
-        the output's padded rows are zero: the kernels implement exactly that.  Masks
-        with interior holes would change valid rows and are rejected."""
+        a prefix-valid mask (``True`` then ``False`` along each sequence, what
+        ``generate_random_case`` produces, TTB:1793-1803) that is: attention limited to
+        each sequence's first ``len`` keys (automatic for valid rows under causal
+        attention; the kernels apply it for non-causal attention from the per-sequence
+        lengths) and the output's padded rows set to zero.  Padded rows never influence
+        valid rows, so their intermediate values need no masking.  Masks with interior
+        holes are rejected."""
         if m is None:
             return None
         key = (m.data_ptr(), tuple(m.shape), str(m.device))
@@ -215,7 +220,7 @@ class UserOptimizedTransformer(nn.Module):
         if hit is None:
             mb = m.to(torch.bool)
             if bool(mb.all()):
-                hit = ("ones", None)
+                hit = ("ones", None, None)
             else:
                 if mb.dim() != 2:
                     raise ValueError("valid_token_mask must be [batch, seq_len]")
@@ -224,13 +229,19 @@ class UserOptimizedTransformer(nn.Module):
                     raise NotImplementedError(
                         "valid_token_mask must be prefix-valid per sequence (valid tokens first, padding last); "
                         "masks with interior holes are not supported")
-                hit = ("pad", mb.to(torch.uint8).contiguous().reshape(-1))
+                hit = ("pad", mb.to(torch.uint8).contiguous().reshape(-1), mb.sum(1).to(torch.int32).contiguous())
             self._mask_cache[key] = hit
-        rows = hit[1]
-        if rows is not None and device is not None and rows.device != device:
-            rows = rows.to(device)
-            self._mask_cache[key] = ("pad", rows)
-        return rows
+        if hit[1] is not None and device is not None and hit[1].device != device:
+            hit = ("pad", hit[1].to(device), hit[2].to(device))
+            self._mask_cache[key] = hit
+        return hit[1]
+
+    def _padding_lens(self, m: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
+        """Valid tokens per sequence (int32 [B]) of a cached padding mask, or None."""
+        if m is None:
+            return None
+        hit = self._mask_cache.get((m.data_ptr(), tuple(m.shape), str(m.device)))
+        return None if hit is None else hit[2] if len(hit) > 2 else None
 
     def _fused_small_eligible(self) -> bool:
         c = self.config
@@ -254,6 +265,8 @@ class UserOptimizedTransformer(nn.Module):
             if self.force_strategy == "fused_small" and not (self._fused_small_eligible() and S <= 128):
                 raise ValueError("fused_small needs d_model=128, 4 heads, ffn_dim<=512 (multiple of 128), seq_len<=128")
             if self.force_strategy == "chunked":
+                if not self.config.causal:
+                    raise ValueError("the chunked strategy is causal-only (prefix chunks)")
                 self._chunk_plan[(B, S, device.index)] = self._chunk_rows_for(B, S, device)
             return self.force_strategy
         key = (B, S, device.index)
@@ -263,7 +276,7 @@ class UserOptimizedTransformer(nn.Module):
         cfg = self.config
         if self._fused_small_eligible() and S <= 128:
             strat = "fused_small"
-        elif _CHUNK_FORCE_ROWS > 0 or self._would_oom(B, S, device):
+        elif cfg.causal and (_CHUNK_FORCE_ROWS > 0 or self._would_oom(B, S, device)):
             strat = "chunked"
             self._chunk_plan[key] = self._chunk_rows_for(B, S, device)
         else:
@@ -308,8 +321,6 @@ class UserOptimizedTransformer(nn.Module):
     # ------------------------------------------------------------------ forward
     def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
         cfg = self.config
-        if not cfg.causal:
-            raise NotImplementedError("UserOptimizedTransformer implements the causal forward only")
         if not x.is_cuda:
             raise RuntimeError("UserOptimizedTransformer runs on a CUDA (B200, sm_100a) device only; "
                                "there is no CPU fallback")
@@ -319,16 +330,17 @@ class UserOptimizedTransformer(nn.Module):
         if valid_token_mask is not None and tuple(valid_token_mask.shape) != (B, S):
             raise ValueError(f"valid_token_mask must be [{B}, {S}], got {tuple(valid_token_mask.shape)}")
         rows_valid = self._padding_rows(valid_token_mask, x.device)
+        kv_lens = self._padding_lens(valid_token_mask) if rows_valid is not None else None
         out_dtype = x.dtype
         xin = x if (x.dtype == torch.float32 and x.is_contiguous()) else x.to(torch.float32).contiguous()
         dev = xin.device
         with torch.cuda.device(dev):
             y = torch.empty_like(xin)
-            self._forward_into(xin, y, rows_valid)
+            self._forward_into(xin, y, rows_valid, kv_lens)
         return y if out_dtype == torch.float32 else y.to(out_dtype)
 
     def _run_graphed(self, x: torch.Tensor, y: torch.Tensor, ws: torch.Tensor, strat: str,
-                     rows_valid: Optional[torch.Tensor] = None) -> None:
+                     rows_valid: Optional[torch.Tensor] = None, kv_lens: Optional[torch.Tensor] = None) -> None:
         """Replay (or capture) the forward as one CUDA graph keyed by shape and pointers.
 
         The graph reads x (and the padding flags) and writes y at the addresses it was
@@ -336,19 +348,20 @@ class UserOptimizedTransformer(nn.Module):
         the caching allocator hands the same output block back to a loop that drops its
         previous result, so steady-state calls replay without copies."""
         rv = 0 if rows_valid is None else rows_valid.data_ptr()
-        key = (tuple(x.shape), x.data_ptr(), y.data_ptr(), ws.data_ptr(), strat, rv)
+        kl = 0 if kv_lens is None else kv_lens.data_ptr()
+        key = (tuple(x.shape), x.data_ptr(), y.data_ptr(), ws.data_ptr(), strat, rv, kl)
         g = self._graphs.get(key)
         if g is None:
             shape_key = (tuple(x.shape), strat)
             if shape_key not in self._warm:
                 # first call at this shape: launch eagerly (sets kernel attributes, validates arguments)
-                self._launch(x, y, ws, strat, rows_valid)
+                self._launch(x, y, ws, strat, rows_valid, kv_lens)
                 torch.cuda.current_stream().synchronize()
                 self._warm.add(shape_key)
                 return
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
-                self._launch(x, y, ws, strat, rows_valid)
+                self._launch(x, y, ws, strat, rows_valid, kv_lens)
             self._graphs[key] = g
             while len(self._graphs) > _GRAPH_CACHE:
                 self._graphs.popitem(last=False)
@@ -357,7 +370,7 @@ class UserOptimizedTransformer(nn.Module):
         g.replay()
 
     def _launch(self, x: torch.Tensor, y: torch.Tensor, ws: torch.Tensor, strat: str,
-                rows_valid: Optional[torch.Tensor] = None) -> None:
+                rows_valid: Optional[torch.Tensor] = None, kv_lens: Optional[torch.Tensor] = None) -> None:
         if strat == "fused_small":
             self._forward_fused_small(x, y, rows_valid)
             return
@@ -365,7 +378,7 @@ class UserOptimizedTransformer(nn.Module):
             B, S, _ = x.shape
             self._forward_chain(x, y, ws, chunk_rows=self._chunk_plan[(B, S, x.device.index)])
         else:
-            self._forward_chain(x, y, ws)
+            self._forward_chain(x, y, ws, kv_lens=kv_lens)
         if rows_valid is not None:
             rt.zero_masked_rows(y, rows_valid)
 
@@ -384,10 +397,11 @@ class UserOptimizedTransformer(nn.Module):
         a.lnf_w, a.lnf_b = self._lnf[0].data_ptr(), self._lnf[1].data_ptr()
         a.eps = float(self.layers[0].norm1.eps)
         a.row_valid = None if rows_valid is None else rows_valid.data_ptr()
+        a.non_causal = 0 if cfg.causal else 1
         rt.fused_small(a)
 
     def _forward_chain(self, x: torch.Tensor, y: torch.Tensor, ws: torch.Tensor,
-                       chunk_rows: Optional[int] = None) -> None:
+                       chunk_rows: Optional[int] = None, kv_lens: Optional[torch.Tensor] = None) -> None:
         cfg = self.config
         B, S, d = x.shape
         cur = x
@@ -411,6 +425,8 @@ class UserOptimizedTransformer(nn.Module):
                 a.lnf_w, a.lnf_b = None, None
             a.eps = float(self.layers[i].norm1.eps)
             a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+            a.non_causal = 0 if cfg.causal else 1
+            a.kv_lens = None if kv_lens is None else kv_lens.data_ptr()
             if chunk_rows:
                 rt.block_forward_chunked(a, chunk_rows)
             else:
@@ -493,7 +509,8 @@ class UserOptimizedTransformer(nn.Module):
             pipes[key] = pipe
         return pipe
 
-    def _forward_into(self, xin: torch.Tensor, y: torch.Tensor, rows_valid: Optional[torch.Tensor] = None) -> None:
+    def _forward_into(self, xin: torch.Tensor, y: torch.Tensor, rows_valid: Optional[torch.Tensor] = None,
+                      kv_lens: Optional[torch.Tensor] = None) -> None:
         """Forward of a contiguous fp32 CUDA tensor into a preallocated ``y`` (current stream);
         ``rows_valid`` (uint8 [B*S], optional) zeroes padded output rows."""
         B, S, d = xin.shape
@@ -509,9 +526,9 @@ class UserOptimizedTransformer(nn.Module):
         else:
             ws = self._workspace(256, dev)
         if _GRAPHS_ON and xin.numel() <= _GRAPH_MAX_ELEMS:
-            self._run_graphed(xin, y, ws, strat, rows_valid)
+            self._run_graphed(xin, y, ws, strat, rows_valid, kv_lens)
         else:
-            self._launch(xin, y, ws, strat, rows_valid)
+            self._launch(xin, y, ws, strat, rows_valid, kv_lens)
 
     # ------------------------------------------------------------------ profiling helper
     @torch.no_grad()
@@ -559,7 +576,7 @@ class UserOptimizedTransformer(nn.Module):
             ("ln1", lambda: rt.layernorm(x2, pk.ln1_w, pk.ln1_b, n, eps)),
             ("qkv", lambda: rt.gemm(rt.EPI_BIAS_F16, n, pk.w_qkv, pk.b_qkv, qkv)),
             ("attn", lambda: rt.flash_causal(qkv, qkv, qkv, ctx, batch=B, heads=H, head_dim=d // H, q_len=S,
-                                             kv_len=S, k_col0=d, v_col0=2 * d)),
+                                             kv_len=S, k_col0=d, v_col0=2 * d, non_causal=not cfg.causal)),
             ("out_proj", lambda: rt.gemm(rt.EPI_BIAS_RESID_F32, ctx, pk.w_o, pk.b_o, x1, resid=x2)),
             ("ln2", lambda: rt.layernorm(x1, pk.ln2_w, pk.ln2_b, n, eps)),
             ("ffn_in", lambda: rt.gemm(rt.EPI_BIAS_GELU_F16, n, pk.w_in, pk.b_in, h)),

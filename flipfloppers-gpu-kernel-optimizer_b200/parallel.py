@@ -183,7 +183,7 @@ class TensorParallelTransformer:
         for i, w in enumerate(self._weights):
             rt.gemm(rt.EPI_BIAS_F16, n, w["w_qkv"], w["b_qkv"], qkv)
             rt.flash_causal(qkv, qkv, qkv, ctx, batch=B, heads=Hl, head_dim=hd, q_len=S, kv_len=S,
-                            q_col0=0, k_col0=dl, v_col0=2 * dl)
+                            q_col0=0, k_col0=dl, v_col0=2 * dl, non_causal=not cfg.causal)
             rt.gemm(rt.EPI_BIAS_F32, ctx, w["w_o"], None, part)
             dist.all_reduce(part, op=dist.ReduceOp.SUM, group=self.group)
             # x1 = x + partial + b_o ; n = LN2(x1)

@@ -57,6 +57,7 @@ class AttnArgs(ctypes.Structure):
         ("q_row0", ctypes.c_int), ("kv_row0", ctypes.c_int),
         ("q_col0", ctypes.c_int), ("k_col0", ctypes.c_int), ("v_col0", ctypes.c_int),
         ("out", _vp), ("ld_out", _c_ll), ("out_seq_rows", ctypes.c_int), ("out_row0", ctypes.c_int),
+        ("non_causal", ctypes.c_int), ("kv_lens", _vp),
     ]
 
 
@@ -74,6 +75,7 @@ class BlockArgs(ctypes.Structure):
         ("lnf_w", _vp), ("lnf_b", _vp),
         ("eps", ctypes.c_float),
         ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
+        ("non_causal", ctypes.c_int), ("kv_lens", _vp),
     ]
 
 
@@ -91,6 +93,7 @@ class FusedSmallArgs(ctypes.Structure):
         ("lnf_w", _vp), ("lnf_b", _vp),
         ("eps", ctypes.c_float),
         ("row_valid", _vp),
+        ("non_causal", ctypes.c_int),
     ]
 
 
@@ -224,8 +227,9 @@ def gemm(epilogue: int, a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.T
 def flash_causal(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor, *, batch: int, heads: int,
                  head_dim: int, q_len: int, kv_len: int, q_offset: int = 0, q_seq_rows: int = None,
                  kv_seq_rows: int = None, q_col0: int = 0, k_col0: int = 0, v_col0: int = 0, q_row0: int = 0,
-                 kv_row0: int = 0, out_seq_rows: int = None, out_row0: int = 0, stream=None) -> torch.Tensor:
-    """Prefix-causal attention over 2-D fp16 tensors (see B200AttnArgs)."""
+                 kv_row0: int = 0, out_seq_rows: int = None, out_row0: int = 0, non_causal: bool = False,
+                 kv_lens: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """Prefix-causal (or full) attention over 2-D fp16 tensors (see B200AttnArgs)."""
     _require_cuda(q, k, v, out)
     a = AttnArgs()
     a.q, a.k, a.v = q.data_ptr(), k.data_ptr(), v.data_ptr()
@@ -240,6 +244,8 @@ def flash_causal(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.T
     a.out, a.ld_out = out.data_ptr(), out.stride(0)
     a.out_seq_rows = q_len if out_seq_rows is None else out_seq_rows
     a.out_row0 = out_row0
+    a.non_causal = int(bool(non_causal))
+    a.kv_lens = None if kv_lens is None else kv_lens.data_ptr()
     check(lib().b200_flash_causal_launch(ctypes.byref(a), _stream(stream)), "b200_flash_causal_launch")
     return out
 

@@ -110,7 +110,7 @@ int b200_gemm_launch(int epilogue, const void* A, long long lda, const void* W, 
                      const float* resid, long long ld_resid, void* out, long long ld_out, int M, int N, int K,
                      b200_stream_t stream);
 
-/* Causal attention.  Q, K, V fp16 2-D tensors [rows, ld] holding head h of
+/* Causal (or, with non_causal = 1, full) attention.  Q, K, V fp16 2-D tensors [rows, ld] holding head h of
  * sequence b at rows (row0 + b*seq_rows + position) and columns
  * (col0 + h*head_dim ...).  Query i of a sequence sits at absolute position
  * q_offset + i and attends keys 0..q_offset+i (prefix-causal).  Writes the
@@ -133,6 +133,8 @@ typedef struct {
   long long ld_out;
   int out_seq_rows;
   int out_row0;
+  int non_causal;        /* 0: causal (query i sees keys <= q_offset+i); 1: every valid key */
+  const int* kv_lens;    /* device [batch]: valid keys per sequence (key padding); NULL = kv_len */
 } B200AttnArgs;
 
 int b200_flash_causal_launch(const B200AttnArgs* args, b200_stream_t stream);
@@ -164,6 +166,8 @@ typedef struct {
   float eps;
   void* workspace;         /* >= b200_block_workspace_bytes(batch*seq_len, d_model, ffn_dim) */
   size_t workspace_bytes;
+  int non_causal;          /* 0: causal block; 1: full attention (the reference without --causal) */
+  const int* kv_lens;      /* device [batch] valid tokens per sequence (key padding), NULL = all */
 } B200BlockArgs;
 
 size_t b200_block_workspace_bytes(long long tokens, int d_model, int ffn_dim);
@@ -206,7 +210,9 @@ typedef struct {
   const float* lnf_b;
   float eps;
   const void* row_valid;   /* [batch*seq_len] uint8 key-padding mask (0 = padded row; prefix-valid per
-                              sequence); padded rows of y are written as 0.  NULL = no padding. */
+                              sequence); padded keys are masked and padded rows of y written as 0.
+                              NULL = no padding. */
+  int non_causal;          /* 0: causal; 1: full attention */
 } B200FusedSmallArgs;
 
 int b200_block_fused_small_launch(const B200FusedSmallArgs* args, b200_stream_t stream);

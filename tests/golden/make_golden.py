@@ -32,7 +32,7 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 
-# (name, B, S, d, H, ffn, L, padding_ratio, seed, trial)
+# (name, B, S, d, H, ffn, L, padding_ratio, seed, trial[, causal])
 CASES = [
     ("c1", 4, 128, 128, 4, 512, 1, 0.0, 1234, 0),        # BASELINE config 1, trial 0
     ("c1_t1", 4, 128, 128, 4, 512, 1, 0.0, 1234, 1),     # trial 1 (seed 1235)
@@ -41,6 +41,8 @@ CASES = [
     ("h16", 1, 96, 1024, 16, 4096, 1, 0.0, 1234, 0),      # d=1024, H=16 (config-5 head shape)
     ("hd256", 2, 32, 1024, 4, 4096, 1, 0.0, 1234, 0),     # head_dim 256 (config 4b head shape)
     ("pad_l2", 3, 48, 64, 2, 256, 2, 0.3, 1234, 1),       # padding mask + two layers
+    ("nc_c1", 4, 128, 128, 4, 512, 1, 0.0, 1234, 0, False),   # non-causal (harness default without --causal)
+    ("nc_pad", 3, 100, 256, 4, 1024, 2, 0.4, 1234, 2, False),  # non-causal + padding + two layers
 ]
 
 
@@ -63,9 +65,11 @@ def main() -> int:
     ref = load_reference(args.reference)
     torch.set_num_threads(os.cpu_count() or 1)
     index = []
-    for name, B, S, d, H, F, L, pad, seed, trial in CASES:
+    for case in CASES:
+        name, B, S, d, H, F, L, pad, seed, trial = case[:10]
+        causal = case[10] if len(case) > 10 else True
         cfg = ref.TransformerConfig(batch_size=B, seq_len=S, d_model=d, num_heads=H,
-                                    ffn_dim=F, num_layers=L, causal=True)
+                                    ffn_dim=F, num_layers=L, causal=causal)
         cfg.validate()
         torch.manual_seed(seed)
         base = ref.BaselineTransformer(cfg).eval()
@@ -85,7 +89,7 @@ def main() -> int:
             fingerprint=json.dumps(fp),
         )
         index.append(dict(name=name, B=B, S=S, d=d, H=H, ffn=F, L=L, padding_ratio=pad,
-                          seed=seed, trial=trial, x_seed=seed + trial,
+                          seed=seed, trial=trial, x_seed=seed + trial, causal=causal,
                           torch=torch.__version__))
         print(f"{name}: y max|.|={float(y.abs().max()):.4f}")
     with open(os.path.join(args.out, "golden_index.json"), "w") as f:

@@ -77,3 +77,19 @@ def test_fused_repeatable_and_graph_replay(tt):
     torch.cuda.synchronize()
     for o in outs[1:]:
         assert torch.equal(o, outs[0])
+
+
+@pytest.mark.parametrize("B,S,F,L", [(4, 128, 512, 1), (3, 70, 256, 2)])
+def test_fused_small_noncausal(tt, B, S, F, L):
+    cfg = tt.TransformerConfig(B, S, 128, 4, F, L, False)
+    torch.manual_seed(3)
+    model = tt.UserOptimizedTransformer(cfg).to(DEV).eval()
+    x, mask = oracle.generate_random_case(B, S, 128, 4, padding_ratio=0.3)
+    for m in (None, mask):
+        with torch.inference_mode():
+            y = model(x.to(DEV), None if m is None else m.to(DEV)).cpu()
+        assert model.last_strategy == "fused_small"
+        ref = oracle.model_forward(oracle.params_from_state_dict(model.state_dict()),
+                                   oracle.OracleConfig(B, S, 128, 4, F, L, False), x.numpy(),
+                                   None if m is None else m.numpy())
+        assert oracle.compare_outputs(ref, y, rtol=RTOL, atol=ATOL).passed

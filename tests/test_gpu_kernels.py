@@ -193,3 +193,22 @@ def test_launch_rejects_unsupported_shapes(rt):
     o = torch.zeros(128, 96, dtype=torch.float16, device=DEV)
     with pytest.raises(rt.B200Error, match="head_dim"):
         rt.flash_causal(qkv, qkv, qkv, o, batch=1, heads=2, head_dim=48, q_len=128, kv_len=128)
+
+
+@pytest.mark.parametrize("B,H,S,hd", [(2, 2, 200, 64), (2, 4, 128, 32), (1, 2, 2200, 64), (2, 2, 300, 256)])
+def test_flash_noncausal_with_key_lengths_vs_torch(rt, B, H, S, hd):
+    """Full attention with per-sequence valid key counts (key padding)."""
+    g = torch.Generator().manual_seed(S + hd)
+    d = H * hd
+    qkv = torch.randn(B * S, 3 * d, generator=g).to(torch.float16).to(DEV)
+    lens = torch.tensor([S - 37 * (i + 1) for i in range(B)], dtype=torch.int32)
+    out = torch.empty(B * S, d, dtype=torch.float16, device=DEV)
+    rt.flash_causal(qkv, qkv, qkv, out, batch=B, heads=H, head_dim=hd, q_len=S, kv_len=S, k_col0=d, v_col0=2 * d,
+                    non_causal=True, kv_lens=lens.to(DEV))
+    t = qkv.float().view(B, S, 3, H, hd).permute(2, 0, 3, 1, 4)
+    s_ = (t[0] @ t[1].transpose(-1, -2)) * hd ** -0.5
+    keymask = torch.arange(S, device=DEV)[None, :] >= lens.to(DEV)[:, None].long()
+    s_ = s_.masked_fill(keymask[:, None, None, :], float("-inf"))
+    ref = (torch.softmax(s_, -1) @ t[2]).permute(0, 2, 1, 3).reshape(B * S, d)
+    torch.cuda.synchronize()
+    assert (out.float() - ref).abs().max().item() < 4e-3

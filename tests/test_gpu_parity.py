@@ -24,8 +24,8 @@ ATOL, RTOL = 0.002, 0.02
 DEV = "cuda"
 
 
-def _model(tt, B, S, d, H, F, L, seed=1234):
-    cfg = tt.TransformerConfig(B, S, d, H, F, L, True)
+def _model(tt, B, S, d, H, F, L, seed=1234, causal=True):
+    cfg = tt.TransformerConfig(B, S, d, H, F, L, causal)
     cfg.validate()
     torch.manual_seed(seed)
     return tt.UserOptimizedTransformer(cfg).to(DEV).eval(), cfg
@@ -51,7 +51,8 @@ def _clean_device_errors(pkg):
 def test_golden_cases(tt, case):
     g = load_golden(case["name"])
     x, mask = oracle.generate_random_case(case["B"], case["S"], case["d"], case["x_seed"], case["padding_ratio"])
-    model, _ = _model(tt, case["B"], case["S"], case["d"], case["H"], case["ffn"], case["L"], case["seed"])
+    model, _ = _model(tt, case["B"], case["S"], case["d"], case["H"], case["ffn"], case["L"], case["seed"],
+                      causal=case.get("causal", True))
     with torch.inference_mode():
         y = model(x.to(DEV), mask.to(DEV)).cpu()
     res = oracle.compare_outputs(g["y"], y, rtol=RTOL, atol=ATOL)
@@ -177,21 +178,37 @@ def test_forward_host_pipeline_matches_device_path(tt, d, H, F):
             assert torch.equal(o, ref)
 
 
-@pytest.mark.parametrize("B,S,d,H,F,L", [(8, 128, 128, 4, 512, 1), (6, 96, 128, 4, 256, 2), (5, 200, 256, 4, 1024, 1)])
-def test_padding_masks_against_oracle(tt, B, S, d, H, F, L):
+@pytest.mark.parametrize("causal", [True, False], ids=["causal", "noncausal"])
+@pytest.mark.parametrize("B,S,d,H,F,L", [(8, 128, 128, 4, 512, 1), (6, 96, 128, 4, 256, 2), (5, 200, 256, 4, 1024, 1),
+                                         (2, 2300, 256, 4, 512, 1)])
+def test_padding_masks_against_oracle(tt, B, S, d, H, F, L, causal):
     """Prefix-valid key-padding masks (generate_random_case with padding_ratio > 0):
     valid rows match the reference's masked forward, padded rows are exactly 0 --
-    on the fused small-model kernel (d=128) and on the chain."""
-    model, _ = _model(tt, B, S, d, H, F, L, seed=31)
+    on the fused small-model kernel (d=128), on the chain, and (S >= 2048) with
+    the two-query-tile attention kernel; causal and non-causal."""
+    model, _ = _model(tt, B, S, d, H, F, L, seed=31, causal=causal)
     x, mask = oracle.generate_random_case(B, S, d, 32, padding_ratio=0.5)
     assert not bool(mask.all())
     with torch.inference_mode():
         y = model(x.to(DEV), mask.to(DEV)).cpu()
     ref = oracle.model_forward(oracle.params_from_state_dict(model.state_dict()),
-                               oracle.OracleConfig(B, S, d, H, F, L, True), x.numpy(), mask.numpy())
+                               oracle.OracleConfig(B, S, d, H, F, L, causal), x.numpy(), mask.numpy())
     res = oracle.compare_outputs(ref, y, rtol=RTOL, atol=ATOL)
     assert res.passed, res
     assert torch.all(y[~mask] == 0)
+
+
+@pytest.mark.parametrize("B,S,d,H,F,L", [(4, 128, 128, 4, 512, 1), (3, 77, 128, 4, 256, 2), (2, 300, 1024, 16, 4096, 1),
+                                         (1, 2500, 256, 4, 1024, 1)])
+def test_noncausal_against_oracle(tt, B, S, d, H, F, L):
+    """The reference harness without --causal (full attention), no padding."""
+    model, _ = _model(tt, B, S, d, H, F, L, seed=5, causal=False)
+    x, _ = oracle.generate_random_case(B, S, d, 6)
+    y = _run(model, x)
+    ref = oracle.model_forward(oracle.params_from_state_dict(model.state_dict()),
+                               oracle.OracleConfig(B, S, d, H, F, L, False), x.numpy())
+    res = oracle.compare_outputs(ref, y, rtol=RTOL, atol=ATOL)
+    assert res.passed, res
 
 
 def test_mask_with_holes_is_rejected(tt):
