@@ -73,6 +73,10 @@ def rank_batch(cfg_name, rank, world):
     return B
 
 
+# ~20 ms of device-side spinning queued ahead of the timed steps
+QUEUE_PREFILL_CYCLES = 40_000_000
+
+
 def flushes(cfg_name):
     """Flush L2 between steps unless one step's input alone is several times the 126 MB L2."""
     B, S, d = CONFIGS[cfg_name][:3]
@@ -345,6 +349,10 @@ def main():
         ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         barrier()
         torch.cuda.synchronize()
+        # keep the GPU busy while the host enqueues every timed step, so no
+        # host-side enqueue latency (Python call overhead) falls between an
+        # event pair: the events then bracket device work only
+        torch.cuda._sleep(QUEUE_PREFILL_CYCLES)
         for i in range(args.steps):
             flush.zero_()
             starts[i].record(stream)

@@ -48,7 +48,7 @@ __global__ void __launch_bounds__(320, 1)
                     const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
   using C = Attn2Cfg<HD>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = smem_align1024(smem_raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* q_full = bars + 0;
   uint64_t* kv_full = bars + 1;            // [ST]

@@ -135,6 +135,23 @@ int make_map_f16(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols,
   return r == CUDA_SUCCESS ? B200_OK : B200_ERR_TMAP;
 }
 
+// [num_seq, seq_len, cols] fp32 activations as a 3-D map with SWIZZLE_128B
+// boxes of 32 columns x box_rows rows x 1 sequence: rows past seq_len are
+// zero-filled on load and not written on store, so a box never reaches into
+// the next sequence.
+int make_map_f32_seq(CUtensorMap* m, const void* base, uint64_t num_seq, uint64_t seq_len, uint64_t cols,
+                     uint32_t box_rows) {
+  if (ensure_encode() != B200_OK) return B200_ERR_TMAP;
+  cuuint64_t dims[3] = {cols, seq_len, num_seq};
+  cuuint64_t strides[2] = {cols * 4, seq_len * cols * 4};
+  cuuint32_t box[3] = {32, box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? B200_OK : B200_ERR_TMAP;
+}
+
 // ------------------------------------------------------------------ GEMM
 template <int BN, int STAGES, int EPI>
 int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p, cudaStream_t st) {
@@ -413,6 +430,9 @@ int fused_small_impl(const B200FusedSmallArgs* a, cudaStream_t st) {
   if (int rc = make_map_f16(&to, a->w_o, static_cast<uint64_t>(L) * 128, 128, 128, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
   if (int rc = make_map_f16(&ti, a->w_in, static_cast<uint64_t>(L) * F, 128, 128, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
   if (int rc = make_map_f16(&tout, a->w_out, static_cast<uint64_t>(L) * 128, F, F, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
+  CUtensorMap tx, ty;
+  if (int rc = make_map_f32_seq(&tx, a->x, a->batch, a->seq_len, 128, 128)) return rc;
+  if (int rc = make_map_f32_seq(&ty, a->y, a->batch, a->seq_len, 128, 32)) return rc;
   SmallParams p{};
   p.num_seq = a->batch;
   p.seq_len = a->seq_len;
@@ -438,7 +458,7 @@ int fused_small_impl(const B200FusedSmallArgs* a, cudaStream_t st) {
   if (int rc = set_smem(reinterpret_cast<const void*>(k_block_small), smem)) return rc;
   if (int rc = check_block_fits(reinterpret_cast<const void*>(k_block_small), SmallCfg::THREADS)) return rc;
   const int grid = a->batch < num_sms() ? a->batch : num_sms();
-  k_block_small<<<grid, SmallCfg::THREADS, smem, st>>>(tq, to, ti, tout, p);
+  k_block_small<<<grid, SmallCfg::THREADS, smem, st>>>(tq, to, ti, tout, tx, ty, p);
   return launch_status();
 }
 

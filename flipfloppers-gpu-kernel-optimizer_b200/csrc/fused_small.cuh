@@ -7,12 +7,17 @@
 // persistent CTA per SM walks sequences; for each sequence and layer the whole
 // pre-LN block runs on chip -- LN1, QKV projection, 4-head causal attention,
 // out_proj + residual, LN2, ffn_in + erf-GELU, ffn_out + residual, and the
-// final LayerNorm after the last layer.  Only x is read and y written in HBM;
-// weights (384 KB per layer at ffn=512) are streamed from L2 by TMA.
+// final LayerNorm after the last layer.  Only x is read and y written in HBM,
+// both by TMA (x as four 128-row x 32-column fp32 boxes, prefetched for the
+// next sequence while the current one is in its FFN; y as one 32x32 box per
+// worker warp); weights (384 KB per layer at ffn=512) are streamed from L2 by
+// TMA.  Every global access is a bulk copy: a thread owns a row, so plain
+// per-thread loads and stores would touch 32 rows per warp instruction.
 //
 // Roles (18 warps):
-//   warp 0      TMA producer: 128x64 fp16 weight boxes (SWIZZLE_128B) through a
-//               3-stage ring, in exactly the order the MMA warp consumes them;
+//   warp 0      TMA producer: x of each sequence, and 128x64 fp16 weight boxes
+//               (SWIZZLE_128B) through a 3-stage ring, in exactly the order
+//               the MMA warp consumes them;
 //   warp 1      TMEM owner (512 columns) and tcgen05.mma issuer;
 //   warps 2-17  workers: warp w owns TMEM lane quadrant q = w%4 (rows
 //               32q..32q+31, one row per lane) and column group g = (w-2)/4
@@ -21,15 +26,19 @@
 //               combined across the 4 groups of a row in shared memory behind
 //               one named barrier per quadrant.
 //
-// TMEM columns:  [0,384) QKV accumulator | then [0,128),[128,256) S of two
-//   heads in flight, [256,384) O of the 4 heads, [384,512) out_proj
-//   accumulator, overwritten in place by the fp32 residual x1 | then
-//   [0,128),[128,256) ffn_in chunk accumulators (ping-pong), [256,384) ffn_out
-//   accumulator.
+// TMEM columns:  [384,512) is the residual stream: x is stored there before
+//   LN1, out_proj accumulates onto it (x + ctx.Wo^T), the bias is added in
+//   place (x1), and ffn_out accumulates onto x1.  [0,384) QKV accumulator |
+//   then [0,128),[128,256) S of two heads in flight, [256,384) O of the 4
+//   heads | then [0,128),[128,256) ffn_in chunk accumulators (ping-pong).
 // Shared memory (1 CTA/SM): XA 32 KB (LN1 out -> context -> LN2 out, fp16,
 //   SW128 K-major), Q/K/V 3 x 4 heads x 8 KB (SW64; V read MN-major), P 32 KB,
 //   weight ring 48 KB, GELU chunk ping-pong aliasing the Q and K areas, the
 //   layer's biases and LayerNorm parameters (7.5 KB, staged once per layer).
+//   The layer input XIN (fp32, four SW128 boxes of 128 rows x 128 bytes)
+//   aliases V and P: it is filled by TMA (layer 0, after the previous
+//   sequence's attention) or by each thread's own W7 stores (later layers).
+//   The y staging boxes (16 x 4 KB, one per worker warp) alias Q and K.
 //
 // Every wait is bounded (ptx.cuh); a worker that gives up still executes every
 // named barrier (control flow never depends on data), so the CTA always
@@ -46,7 +55,7 @@ struct SmallParams {
   int layers;
   int ffn;            // multiple of 128, <= 512
   const float* x;     // [num_seq*seq_len, 128]
-  float* y;           // [num_seq*seq_len, 128]; holds the residual between layers
+  float* y;           // [num_seq*seq_len, 128]
   const float* ln1_w; const float* ln1_b;   // [layers, 128]
   const float* b_qkv;                       // [layers, 384]
   const float* b_o;                         // [layers, 128]
@@ -72,6 +81,8 @@ struct SmallCfg {
   static constexpr int OFF_V = 98304;
   static constexpr int OFF_P = 131072;          // 32 KB
   static constexpr int OFF_W = 163840;          // WST x 16 KB
+  static constexpr int OFF_XIN = OFF_V;         // 64 KB layer input, aliases V and P
+  static constexpr int OFF_YST = OFF_Q;         // 64 KB y staging, aliases Q and K
   static constexpr int OFF_STATS = OFF_W + WST * BOX;   // float [2][4][128]
   static constexpr int OFF_VEC = OFF_STATS + 2 * 4 * 128 * 4;  // per-layer vectors, fp32
   // float offsets inside the vector block
@@ -99,7 +110,8 @@ enum SmallBar : int {
   SB_HFREE = 20,       // [2] MMA: ffn_out consumed a GELU chunk buffer
   SB_FOUT = 22,        // MMA: ffn_out accumulator complete
   SB_DRAIN = 23,
-  SB_COUNT = 24
+  SB_XFULL = 24,       // TMA: x of the CTA's current sequence in XIN
+  SB_COUNT = 25
 };
 
 __device__ __forceinline__ void named_bar(int id, int count) {
@@ -115,10 +127,11 @@ __device__ __forceinline__ uint32_t par(int step, int per, int idx) {
 __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
     k_block_small(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_o,
                   const __grid_constant__ CUtensorMap tm_in, const __grid_constant__ CUtensorMap tm_out,
+                  const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_y,
                   const SmallParams p) {
   using C = SmallCfg;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = smem_align1024(smem_raw);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + SB_COUNT);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -155,6 +168,7 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
     mbar_init(&bar[SB_HFREE + 1], 1);
     mbar_init(&bar[SB_FOUT], 1);
     mbar_init(&bar[SB_DRAIN], 1);
+    mbar_init(&bar[SB_XFULL], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -174,8 +188,18 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
       tma_prefetch_desc(&tm_o);
       tma_prefetch_desc(&tm_in);
       tma_prefetch_desc(&tm_out);
+      tma_prefetch_desc(&tm_x);
       int box = 0;
       bool ok = true;
+      // x of sequence `seq` (rows past seq_len are zero-filled) -> XIN
+      int xloads = 0;
+      auto load_x = [&](int seq) {
+        ++xloads;
+        mbar_arrive_expect_tx(&bar[SB_XFULL], 4 * 128 * 128);
+        for (int g = 0; g < 4; ++g)
+          tma_load_3d(smem + C::OFF_XIN + g * 16384, &tm_x, &bar[SB_XFULL], 32 * g, 0, seq);
+      };
+      if (nsteps > 0) load_x(static_cast<int>(blockIdx.x));
       auto load = [&](const CUtensorMap* m, int col, int row) {
         const int s = box % C::WST;
         if (box >= C::WST && !mbar_wait(&bar[SB_WEMPTY + s], ((box / C::WST) - 1) & 1, abort_flag, DERR_WAIT_SLOT)) {
@@ -192,15 +216,27 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
           for (int kh = 0; ok && kh < 2; ++kh) load(&tm_qkv, kh * 64, l * 384 + nt * 128);
         for (int kh = 0; ok && kh < 2; ++kh) load(&tm_o, kh * 64, l * 128);
         for (int kh = 0; ok && kh < 2; ++kh) load(&tm_in, kh * 64, l * p.ffn);
+        // after the last layer's attention (V and P consumed, CTX published) the
+        // next sequence's x can overwrite XIN while this one runs its FFN
+        const int next_seq = static_cast<int>(blockIdx.x) + (step / p.layers + 1) * static_cast<int>(gridDim.x);
+        if (ok && l == p.layers - 1 && next_seq < p.num_seq) {
+          if (!mbar_wait(&bar[SB_CTX], par(step, 1, 0), abort_flag, DERR_WAIT_SOFTMAX)) {
+            ok = false;
+            break;
+          }
+          load_x(next_seq);
+        }
         for (int c = 0; ok && c < nch; ++c) {
           if (c + 1 < nch)
             for (int kh = 0; ok && kh < 2; ++kh) load(&tm_in, kh * 64, l * p.ffn + (c + 1) * 128);
           for (int kh = 0; ok && kh < 2; ++kh) load(&tm_out, c * 128 + kh * 64, l * 128);
         }
       }
-      if (*abort_flag)
+      if (*abort_flag) {
         for (int b = (box > C::WST ? box - C::WST : 0); b < box; ++b)
           mbar_wait_drain(&bar[SB_WFULL + b % C::WST], (b / C::WST) & 1);
+        if (xloads > 0) mbar_wait_drain(&bar[SB_XFULL], (xloads - 1) & 1);
+      }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -268,7 +304,7 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
         // out_proj
         if (!mbar_wait(&bar[SB_CTX], par(step, 1, 0), abort_flag, DERR_WAIT_SOFTMAX)) break;
         tc_fence_after();
-        gemm_k128(xa, 384, false);
+        gemm_k128(xa, 384, true);  // onto the residual x stored by the workers
         if (!ok) break;
         tc_commit(&bar[SB_OP_DONE]);
         // FFN: fin_0, then per chunk c: fin_{c+1}, fout_c
@@ -289,7 +325,7 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
             break;
           }
           tc_fence_after();
-          gemm_k128(smem_u32(smem + (b ? C::OFF_K : C::OFF_Q)), 256, c > 0);
+          gemm_k128(smem_u32(smem + (b ? C::OFF_K : C::OFF_Q)), 384, true);  // onto x1
           if (!ok) break;
           tc_commit(&bar[SB_HFREE + b]);
         }
@@ -402,20 +438,28 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
       const int seq = static_cast<int>(blockIdx.x) + (step / p.layers) * static_cast<int>(gridDim.x);
       const bool row_ok = r < p.seq_len;
       const int64_t grow = static_cast<int64_t>(seq) * p.seq_len + r;
-      const float* xin = (l == 0 ? p.x : p.y) + grow * C::D + c0;
-      // ---- W1: LN1 -> XA (x loads first, so their latency overlaps the vector staging)
-#pragma unroll
-      for (int i = 0; i < 32; i += 4) {
-        float4 t = row_ok ? *reinterpret_cast<const float4*>(xin + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-        v[i] = t.x; v[i + 1] = t.y; v[i + 2] = t.z; v[i + 3] = t.w;
-      }
+      // this thread's 32 columns of row r in XIN (box g, SW128)
+      uint8_t* xin_row = smem + C::OFF_XIN + g * 16384;
+      // ---- W1: x -> residual in TMEM [384,512); LN1 -> XA
       if (step == 0 || p.layers > 1) {
         named_bar(5, 32 * C::NW);  // every worker is done with the previous layer's vectors
         stage_vectors(l);
         named_bar(5, 32 * C::NW);
       }
+      // layer 0: x arrives by TMA; later layers: this thread wrote its own slice in W7
+      if (l == 0) wait_w(SB_XFULL, static_cast<uint32_t>((step / p.layers) & 1));
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 t = *reinterpret_cast<const float4*>(xin_row + sw128_off(r, j));
+        v[4 * j] = t.x; v[4 * j + 1] = t.y; v[4 * j + 2] = t.z; v[4 * j + 3] = t.w;
+      }
+      if (ok) tmem_st32(trow + 384 + c0, v);
       layer_norm(vec + C::V_LN1W, vec + C::V_LN1B);
       store_sw128(xa);
+      // the previous step's y store must have read its staging box before Q/K
+      // (which it aliases) are rewritten, and they are rewritten only after N1
+      if (lane == 0) bulk_wait_read_all();
+      __syncwarp();
       publish(SB_N1);
       // ---- W2: QKV accumulator -> Q/K/V tiles (head g = column group g)
       wait_w(SB_QKV_DONE, par(step, 1, 0));
@@ -479,20 +523,13 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
       }
       store_sw128(xa);
       publish(SB_CTX);
-      // ---- W5: x1 = x + ctx.Wo^T + bo (kept in TMEM) ; LN2 -> XA
-#pragma unroll
-      for (int i = 0; i < 32; i += 4) {  // residual + bias, loaded while the out_proj MMA runs
-        const float4 bb = *reinterpret_cast<const float4*>(vec + C::V_BO + c0 + i);
-        const float4 xr = row_ok ? *reinterpret_cast<const float4*>(xin + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-        v[i] = bb.x + xr.x; v[i + 1] = bb.y + xr.y; v[i + 2] = bb.z + xr.z; v[i + 3] = bb.w + xr.w;
-      }
+      // ---- W5: x1 = (x + ctx.Wo^T, accumulated in TMEM) + bo, back into TMEM ; LN2 -> XA
       wait_w(SB_OP_DONE, par(step, 1, 0));
+      if (ok) tmem_ld32(trow + 384 + c0, v);
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        float t[16];
-        if (ok) tmem_ld16(trow + 384 + c0 + 16 * half, t);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v[16 * half + i] += t[i];
+      for (int i = 0; i < 32; i += 4) {
+        const float4 bb = *reinterpret_cast<const float4*>(vec + C::V_BO + c0 + i);
+        v[i] += bb.x; v[i + 1] += bb.y; v[i + 2] += bb.z; v[i + 3] += bb.w;
       }
       if (ok) tmem_st32(trow + 384 + c0, v);
       layer_norm(vec + C::V_LN2W, vec + C::V_LN2B);
@@ -504,14 +541,6 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
         const int b = c & 1;
         wait_w(SB_FIN + b, par(step, b ? per_b1 : per_b0, c >> 1));
         if (ok) tmem_ld32(trow + b * 128 + c0, v);
-        if (c == 0 && l == p.layers - 1) {
-          // pull the next sequence's rows toward L2 while the FFN runs
-          const int nseq = seq + static_cast<int>(gridDim.x);
-          if (nseq < p.num_seq && row_ok) {
-            const float* nx = p.x + (static_cast<int64_t>(nseq) * p.seq_len + r) * C::D + c0;
-            asm volatile("prefetch.global.L2 [%0];" ::"l"(nx) : "memory");
-          }
-        }
         const float* b1 = vec + C::V_BIN + c * 128 + c0;
 #pragma unroll
         for (int i = 0; i < 32; i += 4) {
@@ -526,36 +555,42 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
         store_sw128(smem + (b ? C::OFF_K : C::OFF_Q));
         publish(SB_H + b);
       }
-      // ---- W7: x2 = x1 + h.W2^T + b2 ; final LayerNorm (last layer) -> y
+      // ---- W7: x2 = (x1 + h.W2^T, accumulated in TMEM) + b2 ; final LayerNorm (last layer) -> y
       wait_w(SB_FOUT, par(step, 1, 0));
-      if (ok) tmem_ld32(trow + 256 + c0, v);
+      if (ok) tmem_ld32(trow + 384 + c0, v);
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        float x1[16];
-        if (ok) tmem_ld16(trow + 384 + c0 + 16 * half, x1);
-        const float* b2 = vec + C::V_BOUT + c0 + 16 * half;
-#pragma unroll
-        for (int i = 0; i < 16; i += 4) {
-          const float4 bb = *reinterpret_cast<const float4*>(b2 + i);
-          float* w = v + 16 * half + i;
-          w[0] += bb.x + x1[i]; w[1] += bb.y + x1[i + 1]; w[2] += bb.z + x1[i + 2]; w[3] += bb.w + x1[i + 3];
-        }
+      for (int i = 0; i < 32; i += 4) {
+        const float4 bb = *reinterpret_cast<const float4*>(vec + C::V_BOUT + c0 + i);
+        v[i] += bb.x; v[i + 1] += bb.y; v[i + 2] += bb.z; v[i + 3] += bb.w;
       }
-      if (l == p.layers - 1) layer_norm(vec + C::V_LNFW, vec + C::V_LNFB);
-      if (row_ok && ok) {
+      if (l == p.layers - 1) {
+        layer_norm(vec + C::V_LNFW, vec + C::V_LNFB);
         // padded rows of the model output are zero (with causal attention and prefix-valid
         // padding the valid rows never see a padded key, so only the output needs masking)
-        const bool zero = l == p.layers - 1 && p.row_valid != nullptr && p.row_valid[grow] == 0;
-        float* yo = p.y + grow * C::D + c0;
+        const bool zero = row_ok && p.row_valid != nullptr && p.row_valid[grow] == 0;
+        // this warp's 32x32 box of y (rows 32q.., columns c0..), staged SW128 and stored
+        // by TMA; rows past seq_len fall outside the tensor map and are not written
+        uint8_t* ybox = smem + C::OFF_YST + (q * 4 + g) * 4096;
 #pragma unroll
-        for (int i = 0; i < 32; i += 4)
-          *reinterpret_cast<float4*>(yo + i) =
-              zero ? make_float4(0.f, 0.f, 0.f, 0.f) : make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+        for (int j = 0; j < 8; ++j)
+          *reinterpret_cast<float4*>(ybox + sw128_off(lane, j)) =
+              zero ? make_float4(0.f, 0.f, 0.f, 0.f) : make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && ok) {
+          tma_store_3d(&tm_y, ybox, c0, 32 * q, seq);
+          bulk_commit();
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          *reinterpret_cast<float4*>(xin_row + sw128_off(r, j)) = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
       }
       // the next step's LN1 (which reuses the statistics buffers) must not race
       // this step's final row reduction
       named_bar(bar_id, 128);
     }
+    if (lane == 0) bulk_wait_all();  // the last y stores are complete before the CTA exits
   }
   tc_fence_before();
   __syncthreads();

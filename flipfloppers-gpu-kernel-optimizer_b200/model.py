@@ -162,7 +162,10 @@ class UserOptimizedTransformer(nn.Module):
 
     # ------------------------------------------------------------------ weights
     def _param_key(self, device) -> tuple:
-        return (device, tuple((id(p), p._version) for p in self.parameters()))
+        # Inference tensors (a model built under torch.inference_mode) carry no
+        # version counter; their identity and storage stand in for it.
+        return (device, tuple((id(p), p.data_ptr(), -1 if p.is_inference() else p._version)
+                              for p in self.parameters()))
 
     def _ensure_packs(self, device: torch.device) -> None:
         key = self._param_key(device)
@@ -547,6 +550,8 @@ class UserOptimizedTransformer(nn.Module):
             stream = torch.cuda.current_stream()
             tot = 0.0
             for it in range(steps + 3):
+                # device-side spin while the host enqueues the pair, so the events bracket the kernel only
+                torch.cuda._sleep(200_000)
                 if flush is not None:
                     flush.zero_()
                 a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -587,6 +592,7 @@ class UserOptimizedTransformer(nn.Module):
         tot = {k: 0.0 for k, _ in stages}
         for it in range(steps + 3):
             evs = []
+            torch.cuda._sleep(2_000_000)  # device-side spin covering the host enqueue of the stages
             for name, fn in stages:
                 if flush is not None:
                     flush.zero_()

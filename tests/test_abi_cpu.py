@@ -90,3 +90,15 @@ def test_cpu_tensor_raises_no_fallback(tt):
     m = tt.UserOptimizedTransformer(cfg)
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         m(torch.randn(1, 8, 64))
+
+
+def test_model_built_under_inference_mode_has_param_key():
+    """A model constructed inside torch.inference_mode (inference tensors, no
+    version counter) must still produce its weight-pack key."""
+    import torch
+    import torch_transformer_benchmark as T
+    with torch.inference_mode():
+        m = T.UserOptimizedTransformer(T.TransformerConfig(1, 8, 64, 2, 128, 1, True))
+        k1 = m._param_key(torch.device("cpu"))
+        k2 = m._param_key(torch.device("cpu"))
+    assert k1 == k2
