@@ -369,26 +369,39 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
       return fmaxf(fmaxf(buf[r], buf[128 + r]), fmaxf(buf[256 + r], buf[384 + r]));
     };
     // LayerNorm of v (32 columns of this row) in place, two-pass statistics
+    // (f32x2 pairs throughout: the statistics use 2 pair accumulators each)
     auto layer_norm = [&](const float* gamma, const float* beta) {  // gamma/beta: shared memory
-      float s4[4] = {0.f, 0.f, 0.f, 0.f};
+      uint64_t a0 = f2pk(0.f, 0.f), a1 = a0;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) s4[i & 3] += v[i];
-      const float mean = row_sum((s4[0] + s4[1]) + (s4[2] + s4[3]), st0) * (1.f / 128.f);
-      float q4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        v[i] -= mean;
-        q4[i & 3] += v[i] * v[i];
+      for (int i = 0; i < 32; i += 4) {
+        a0 = f2add(a0, f2pk(v[i], v[i + 1]));
+        a1 = f2add(a1, f2pk(v[i + 2], v[i + 3]));
       }
-      const float rstd = rsqrtf(row_sum((q4[0] + q4[1]) + (q4[2] + q4[3]), st1) * (1.f / 128.f) + p.eps);
+      float t0, t1, t2, t3;
+      f2upk(a0, t0, t1);
+      f2upk(a1, t2, t3);
+      const float mean = row_sum((t0 + t2) + (t1 + t3), st0) * (1.f / 128.f);
+      const uint64_t nm = f2pk(-mean, -mean);
+      a0 = f2pk(0.f, 0.f);
+      a1 = a0;
+#pragma unroll
+      for (int i = 0; i < 32; i += 4) {
+        const uint64_t d0 = f2add(f2pk(v[i], v[i + 1]), nm), d1 = f2add(f2pk(v[i + 2], v[i + 3]), nm);
+        a0 = f2fma(d0, d0, a0);
+        a1 = f2fma(d1, d1, a1);
+        f2upk(d0, v[i], v[i + 1]);
+        f2upk(d1, v[i + 2], v[i + 3]);
+      }
+      f2upk(a0, t0, t1);
+      f2upk(a1, t2, t3);
+      const float rstd = rsqrtf(row_sum((t0 + t2) + (t1 + t3), st1) * (1.f / 128.f) + p.eps);
+      const uint64_t rs = f2pk(rstd, rstd);
 #pragma unroll
       for (int i = 0; i < 32; i += 4) {
         const float4 gg = *reinterpret_cast<const float4*>(gamma + c0 + i);
         const float4 bb = *reinterpret_cast<const float4*>(beta + c0 + i);
-        v[i] = v[i] * rstd * gg.x + bb.x;
-        v[i + 1] = v[i + 1] * rstd * gg.y + bb.y;
-        v[i + 2] = v[i + 2] * rstd * gg.z + bb.z;
-        v[i + 3] = v[i + 3] * rstd * gg.w + bb.w;
+        f2upk(f2fma(f2mul(f2pk(v[i], v[i + 1]), rs), f2pk(gg.x, gg.y), f2pk(bb.x, bb.y)), v[i], v[i + 1]);
+        f2upk(f2fma(f2mul(f2pk(v[i + 2], v[i + 3]), rs), f2pk(gg.z, gg.w), f2pk(bb.z, bb.w)), v[i + 2], v[i + 3]);
       }
     };
     // 32 fp16 values of this row at column c0 of a 128-wide SW128 K-major tile (2 atoms of 64)
@@ -466,24 +479,19 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
 #pragma unroll 1
       for (int nt = 0; nt < 3; ++nt) {
         if (ok) tmem_ld32(trow + nt * 128 + c0, v);
-        const float* bq = vec + C::V_BQKV + nt * 128 + c0;
-#pragma unroll
-        for (int i = 0; i < 32; i += 4) {
-          const float4 bb = *reinterpret_cast<const float4*>(bq + i);
-          v[i] += bb.x; v[i + 1] += bb.y; v[i + 2] += bb.z; v[i + 3] += bb.w;
-        }
+        f2_add_bias32(v, vec + C::V_BQKV + nt * 128 + c0);
         store_sw64(smem + (nt == 0 ? C::OFF_Q : nt == 1 ? C::OFF_K : C::OFF_V) + g * 8192);
       }
       publish(SB_QKV_SMEM);
       // ---- W3: softmax per head (this thread: row r, keys c0..c0+31)
-      // bit i: key c0+i exists and is not padding (the causal bound is applied per row below)
-      uint32_t kvalid = 0;
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int k = c0 + i;
-        const bool v_ok = k < p.seq_len &&
-                          (p.row_valid == nullptr || p.row_valid[static_cast<int64_t>(seq) * p.seq_len + k] != 0);
-        kvalid |= (v_ok ? 1u : 0u) << i;
+      // bit i: key c0+i exists and is not padding (the causal bound is applied per row below);
+      // lane i of the warp tests key c0+i (one coalesced byte load) and the ballot gathers them
+      uint32_t kvalid;
+      {
+        const int k = c0 + lane;
+        bool v_ok = k < p.seq_len;
+        if (v_ok && p.row_valid != nullptr) v_ok = p.row_valid[static_cast<int64_t>(seq) * p.seq_len + k] != 0;
+        kvalid = __ballot_sync(0xffffffffu, v_ok);
       }
       if (!p.non_causal) kvalid &= (r >= c0 + 31) ? 0xffffffffu : (r < c0 ? 0u : (0xffffffffu >> (31 - (r - c0))));
       float my_l = 1.f;  // softmax denominator of head g (this thread's head in the context step)
@@ -491,21 +499,30 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
       for (int h = 0; h < 4; ++h) {
         wait_w(SB_S_FULL + (h & 1), par(step, 2, h >> 1));
         if (ok) tmem_ld32(trow + (h & 1) * 128 + c0, v);
+        if (kvalid != 0xffffffffu) {  // raw scores; the positive scale is applied in the exponent
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (!((kvalid >> i) & 1u)) v[i] = -INFINITY;
+        }
         float mx = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {  // raw scores; the positive scale is applied in the exponent
-          if (!((kvalid >> i) & 1u)) v[i] = -INFINITY;
-          mx = fmaxf(mx, v[i]);
-        }
+        for (int i = 0; i < 32; i += 2) mx = fmax3(mx, v[i], v[i + 1]);
         const float m = row_max(mx, st0) * p.scale_log2;  // reductions alternate st0/st1 strictly
-        float s4[4] = {0.f, 0.f, 0.f, 0.f};
+        const uint64_t sc = f2pk(p.scale_log2, p.scale_log2), nm = f2pk(-m, -m);
+        uint64_t a0 = f2pk(0.f, 0.f), a1 = a0;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float e = fast_exp2(fmaf(v[i], p.scale_log2, -m));
-          v[i] = e;
-          s4[i & 3] += e;
+        for (int i = 0; i < 32; i += 4) {
+          float e0, e1, e2, e3;
+          f2upk(f2fma(f2pk(v[i], v[i + 1]), sc, nm), e0, e1);
+          f2upk(f2fma(f2pk(v[i + 2], v[i + 3]), sc, nm), e2, e3);
+          v[i] = fast_exp2(e0); v[i + 1] = fast_exp2(e1); v[i + 2] = fast_exp2(e2); v[i + 3] = fast_exp2(e3);
+          a0 = f2add(a0, f2pk(v[i], v[i + 1]));
+          a1 = f2add(a1, f2pk(v[i + 2], v[i + 3]));
         }
-        const float sum = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+        float t0, t1, t2, t3;
+        f2upk(a0, t0, t1);
+        f2upk(a1, t2, t3);
+        const float sum = (t0 + t2) + (t1 + t3);
         // P of the previous head must have been consumed before P is overwritten
         if (h > 0) wait_w(SB_PV_DONE, par(step, 4, h - 1));
         store_sw128(smem + C::OFF_P);
@@ -518,19 +535,16 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
       if (ok) tmem_ld32(trow + 256 + c0, v);
       {
         const float inv = 1.f / my_l;
+        const uint64_t iv = f2pk(inv, inv);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] *= inv;
+        for (int i = 0; i < 32; i += 2) f2upk(f2mul(f2pk(v[i], v[i + 1]), iv), v[i], v[i + 1]);
       }
       store_sw128(xa);
       publish(SB_CTX);
       // ---- W5: x1 = (x + ctx.Wo^T, accumulated in TMEM) + bo, back into TMEM ; LN2 -> XA
       wait_w(SB_OP_DONE, par(step, 1, 0));
       if (ok) tmem_ld32(trow + 384 + c0, v);
-#pragma unroll
-      for (int i = 0; i < 32; i += 4) {
-        const float4 bb = *reinterpret_cast<const float4*>(vec + C::V_BO + c0 + i);
-        v[i] += bb.x; v[i + 1] += bb.y; v[i + 2] += bb.z; v[i + 3] += bb.w;
-      }
+      f2_add_bias32(v, vec + C::V_BO + c0);
       if (ok) tmem_st32(trow + 384 + c0, v);
       layer_norm(vec + C::V_LN2W, vec + C::V_LN2B);
       store_sw128(xa);
@@ -541,15 +555,9 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
         const int b = c & 1;
         wait_w(SB_FIN + b, par(step, b ? per_b1 : per_b0, c >> 1));
         if (ok) tmem_ld32(trow + b * 128 + c0, v);
-        const float* b1 = vec + C::V_BIN + c * 128 + c0;
+        f2_add_bias32(v, vec + C::V_BIN + c * 128 + c0);
 #pragma unroll
-        for (int i = 0; i < 32; i += 4) {
-          const float4 bb = *reinterpret_cast<const float4*>(b1 + i);
-          v[i] = gelu_as(v[i] + bb.x);
-          v[i + 1] = gelu_as(v[i + 1] + bb.y);
-          v[i + 2] = gelu_as(v[i + 2] + bb.z);
-          v[i + 3] = gelu_as(v[i + 3] + bb.w);
-        }
+        for (int i = 0; i < 32; i += 2) gelu_as2(v[i], v[i + 1]);
         // the buffer's previous chunk (c-2) must have been consumed by ffn_out
         if (c >= 2) wait_w(SB_HFREE + b, par(step, b ? per_b1 : per_b0, (c >> 1) - 1));
         store_sw128(smem + (b ? C::OFF_K : C::OFF_Q));
@@ -558,11 +566,7 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
       // ---- W7: x2 = (x1 + h.W2^T, accumulated in TMEM) + b2 ; final LayerNorm (last layer) -> y
       wait_w(SB_FOUT, par(step, 1, 0));
       if (ok) tmem_ld32(trow + 384 + c0, v);
-#pragma unroll
-      for (int i = 0; i < 32; i += 4) {
-        const float4 bb = *reinterpret_cast<const float4*>(vec + C::V_BOUT + c0 + i);
-        v[i] += bb.x; v[i + 1] += bb.y; v[i + 2] += bb.z; v[i + 3] += bb.w;
-      }
+      f2_add_bias32(v, vec + C::V_BOUT + c0);
       if (l == p.layers - 1) {
         layer_norm(vec + C::V_LNFW, vec + C::V_LNFB);
         // padded rows of the model output are zero (with causal attention and prefix-valid

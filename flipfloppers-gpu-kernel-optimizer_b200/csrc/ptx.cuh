@@ -115,10 +115,12 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) 
 
 // Warp-uniform variant: every lane polls, the warp proceeds only if all lanes
 // saw the phase complete (a .sync.aligned tcgen05 op follows most waits).
+// (Measured: polling by lane 0 alone plus a broadcast is slower.)
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int code) {
   bool ok = mbar_wait(bar, parity, abort_flag, code);
   return __all_sync(0xffffffffu, ok);
 }
+
 
 // ---------------------------------------------------------------- fences
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -315,6 +317,74 @@ __device__ __forceinline__ float gelu_as(float v) {
   const float e = copysignf(1.0f - fast_rcp(q), v);  // erf(v / sqrt(2))
   const float hv = 0.5f * v;
   return fmaf(hv, e, hv);
+}
+
+// ---------------------------------------------------------------- packed fp32 pairs
+// sm_100 f32x2 arithmetic: one instruction for two fp32 lanes.  The FMA pipe's
+// lane throughput is unchanged, but the issue slots are halved, which is what
+// bounds the per-row elementwise phases of the fused kernel.
+__device__ __forceinline__ uint64_t f2pk(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2upk(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+// v[i] += b[i] for 32 values, b 16-byte aligned (shared memory)
+__device__ __forceinline__ void f2_add_bias32(float (&v)[32], const float* b) {
+#pragma unroll
+  for (int i = 0; i < 32; i += 4) {
+    const float4 bb = *reinterpret_cast<const float4*>(b + i);
+    const uint64_t lo = f2add(f2pk(v[i], v[i + 1]), f2pk(bb.x, bb.y));
+    const uint64_t hi = f2add(f2pk(v[i + 2], v[i + 3]), f2pk(bb.z, bb.w));
+    f2upk(lo, v[i], v[i + 1]);
+    f2upk(hi, v[i + 2], v[i + 3]);
+  }
+}
+// three-input maximum (sm_100)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// gelu_as on two values: the same operations, with the squarings, the 0.5*v
+// scaling and the final FMA done as f32x2 pairs (Horner stays scalar so its
+// coefficients remain immediates).
+__device__ __forceinline__ void gelu_as2(float& v0, float& v1) {
+  float q0 = 4.30638e-5f, q1 = 4.30638e-5f;
+  const float u0 = fabsf(v0) * 0.70710678118654752440f, u1 = fabsf(v1) * 0.70710678118654752440f;
+  q0 = fmaf(q0, u0, 2.765672e-4f);  q1 = fmaf(q1, u1, 2.765672e-4f);
+  q0 = fmaf(q0, u0, 1.520143e-4f);  q1 = fmaf(q1, u1, 1.520143e-4f);
+  q0 = fmaf(q0, u0, 9.2705272e-3f); q1 = fmaf(q1, u1, 9.2705272e-3f);
+  q0 = fmaf(q0, u0, 4.22820123e-2f); q1 = fmaf(q1, u1, 4.22820123e-2f);
+  q0 = fmaf(q0, u0, 7.05230784e-2f); q1 = fmaf(q1, u1, 7.05230784e-2f);
+  q0 = fmaf(q0, u0, 1.0f);          q1 = fmaf(q1, u1, 1.0f);
+  uint64_t q = f2pk(q0, q1);
+  q = f2mul(q, q);
+  q = f2mul(q, q);
+  q = f2mul(q, q);
+  q = f2mul(q, q);  // (1 + a1 u + ... )^16 per lane
+  f2upk(q, q0, q1);
+  const float e0 = copysignf(1.0f - fast_rcp(q0), v0), e1 = copysignf(1.0f - fast_rcp(q1), v1);
+  const uint64_t hv = f2mul(f2pk(v0, v1), f2pk(0.5f, 0.5f));
+  f2upk(f2fma(hv, f2pk(e0, e1), hv), v0, v1);
 }
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
