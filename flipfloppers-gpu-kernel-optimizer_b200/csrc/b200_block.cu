@@ -135,6 +135,20 @@ int make_map_f16(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols,
   return r == CUDA_SUCCESS ? B200_OK : B200_ERR_TMAP;
 }
 
+// [rows, cols] row-major matrix (leading dimension ld elements) as a 2-D map
+// with boxes of box_cols x box_rows.
+int make_map_2d(CUtensorMap* m, CUtensorMapDataType dt, uint32_t esize, const void* base, uint64_t rows,
+                uint64_t cols, uint64_t ld, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle sw) {
+  if (ensure_encode() != B200_OK) return B200_ERR_TMAP;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * esize};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? B200_OK : B200_ERR_TMAP;
+}
+
 // [num_seq, seq_len, cols] fp32 activations as a 3-D map with SWIZZLE_128B
 // boxes of 32 columns x box_rows rows x 1 sequence: rows past seq_len are
 // zero-filled on load and not written on store, so a box never reaches into
@@ -154,23 +168,25 @@ int make_map_f32_seq(CUtensorMap* m, const void* base, uint64_t num_seq, uint64_
 
 // ------------------------------------------------------------------ GEMM
 template <int BN, int STAGES, int EPI>
-int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p, cudaStream_t st) {
+int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const GemmParams& p,
+                  cudaStream_t st) {
   auto kern = k_gemm_tn<BN, STAGES, EPI>;
   const int smem = GemmSmem<BN, STAGES>::TOTAL;
   if (int rc = set_smem(reinterpret_cast<const void*>(kern), smem)) return rc;
   const long long tiles = static_cast<long long>((p.M + 127) / 128) * ((p.N + BN - 1) / BN);
   const int grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
-  kern<<<grid, GEMM_THREADS, smem, st>>>(ta, tw, p);
+  kern<<<grid, GEMM_THREADS, smem, st>>>(ta, tw, to, p);
   return launch_status();
 }
 
 template <int BN, int STAGES>
-int launch_gemm_bn(int epi, const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p, cudaStream_t st) {
+int launch_gemm_bn(int epi, const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const GemmParams& p,
+                   cudaStream_t st) {
   switch (epi) {
-    case EPI_BIAS_F16: return launch_gemm_t<BN, STAGES, EPI_BIAS_F16>(ta, tw, p, st);
-    case EPI_BIAS_GELU_F16: return launch_gemm_t<BN, STAGES, EPI_BIAS_GELU_F16>(ta, tw, p, st);
-    case EPI_BIAS_RESID_F32: return launch_gemm_t<BN, STAGES, EPI_BIAS_RESID_F32>(ta, tw, p, st);
-    case EPI_BIAS_F32: return launch_gemm_t<BN, STAGES, EPI_BIAS_F32>(ta, tw, p, st);
+    case EPI_BIAS_F16: return launch_gemm_t<BN, STAGES, EPI_BIAS_F16>(ta, tw, to, p, st);
+    case EPI_BIAS_GELU_F16: return launch_gemm_t<BN, STAGES, EPI_BIAS_GELU_F16>(ta, tw, to, p, st);
+    case EPI_BIAS_RESID_F32: return launch_gemm_t<BN, STAGES, EPI_BIAS_RESID_F32>(ta, tw, to, p, st);
+    case EPI_BIAS_F32: return launch_gemm_t<BN, STAGES, EPI_BIAS_F32>(ta, tw, to, p, st);
     default: return B200_ERR_CONFIG;
   }
 }
@@ -200,61 +216,78 @@ int gemm_impl(int epi, const void* A, long long lda, const void* W, long long ld
   CUtensorMap ta, tw;
   if (int rc = make_map_f16(&ta, A, M, K, lda, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
   if (int rc = make_map_f16(&tw, W, N, K, ldw, 64, BN, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
+  // the epilogue writes 64-byte rows of 32-row boxes (SWIZZLE_64B): 32 fp16 or 16 fp32 columns
+  CUtensorMap to;
+  if (f32_out) {
+    if (int rc = make_map_2d(&to, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, out, M, N, ld_out, 16, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+      return rc;
+  } else {
+    if (int rc = make_map_2d(&to, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, out, M, N, ld_out, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+      return rc;
+  }
+  // the residual epilogue adds onto `out` in place (TMA add-reduce); a distinct
+  // residual is copied into `out` first
+  if (epi == EPI_BIAS_RESID_F32 && (resid != out || ld_resid != ld_out)) {
+    const cudaError_t e = cudaMemcpy2DAsync(out, static_cast<size_t>(ld_out) * 4, resid, static_cast<size_t>(ld_resid) * 4,
+                                            static_cast<size_t>(N) * 4, static_cast<size_t>(M), cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return B200_ERR_LAUNCH;
+    }
+  }
   GemmParams p{};
   p.M = M;
   p.N = N;
   p.K = K;
   p.a_row0 = 0;
   p.bias = bias;
-  p.resid = resid;
-  p.ld_resid = ld_resid;
-  p.out = out;
-  p.ld_out = ld_out;
-  if (BN == 256) return launch_gemm_bn<256, 4>(epi, ta, tw, p, st);
-  return launch_gemm_bn<128, 6>(epi, ta, tw, p, st);
+  if (BN == 256) return launch_gemm_bn<256, 4>(epi, ta, tw, to, p, st);
+  return launch_gemm_bn<128, 6>(epi, ta, tw, to, p, st);
 }
 
 // ------------------------------------------------------------------ LayerNorm
 template <int VPL, bool VEC4>
 int launch_ln_t(const float* x, long long ldx, const float* g, const float* b, void* out, long long ldo, bool f16,
-                int rows, int d, float eps, cudaStream_t st) {
+                int rows, int d, float eps, float* copy, long long ldc, cudaStream_t st) {
   const int warps = 8;
   dim3 grid((rows + warps - 1) / warps);
   if (f16)
-    k_layernorm<VPL, VEC4, true><<<grid, 32 * warps, 0, st>>>(x, ldx, g, b, out, ldo, rows, d, eps);
+    k_layernorm<VPL, VEC4, true><<<grid, 32 * warps, 0, st>>>(x, ldx, g, b, out, ldo, rows, d, eps, copy, ldc);
   else
-    k_layernorm<VPL, VEC4, false><<<grid, 32 * warps, 0, st>>>(x, ldx, g, b, out, ldo, rows, d, eps);
+    k_layernorm<VPL, VEC4, false><<<grid, 32 * warps, 0, st>>>(x, ldx, g, b, out, ldo, rows, d, eps, copy, ldc);
   return launch_status();
 }
 
+// copy (may be null): fp32 copy of x's rows, leading dimension ldc
 int ln_impl(const float* x, long long ldx, const float* g, const float* b, void* out, long long ldo, int f16,
-            int rows, int d, float eps, cudaStream_t st) {
+            int rows, int d, float eps, cudaStream_t st, float* copy = nullptr, long long ldc = 0) {
   if (!x || !g || !b || !out || rows < 0 || d <= 0) return B200_ERR_ARG;
   if (rows == 0) return B200_OK;
-  if (d % 32 || d > 4096 || ldx < d || ldo < d) return B200_ERR_TILE;
+  if (d % 32 || d > 4096 || ldx < d || ldo < d || (copy && ldc < d)) return B200_ERR_TILE;
   if (int rc = check_arch()) return rc;
-  if (d % 128 == 0 && ldx % 4 == 0 && ldo % 4 == 0 && al16(x) && al16(out) && al16(g) && al16(b)) {
+  if (d % 128 == 0 && ldx % 4 == 0 && ldo % 4 == 0 && al16(x) && al16(out) && al16(g) && al16(b) &&
+      (!copy || (ldc % 4 == 0 && al16(copy)))) {
     switch (d / 128) {
-      case 1: return launch_ln_t<1, true>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
-      case 2: return launch_ln_t<2, true>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
-      case 4: return launch_ln_t<4, true>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
-      case 8: return launch_ln_t<8, true>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
-      case 16: return launch_ln_t<16, true>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
-      case 32: return launch_ln_t<32, true>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
+      case 1: return launch_ln_t<1, true>(x, ldx, g, b, out, ldo, f16, rows, d, eps, copy, ldc, st);
+      case 2: return launch_ln_t<2, true>(x, ldx, g, b, out, ldo, f16, rows, d, eps, copy, ldc, st);
+      case 4: return launch_ln_t<4, true>(x, ldx, g, b, out, ldo, f16, rows, d, eps, copy, ldc, st);
+      case 8: return launch_ln_t<8, true>(x, ldx, g, b, out, ldo, f16, rows, d, eps, copy, ldc, st);
+      case 16: return launch_ln_t<16, true>(x, ldx, g, b, out, ldo, f16, rows, d, eps, copy, ldc, st);
+      case 32: return launch_ln_t<32, true>(x, ldx, g, b, out, ldo, f16, rows, d, eps, copy, ldc, st);
       default: break;
     }
   }
   switch (d / 32) {
-    case 1: return launch_ln_t<1, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
-    case 2: return launch_ln_t<2, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
-    case 3: return launch_ln_t<3, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
-    case 4: return launch_ln_t<4, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
-    case 6: return launch_ln_t<6, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
-    case 8: return launch_ln_t<8, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
-    case 12: return launch_ln_t<12, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
-    case 16: return launch_ln_t<16, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
-    case 24: return launch_ln_t<24, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
-    case 32: return launch_ln_t<32, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, st);
+    case 1: return launch_ln_t<1, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, copy, ldc, st);
+    case 2: return launch_ln_t<2, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, copy, ldc, st);
+    case 3: return launch_ln_t<3, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, copy, ldc, st);
+    case 4: return launch_ln_t<4, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, copy, ldc, st);
+    case 6: return launch_ln_t<6, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, copy, ldc, st);
+    case 8: return launch_ln_t<8, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, copy, ldc, st);
+    case 12: return launch_ln_t<12, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, copy, ldc, st);
+    case 16: return launch_ln_t<16, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, copy, ldc, st);
+    case 24: return launch_ln_t<24, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, copy, ldc, st);
+    case 32: return launch_ln_t<32, false>(x, ldx, g, b, out, ldo, f16, rows, d, eps, copy, ldc, st);
     default: return B200_ERR_TILE;
   }
 }
@@ -507,8 +540,11 @@ int block_impl(const B200BlockArgs* a, cudaStream_t st) {
   if (!a->workspace || a->workspace_bytes < w.bytes) return B200_ERR_WORKSPACE;
   if (!al16(a->workspace)) return B200_ERR_ALIGN;
   int rc;
-  // 1. n = LN1(x) (fp16)
-  if ((rc = ln_impl(a->x, d, a->ln1_w, a->ln1_b, w.n, d, 1, static_cast<int>(M), d, a->eps, st))) return rc;
+  // residual stream: x1 (final norm follows) or y itself; the projection GEMMs
+  // add onto it in place
+  float* res = a->lnf_w ? w.x1 : a->y;
+  // 1. n = LN1(x) (fp16), res = x
+  if ((rc = ln_impl(a->x, d, a->ln1_w, a->ln1_b, w.n, d, 1, static_cast<int>(M), d, a->eps, st, res, d))) return rc;
   // 2. qkv = n . Wqkv^T + bqkv
   if ((rc = gemm_impl(EPI_BIAS_F16, w.n, d, a->w_qkv, d, a->b_qkv, nullptr, 0, w.qkv, 3 * d, static_cast<int>(M),
                       3 * d, d, st)))
@@ -535,19 +571,18 @@ int block_impl(const B200BlockArgs* a, cudaStream_t st) {
   at.non_causal = a->non_causal;
   at.kv_lens = a->kv_lens;
   if ((rc = attn_impl(&at, st))) return rc;
-  // 4. x1 = x + ctx . Wo^T + bo
-  if ((rc = gemm_impl(EPI_BIAS_RESID_F32, w.ctx, d, a->w_o, d, a->b_o, a->x, d, w.x1, d, static_cast<int>(M), d, d,
+  // 4. x1 = x + ctx . Wo^T + bo  (res += ...)
+  if ((rc = gemm_impl(EPI_BIAS_RESID_F32, w.ctx, d, a->w_o, d, a->b_o, res, d, res, d, static_cast<int>(M), d, d,
                       st)))
     return rc;
   // 5. n = LN2(x1)
-  if ((rc = ln_impl(w.x1, d, a->ln2_w, a->ln2_b, w.n, d, 1, static_cast<int>(M), d, a->eps, st))) return rc;
+  if ((rc = ln_impl(res, d, a->ln2_w, a->ln2_b, w.n, d, 1, static_cast<int>(M), d, a->eps, st))) return rc;
   // 6. h = gelu(n . W1^T + b1)
   if ((rc = gemm_impl(EPI_BIAS_GELU_F16, w.n, d, a->w_in, d, a->b_in, nullptr, 0, w.h, F, static_cast<int>(M), F, d,
                       st)))
     return rc;
-  // 7. x2 = x1 + h . W2^T + b2 (in place in x1, or straight into y without a final norm)
-  float* x2 = a->lnf_w ? w.x1 : a->y;
-  if ((rc = gemm_impl(EPI_BIAS_RESID_F32, w.h, F, a->w_out, F, a->b_out, w.x1, d, x2, d, static_cast<int>(M), d, F,
+  // 7. x2 = x1 + h . W2^T + b2  (res += ...; without a final norm res is y)
+  if ((rc = gemm_impl(EPI_BIAS_RESID_F32, w.h, F, a->w_out, F, a->b_out, res, d, res, d, static_cast<int>(M), d, F,
                       st)))
     return rc;
   // 8. y = LN_f(x2)
@@ -618,7 +653,8 @@ int block_chunked_impl(const B200BlockArgs* a, int chunk_rows, cudaStream_t st) 
       const long long row0 = static_cast<long long>(b) * S + c0;
       const float* xr = a->x + row0 * d;
       float* yr = a->y + row0 * d;
-      if ((rc = ln_impl(xr, d, a->ln1_w, a->ln1_b, w.n, d, 1, Rc, d, a->eps, st))) return rc;
+      float* res = a->lnf_w ? w.x1 : yr;  // the chunk's residual stream
+      if ((rc = ln_impl(xr, d, a->ln1_w, a->ln1_b, w.n, d, 1, Rc, d, a->eps, st, res, d))) return rc;
       // q rows of the fused QKV weight -> chunk buffer; k|v rows -> the cache at this chunk's rows
       if ((rc = gemm_impl(EPI_BIAS_F16, w.n, d, wq, d, a->b_qkv, nullptr, 0, w.q, d, Rc, d, d, st))) return rc;
       if ((rc = gemm_impl(EPI_BIAS_F16, w.n, d, wq + static_cast<size_t>(d) * d, d, a->b_qkv + d, nullptr, 0,
@@ -651,11 +687,10 @@ int block_chunked_impl(const B200BlockArgs* a, int chunk_rows, cudaStream_t st) 
       at.out_seq_rows = Rc;
       at.out_row0 = 0;
       if ((rc = attn_impl(&at, st))) return rc;
-      if ((rc = gemm_impl(EPI_BIAS_RESID_F32, w.ctx, d, a->w_o, d, a->b_o, xr, d, w.x1, d, Rc, d, d, st))) return rc;
-      if ((rc = ln_impl(w.x1, d, a->ln2_w, a->ln2_b, w.n, d, 1, Rc, d, a->eps, st))) return rc;
+      if ((rc = gemm_impl(EPI_BIAS_RESID_F32, w.ctx, d, a->w_o, d, a->b_o, res, d, res, d, Rc, d, d, st))) return rc;
+      if ((rc = ln_impl(res, d, a->ln2_w, a->ln2_b, w.n, d, 1, Rc, d, a->eps, st))) return rc;
       if ((rc = gemm_impl(EPI_BIAS_GELU_F16, w.n, d, a->w_in, d, a->b_in, nullptr, 0, w.h, F, Rc, F, d, st))) return rc;
-      float* x2 = a->lnf_w ? w.x1 : yr;
-      if ((rc = gemm_impl(EPI_BIAS_RESID_F32, w.h, F, a->w_out, F, a->b_out, w.x1, d, x2, d, Rc, d, F, st))) return rc;
+      if ((rc = gemm_impl(EPI_BIAS_RESID_F32, w.h, F, a->w_out, F, a->b_out, res, d, res, d, Rc, d, F, st))) return rc;
       if (a->lnf_w && (rc = ln_impl(w.x1, d, a->lnf_w, a->lnf_b, yr, d, 0, Rc, d, a->eps, st))) return rc;
     }
   }
@@ -710,6 +745,14 @@ int b200_device_error(int clear) {
 int b200_layernorm_launch(const float* x, long long ld_x, const float* gamma, const float* beta, void* out,
                           long long ld_out, int out_f16, int rows, int d, float eps, b200_stream_t stream) {
   return ln_impl(x, ld_x, gamma, beta, out, ld_out, out_f16, rows, d, eps, static_cast<cudaStream_t>(stream));
+}
+
+int b200_layernorm_residual_launch(const float* x, long long ld_x, const float* gamma, const float* beta, void* out,
+                                   long long ld_out, int out_f16, float* residual_out, long long ld_residual,
+                                   int rows, int d, float eps, b200_stream_t stream) {
+  if (!residual_out) return B200_ERR_ARG;
+  return ln_impl(x, ld_x, gamma, beta, out, ld_out, out_f16, rows, d, eps, static_cast<cudaStream_t>(stream),
+                 residual_out, ld_residual);
 }
 
 int b200_add_layernorm_launch(const float* a, const float* b, const float* bias, float* sum_out, const float* gamma,

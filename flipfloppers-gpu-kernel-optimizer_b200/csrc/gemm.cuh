@@ -4,8 +4,9 @@
 // TMEM; fp32 bias.  Epilogues:
 //   EPI_BIAS_F16       fp16 out            (QKV projection, reference TTB:1303)
 //   EPI_BIAS_GELU_F16  fp16 gelu(.)        (ffn_in + exact GELU, TTB:1350-1354)
-//   EPI_BIAS_RESID_F32 fp32 out = resid+.  (out_proj / ffn_out + residual,
-//                                           TTB:1333-1339, 1368-1369)
+//   EPI_BIAS_RESID_F32 fp32 out += .       (out_proj / ffn_out + residual,
+//                                           TTB:1333-1339, 1368-1369; `out`
+//                                           holds the residual on entry)
 //   EPI_BIAS_F32       fp32 out            (row-parallel partial sums before
 //                                           the tensor-parallel all-reduce)
 // It replaces the reference's mma.sync GEMM `ws_gemm_kernel`
@@ -17,7 +18,13 @@
 //   warp 1     TMEM owner and tcgen05.mma issuer (one lane), accumulating tile
 //              i into TMEM buffer i%2 while the epilogue drains buffer (i-1)%2;
 //   warps 2-9  epilogue: warp w reads TMEM lane quadrant w%4 (one output row
-//              per thread) and half (w-2)/4 of the tile's columns.
+//              per thread) and half (w-2)/4 of the tile's columns, in chunks of
+//              64 bytes per row (32 fp16 or 16 fp32 columns).  Each chunk is
+//              staged as a 32-row SWIZZLE_64B box in one of the warp's two
+//              2 KB shared-memory slots and written by a TMA store -- or, for
+//              the residual epilogue, a TMA add-reduce into `out`, which then
+//              already holds the residual.  Per-thread stores of a row would
+//              touch 32 rows per warp instruction.
 #pragma once
 
 #include "ptx.cuh"
@@ -30,10 +37,6 @@ struct GemmParams {
   int M, N, K;
   int a_row0;            // first row of A addressed by the tensor map (row offset of this call)
   const float* bias;     // [N] fp32, may be null
-  const float* resid;    // [M, ld_resid] fp32 (EPI_BIAS_RESID_F32)
-  int64_t ld_resid;
-  void* out;             // [M, ld_out], fp16 or fp32
-  int64_t ld_out;
 };
 
 template <int BN, int STAGES>
@@ -41,7 +44,8 @@ struct GemmSmem {
   static constexpr int A_BYTES = 128 * 64 * 2;
   static constexpr int B_BYTES = BN * 64 * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+  static constexpr int STG_OFF = STAGES * STAGE_BYTES;  // epilogue staging: 8 warps x 2 slots x 2 KB
+  static constexpr int BAR_OFF = STG_OFF + 8 * 4096;
   static constexpr int TOTAL = BAR_OFF + 256 + 1024;  // barriers + 1 KB alignment slack
 };
 
@@ -49,7 +53,8 @@ constexpr int GEMM_THREADS = 320;  // producer, MMA, 8 epilogue warps
 
 template <int BN, int STAGES, int EPI>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
-    k_gemm_tn(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW, const GemmParams p) {
+    k_gemm_tn(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+              const __grid_constant__ CUtensorMap tmO, const GemmParams p) {
   using L = GemmSmem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_align1024(smem_raw);
@@ -153,60 +158,72 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     // epilogue warps 2..9
     const int q = warp & 3;
     const int half = (warp - 2) >> 2;
-    constexpr int CW = BN / 2;  // columns per epilogue thread
+    constexpr int CW = BN / 2;                                            // columns per warp per tile
+    constexpr bool F32 = EPI == EPI_BIAS_RESID_F32 || EPI == EPI_BIAS_F32;
+    constexpr int CC = F32 ? 16 : 32;                                     // columns per 64-byte chunk row
+    uint8_t* stg = smem + L::STG_OFF + (warp - 2) * 4096;                 // two 2 KB slots
+    const uint32_t sw = static_cast<uint32_t>((lane >> 1) & 3);           // SWIZZLE_64B phase of row `lane`
+    if (lane == 0) tma_prefetch_desc(&tmO);
+    int gc = 0;  // chunks this warp has staged
     for (int i = 0; i < my_tiles; ++i) {
       const int b = i & 1;
       const int t = static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x);
       const int m0 = (t % mt) * 128, n0 = (t / mt) * BN;
-      const int row = m0 + q * 32 + lane;
       const bool ok = mbar_wait_warp(&acc_full[b], (i >> 1) & 1, abort_flag, DERR_WAIT_MMA);
       if (!ok || *abort_flag) break;
       tc_fence_after();
 #pragma unroll 1
-      for (int c = half * CW; c < (half + 1) * CW; c += 32) {
-        float v[32];
-        tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + b * BN + c, v);
+      for (int c = half * CW; c < (half + 1) * CW; c += CC, ++gc) {
+        const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + b * BN + c;
         const int col = n0 + c;
-        if (row < p.M && col < p.N) {
-          if (p.bias != nullptr) {
+        uint8_t* slot = stg + (gc & 1) * 2048;
+        uint32_t w[16];  // the chunk's 64 bytes of this row
+        if constexpr (F32) {
+          float v[16];
+          tmem_ld16(taddr, v);
+          if (p.bias != nullptr && col < p.N) {
             const float4* b4 = reinterpret_cast<const float4*>(p.bias + col);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
+            for (int j = 0; j < 4; ++j) {
               const float4 bb = __ldg(b4 + j);
-              v[4 * j + 0] += bb.x;
-              v[4 * j + 1] += bb.y;
-              v[4 * j + 2] += bb.z;
-              v[4 * j + 3] += bb.w;
+              v[4 * j] += bb.x; v[4 * j + 1] += bb.y; v[4 * j + 2] += bb.z; v[4 * j + 3] += bb.w;
             }
           }
-          if constexpr (EPI == EPI_BIAS_RESID_F32) {
-            const float4* r4 = reinterpret_cast<const float4*>(p.resid + static_cast<int64_t>(row) * p.ld_resid + col);
-            float4* o4 = reinterpret_cast<float4*>(static_cast<float*>(p.out) + static_cast<int64_t>(row) * p.ld_out + col);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const float4 r = r4[j];
-              o4[j] = make_float4(v[4 * j] + r.x, v[4 * j + 1] + r.y, v[4 * j + 2] + r.z, v[4 * j + 3] + r.w);
-            }
-          } else if constexpr (EPI == EPI_BIAS_F32) {
-            float4* o4 = reinterpret_cast<float4*>(static_cast<float*>(p.out) + static_cast<int64_t>(row) * p.ld_out + col);
+          for (int j = 0; j < 16; ++j) w[j] = __float_as_uint(v[j]);
+        } else {
+          float v[32];
+          tmem_ld32(taddr, v);
+          if (p.bias != nullptr && col < p.N) f2_add_bias32_global(v, p.bias + col);
+          if constexpr (EPI == EPI_BIAS_GELU_F16) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) o4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-          } else {
-            if constexpr (EPI == EPI_BIAS_GELU_F16) {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = gelu_as(v[j]);
-            }
-            uint4* o4 = reinterpret_cast<uint4*>(static_cast<__half*>(p.out) + static_cast<int64_t>(row) * p.ld_out + col);
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              o4[j] = make_uint4(pack_half2(v[8 * j + 0], v[8 * j + 1]), pack_half2(v[8 * j + 2], v[8 * j + 3]),
-                                 pack_half2(v[8 * j + 4], v[8 * j + 5]), pack_half2(v[8 * j + 6], v[8 * j + 7]));
+            for (int j = 0; j < 32; j += 2) gelu_as2(v[j], v[j + 1]);
           }
+#pragma unroll
+          for (int j = 0; j < 16; ++j) w[j] = pack_half2(v[2 * j], v[2 * j + 1]);
+        }
+        // the slot's previous chunk (two chunks ago) must have been read by its store
+        if (lane == 0) bulk_wait_read_1();
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          *reinterpret_cast<uint4*>(slot + lane * 64 + ((j ^ sw) << 4)) =
+              make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (EPI == EPI_BIAS_RESID_F32)
+            tma_reduce_add_2d(&tmO, slot, col, m0 + q * 32);
+          else
+            tma_store_2d(&tmO, slot, col, m0 + q * 32);
+          bulk_commit();
         }
       }
+      // every tcgen05.ld of buffer b has completed (each waits for its data)
       tc_fence_before();
       mbar_arrive(&acc_empty[b]);
     }
+    if (lane == 0) bulk_wait_all();  // the last stores are complete before the CTA exits
   }
   tc_fence_before();
   __syncthreads();

@@ -4,6 +4,8 @@
 // One warp per row; the row is held in registers, mean and variance are two
 // warp-shuffle reductions (two-pass, no E[x^2]-E[x]^2 cancellation).
 // fp32 in; fp16 out (feeds a GEMM's A operand) or fp32 out (model output).
+// Optionally the input row is also copied to `copy_out` (fp32): the block's
+// residual stream, onto which the next projection GEMM accumulates in place.
 #pragma once
 
 #include "ptx.cuh"
@@ -21,7 +23,8 @@ __device__ __forceinline__ float warp_sum(float v) {
 template <int VPL, bool VEC4, bool OUT_F16>
 __global__ void __launch_bounds__(256)
     k_layernorm(const float* __restrict__ x, int64_t ld_x, const float* __restrict__ gamma,
-                const float* __restrict__ beta, void* __restrict__ out, int64_t ld_out, int rows, int d, float eps) {
+                const float* __restrict__ beta, void* __restrict__ out, int64_t ld_out, int rows, int d, float eps,
+                float* __restrict__ copy_out, int64_t ld_copy) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + warp;
   if (row >= rows) return;
@@ -34,10 +37,14 @@ __global__ void __launch_bounds__(256)
     for (int i = 0; i < VPL; ++i) {
       const float4 t = *reinterpret_cast<const float4*>(xr + 4 * lane + 128 * i);
       v[4 * i] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
+      if (copy_out) *reinterpret_cast<float4*>(copy_out + row * ld_copy + 4 * lane + 128 * i) = t;
     }
   } else {
 #pragma unroll
-    for (int i = 0; i < VPL; ++i) v[i] = xr[lane + 32 * i];
+    for (int i = 0; i < VPL; ++i) {
+      v[i] = xr[lane + 32 * i];
+      if (copy_out) copy_out[row * ld_copy + lane + 32 * i] = v[i];
+    }
   }
 #pragma unroll
   for (int i = 0; i < NV; ++i) s += v[i];

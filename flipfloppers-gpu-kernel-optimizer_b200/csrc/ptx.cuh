@@ -159,7 +159,23 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* m, const void* s
                ::"l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
                : "memory");
 }
+// 2-D tiled store / element-wise add-reduce (out += tile, performed in L2) from
+// shared memory, bulk-group completion; elements outside the tensor are skipped.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+               ::"l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* m, const void* src, int x, int y) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];"
+               ::"l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// at most one bulk group committed by this thread is still reading shared memory
+__device__ __forceinline__ void bulk_wait_read_1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
 // every bulk store committed by this thread has finished reading shared memory
 __device__ __forceinline__ void bulk_wait_read_all() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
@@ -351,6 +367,18 @@ __device__ __forceinline__ void f2_add_bias32(float (&v)[32], const float* b) {
 #pragma unroll
   for (int i = 0; i < 32; i += 4) {
     const float4 bb = *reinterpret_cast<const float4*>(b + i);
+    const uint64_t lo = f2add(f2pk(v[i], v[i + 1]), f2pk(bb.x, bb.y));
+    const uint64_t hi = f2add(f2pk(v[i + 2], v[i + 3]), f2pk(bb.z, bb.w));
+    f2upk(lo, v[i], v[i + 1]);
+    f2upk(hi, v[i + 2], v[i + 3]);
+  }
+}
+// v[i] += b[i] for 32 values, b 16-byte aligned global memory (every lane reads
+// the same address: one broadcast request per load)
+__device__ __forceinline__ void f2_add_bias32_global(float (&v)[32], const float* b) {
+#pragma unroll
+  for (int i = 0; i < 32; i += 4) {
+    const float4 bb = __ldg(reinterpret_cast<const float4*>(b + i));
     const uint64_t lo = f2add(f2pk(v[i], v[i + 1]), f2pk(bb.x, bb.y));
     const uint64_t hi = f2add(f2pk(v[i + 2], v[i + 3]), f2pk(bb.z, bb.w));
     f2upk(lo, v[i], v[i + 1]);

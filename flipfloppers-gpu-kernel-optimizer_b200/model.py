@@ -578,11 +578,11 @@ class UserOptimizedTransformer(nn.Module):
         lnf_w, lnf_b = self._lnf
         eps = float(self.layers[0].norm1.eps)
         stages = [
-            ("ln1", lambda: rt.layernorm(x2, pk.ln1_w, pk.ln1_b, n, eps)),
+            ("ln1", lambda: rt.layernorm(x2, pk.ln1_w, pk.ln1_b, n, eps, residual_out=x1)),
             ("qkv", lambda: rt.gemm(rt.EPI_BIAS_F16, n, pk.w_qkv, pk.b_qkv, qkv)),
             ("attn", lambda: rt.flash_causal(qkv, qkv, qkv, ctx, batch=B, heads=H, head_dim=d // H, q_len=S,
                                              kv_len=S, k_col0=d, v_col0=2 * d, non_causal=not cfg.causal)),
-            ("out_proj", lambda: rt.gemm(rt.EPI_BIAS_RESID_F32, ctx, pk.w_o, pk.b_o, x1, resid=x2)),
+            ("out_proj", lambda: rt.gemm(rt.EPI_BIAS_RESID_F32, ctx, pk.w_o, pk.b_o, x1, resid=x1)),
             ("ln2", lambda: rt.layernorm(x1, pk.ln2_w, pk.ln2_b, n, eps)),
             ("ffn_in", lambda: rt.gemm(rt.EPI_BIAS_GELU_F16, n, pk.w_in, pk.b_in, h)),
             ("ffn_out", lambda: rt.gemm(rt.EPI_BIAS_RESID_F32, h, pk.w_out, pk.b_out, x1, resid=x1)),

@@ -105,6 +105,8 @@ EXPORTS = [
     ("b200_device_error", ctypes.c_int, [ctypes.c_int]),
     ("b200_layernorm_launch", ctypes.c_int,
      [_vp, _c_ll, _vp, _vp, _vp, _c_ll, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, _vp]),
+    ("b200_layernorm_residual_launch", ctypes.c_int,
+     [_vp, _c_ll, _vp, _vp, _vp, _c_ll, ctypes.c_int, _vp, _c_ll, ctypes.c_int, ctypes.c_int, ctypes.c_float, _vp]),
     ("b200_add_layernorm_launch", ctypes.c_int,
      [_vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, _vp]),
     ("b200_zero_masked_rows", ctypes.c_int, [_vp, _vp, _c_ll, ctypes.c_int, _vp]),
@@ -173,17 +175,29 @@ def _require_cuda(*ts):
 
 
 def layernorm(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, out: torch.Tensor,
-              eps: float = 1e-5, stream=None) -> torch.Tensor:
-    """out = LayerNorm(x) * gamma + beta over the last dim; out fp16 or fp32."""
-    _require_cuda(x, gamma, beta, out)
+              eps: float = 1e-5, stream=None, residual_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out = LayerNorm(x) * gamma + beta over the last dim; out fp16 or fp32.
+
+    With ``residual_out`` (fp32, x's shape) x is also copied there: the residual
+    stream a following ``gemm(EPI_BIAS_RESID_F32, ..., out=r, resid=r)`` adds onto."""
+    _require_cuda(x, gamma, beta, out, residual_out)
     d = x.shape[-1]
     rows = x.numel() // d
     if x.dtype != torch.float32 or out.dtype not in (torch.float16, torch.float32):
         raise TypeError("layernorm: x must be fp32, out fp16 or fp32")
-    rc = lib().b200_layernorm_launch(_p(x), x.stride(-2) if x.dim() > 1 else d, _p(gamma), _p(beta), _p(out),
-                                     out.stride(-2) if out.dim() > 1 else d, int(out.dtype == torch.float16),
-                                     rows, d, float(eps), _stream(stream))
-    check(rc, "b200_layernorm_launch")
+    ldx = x.stride(-2) if x.dim() > 1 else d
+    ldo = out.stride(-2) if out.dim() > 1 else d
+    if residual_out is None:
+        rc = lib().b200_layernorm_launch(_p(x), ldx, _p(gamma), _p(beta), _p(out), ldo,
+                                         int(out.dtype == torch.float16), rows, d, float(eps), _stream(stream))
+        check(rc, "b200_layernorm_launch")
+    else:
+        if residual_out.dtype != torch.float32:
+            raise TypeError("layernorm: residual_out must be fp32")
+        rc = lib().b200_layernorm_residual_launch(
+            _p(x), ldx, _p(gamma), _p(beta), _p(out), ldo, int(out.dtype == torch.float16), _p(residual_out),
+            residual_out.stride(-2) if residual_out.dim() > 1 else d, rows, d, float(eps), _stream(stream))
+        check(rc, "b200_layernorm_residual_launch")
     return out
 
 

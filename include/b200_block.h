@@ -86,6 +86,14 @@ int b200_device_error(int clear);
 int b200_layernorm_launch(const float* x, long long ld_x, const float* gamma, const float* beta, void* out,
                           long long ld_out, int out_f16, int rows, int d, float eps, b200_stream_t stream);
 
+/* b200_layernorm_launch that also copies x's rows (fp32) into residual_out
+ * [rows, ld_residual]: norm1 together with the residual stream the block's
+ * output projection then accumulates onto in place (torch_transformer_benchmark.py
+ * 1293 and 1333-1339, `residual = x`).  residual_out must not overlap x or out. */
+int b200_layernorm_residual_launch(const float* x, long long ld_x, const float* gamma, const float* beta, void* out,
+                                   long long ld_out, int out_f16, float* residual_out, long long ld_residual,
+                                   int rows, int d, float eps, b200_stream_t stream);
+
 /* sum_out = a + b (+ bias[col]) in fp32, then out = LayerNorm(sum_out) *
  * gamma + beta (fp16 or fp32): the residual add after a tensor-parallel
  * all-reduce fused with the LayerNorm that follows (norm2 / final_norm of the
@@ -103,9 +111,11 @@ int b200_zero_masked_rows(float* y, const unsigned char* row_valid, long long ro
 
 /* out[M,N] = epilogue(A[M,K] . W[N,K]^T + bias[N]).  A, W fp16 row-major with
  * leading dimensions lda, ldw (elements); bias fp32 (may be null); resid fp32
- * [M, ld_resid] for B200_EPI_BIAS_RESID_F32 (may equal out).  Requires
- * N % 32 == 0, K % 8 == 0, lda/ldw % 8 == 0, 16-byte aligned pointers.
- * fp32 accumulation on the tcgen05 tensor cores. */
+ * [M, ld_resid] for B200_EPI_BIAS_RESID_F32.  The residual epilogue adds onto
+ * out in place (out == resid, same leading dimension: no extra traffic);
+ * a different resid is first copied into out, so it must not overlap out.
+ * Requires N % 32 == 0, K % 8 == 0, lda/ldw % 8 == 0, 16-byte aligned
+ * pointers.  fp32 accumulation on the tcgen05 tensor cores. */
 int b200_gemm_launch(int epilogue, const void* A, long long lda, const void* W, long long ldw, const float* bias,
                      const float* resid, long long ld_resid, void* out, long long ld_out, int M, int N, int K,
                      b200_stream_t stream);

@@ -67,6 +67,36 @@ def test_gemm_exact_integer_resid_f32(rt, M, N, K):
     assert torch.equal(resid.double(), ref)
 
 
+@pytest.mark.parametrize("M,N,K", [(300, 96, 520), (1000, 512, 64), (256, 4096, 128)])
+def test_gemm_exact_integer_f32_into_column_slice(rt, M, N, K):
+    """EPI_BIAS_F32 into columns [32, 32+N) of a wider buffer: exact values in
+    the slice (the TMA store box clips at M and N), nothing written outside."""
+    g = torch.Generator().manual_seed(M + 11 * N)
+    a = _ints((M, K), -2, 2, g)
+    w = _ints((N, K), -2, 2, g)
+    bias = torch.randint(-4, 5, (N,), generator=g).float().to(DEV)
+    wide = torch.full((M, N + 96), 7.0, dtype=torch.float32, device=DEV)
+    out = wide[:, 32:32 + N]
+    rt.gemm(rt.EPI_BIAS_F32, a, w, bias, out)
+    ref = a.double() @ w.double().T + bias.double()
+    torch.cuda.synchronize()
+    assert torch.equal(out.double(), ref)
+    assert (wide[:, :32] == 7.0).all() and (wide[:, 32 + N:] == 7.0).all()
+
+
+def test_gemm_f16_into_column_slice(rt):
+    M, N, K = 777, 160, 256
+    g = torch.Generator().manual_seed(3)
+    a = _ints((M, K), -1, 1, g)
+    w = _ints((N, K), -1, 1, g)
+    wide = torch.full((M, 3 * N), -3.0, dtype=torch.float16, device=DEV)
+    out = wide[:, N:2 * N]
+    rt.gemm(rt.EPI_BIAS_F16, a, w, None, out)
+    torch.cuda.synchronize()
+    assert torch.equal(out.double(), a.double() @ w.double().T)
+    assert (wide[:, :N] == -3.0).all() and (wide[:, 2 * N:] == -3.0).all()
+
+
 @pytest.mark.parametrize("M,N,K", [(512, 256, 128), (384, 128, 1024)])
 def test_gemm_one_hot_index_sweep(rt, M, N, K):
     g = torch.Generator().manual_seed(5)
@@ -124,6 +154,24 @@ def test_layernorm_vs_torch(rt, d, f16):
     torch.cuda.synchronize()
     tol = 2e-3 if f16 else 2e-5
     assert ((out.float() - ref).abs() <= tol * (1 + ref.abs())).all()
+
+
+@pytest.mark.parametrize("d", [96, 1024])
+def test_layernorm_residual_copy(rt, d):
+    """norm1 with the residual copy: out as without it, residual_out == x exactly."""
+    g = torch.Generator().manual_seed(d + 1)
+    rows = 1000
+    x = (torch.randn(rows, d, generator=g) * 2).to(DEV)
+    gamma = torch.randn(d, generator=g).to(DEV)
+    beta = torch.randn(d, generator=g).to(DEV)
+    out = torch.empty(rows, d, dtype=torch.float16, device=DEV)
+    out_plain = torch.empty_like(out)
+    res = torch.full((rows, d), float("nan"), device=DEV)
+    rt.layernorm(x, gamma, beta, out, eps=1e-5, residual_out=res)
+    rt.layernorm(x, gamma, beta, out_plain, eps=1e-5)
+    torch.cuda.synchronize()
+    assert torch.equal(res, x)
+    assert torch.equal(out, out_plain)
 
 
 def _attn_ref(q, k, v, q_offset):
