@@ -17,6 +17,7 @@
 #include "ptx.cuh"
 #include "ln.cuh"
 #include "gemm.cuh"
+#include "gemm2.cuh"
 #include "attn.cuh"
 #include "attn2.cuh"
 #include "fused_small.cuh"
@@ -199,6 +200,57 @@ int pick_bn(long long M, int N) {
   return N % 256 == 0 ? 256 : 128;
 }
 
+// CTA-pair kernel: clusters that can be resident at once (queried once per device)
+int g_pair_clusters[128] = {0};
+
+template <int EPI>
+int launch_gemm2_t(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const GemmParams& p,
+                   cudaStream_t st) {
+  auto kern = k_gemm2_tn<EPI>;
+  const int smem = Gemm2Smem<GEMM2_STAGES>::TOTAL;
+  if (int rc = set_smem(reinterpret_cast<const void*>(kern), smem)) return rc;
+  const int dev = current_device();
+  int maxcl = (dev >= 0 && dev < 128) ? g_pair_clusters[dev] : 0;
+  if (maxcl <= 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(num_sms()));
+    cfg.blockDim = dim3(GEMM_THREADS);
+    cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, reinterpret_cast<const void*>(kern), &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = num_sms() / 2;
+    }
+    maxcl = n;
+    if (dev >= 0 && dev < 128) g_pair_clusters[dev] = n;
+  }
+  const long long tiles = static_cast<long long>((p.M + 255) / 256) * ((p.N + 255) / 256);
+  const int clusters = static_cast<int>(tiles < maxcl ? tiles : maxcl);
+  kern<<<2 * clusters, GEMM_THREADS, smem, st>>>(ta, tw, to, p);
+  return launch_status();
+}
+
+// 0: one-SM kernel, 1: CTA-pair kernel, -1 (default): by shape
+int gemm_pair_mode() {
+  static const int mode = [] {
+    const char* e = std::getenv("B200_GEMM_PAIR");
+    return e ? std::atoi(e) : -1;
+  }();
+  return mode;
+}
+
+// Measured on B200 (N-fastest tile order, L2 flushed): the pair kernel is
+// ahead wherever whole 256-column tiles exist and both CTAs get rows, e.g.
+// 100000x3072x1024 434 vs 480 us, 16384x4096x4096 338 vs 365 us, 8192x1024x4096
+// (+residual) 60 vs 67 us; the one-SM kernel keeps N not a multiple of 256
+// (QKV at d=128: N=384) and short M.
+bool use_pair_gemm(long long M, int N, int K) {
+  (void)K;
+  const int mode = gemm_pair_mode();
+  if (mode >= 0) return mode == 1 && M >= 256 && N >= 256;
+  return N % 256 == 0 && M >= 512;
+}
+
 int gemm_impl(int epi, const void* A, long long lda, const void* W, long long ldw, const float* bias,
               const float* resid, long long ld_resid, void* out, long long ld_out, int M, int N, int K,
               cudaStream_t st) {
@@ -241,6 +293,16 @@ int gemm_impl(int epi, const void* A, long long lda, const void* W, long long ld
   p.K = K;
   p.a_row0 = 0;
   p.bias = bias;
+  if (use_pair_gemm(M, N, K)) {
+    CUtensorMap tw2;  // each CTA of the pair loads 128 rows (half the tile's N range) of W
+    if (int rc = make_map_f16(&tw2, W, N, K, ldw, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
+    switch (epi) {
+      case EPI_BIAS_F16: return launch_gemm2_t<EPI_BIAS_F16>(ta, tw2, to, p, st);
+      case EPI_BIAS_GELU_F16: return launch_gemm2_t<EPI_BIAS_GELU_F16>(ta, tw2, to, p, st);
+      case EPI_BIAS_RESID_F32: return launch_gemm2_t<EPI_BIAS_RESID_F32>(ta, tw2, to, p, st);
+      default: return launch_gemm2_t<EPI_BIAS_F32>(ta, tw2, to, p, st);
+    }
+  }
   if (BN == 256) return launch_gemm_bn<256, 4>(epi, ta, tw, to, p, st);
   return launch_gemm_bn<128, 6>(epi, ta, tw, to, p, st);
 }

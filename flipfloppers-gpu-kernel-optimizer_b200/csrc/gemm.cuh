@@ -12,7 +12,10 @@
 // It replaces the reference's mma.sync GEMM `ws_gemm_kernel`
 // (csrc/g4_4_warpspec_gemm.cu:273-795) with a persistent Blackwell design:
 //   grid = min(tiles, SMs); CTA c takes output tiles c, c+grid, ... (tiles
-//   ordered M-fastest so concurrently running CTAs share W tiles in L2);
+//   ordered N-fastest: the CTAs running at one time cover a band of A rows
+//   across every N tile, so each A tile is read from HBM once and then from
+//   L2, and W -- a few MB -- stays L2-resident; M-fastest order would stream
+//   all of A once per N column when A is larger than L2);
 //   warp 0     TMA producer: 64-wide K slices of A and W, SWIZZLE_128B, into a
 //              STAGES-deep shared-memory ring that runs across tiles;
 //   warp 1     TMEM owner and tcgen05.mma issuer (one lane), accumulating tile
@@ -50,6 +53,67 @@ struct GemmSmem {
 };
 
 constexpr int GEMM_THREADS = 320;  // producer, MMA, 8 epilogue warps
+
+// Epilogue of one accumulator tile for one epilogue warp: TMEM lane quadrant q
+// (rows row0 .. row0+31 of the output), columns [c_begin, c_end) of the tile
+// at TMEM column tcol (column col0 of the output).  Chunks of 64 bytes per row
+// alternate between the warp's two 2 KB staging slots `stg`; `gc` counts the
+// chunks this warp has staged (it selects the slot).
+template <int EPI>
+__device__ __forceinline__ void gemm_epilogue_cols(const CUtensorMap* tmO, const GemmParams& p, uint32_t taddr0,
+                                                   int c_begin, int c_end, int col0, int row0, uint8_t* stg, int& gc,
+                                                   int lane) {
+  constexpr bool F32 = EPI == EPI_BIAS_RESID_F32 || EPI == EPI_BIAS_F32;
+  constexpr int CC = F32 ? 16 : 32;                            // columns per 64-byte chunk row
+  const uint32_t sw = static_cast<uint32_t>((lane >> 1) & 3);  // SWIZZLE_64B phase of row `lane`
+#pragma unroll 1
+  for (int c = c_begin; c < c_end; c += CC, ++gc) {
+    const uint32_t taddr = taddr0 + c;
+    const int col = col0 + c;
+    uint8_t* slot = stg + (gc & 1) * 2048;
+    uint32_t w[16];  // the chunk's 64 bytes of this row
+    if constexpr (F32) {
+      float v[16];
+      tmem_ld16(taddr, v);
+      if (p.bias != nullptr && col < p.N) {
+        const float4* b4 = reinterpret_cast<const float4*>(p.bias + col);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float4 bb = __ldg(b4 + j);
+          v[4 * j] += bb.x; v[4 * j + 1] += bb.y; v[4 * j + 2] += bb.z; v[4 * j + 3] += bb.w;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) w[j] = __float_as_uint(v[j]);
+    } else {
+      float v[32];
+      tmem_ld32(taddr, v);
+      if (p.bias != nullptr && col < p.N) f2_add_bias32_global(v, p.bias + col);
+      if constexpr (EPI == EPI_BIAS_GELU_F16) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) gelu_as2(v[j], v[j + 1]);
+      }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) w[j] = pack_half2(v[2 * j], v[2 * j + 1]);
+    }
+    // the slot's previous chunk (two chunks ago) must have been read by its store
+    if (lane == 0) bulk_wait_read_1();
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      *reinterpret_cast<uint4*>(slot + lane * 64 + ((j ^ sw) << 4)) =
+          make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      if constexpr (EPI == EPI_BIAS_RESID_F32)
+        tma_reduce_add_2d(tmO, slot, col, row0);
+      else
+        tma_store_2d(tmO, slot, col, row0);
+      bulk_commit();
+    }
+  }
+}
 
 template <int BN, int STAGES, int EPI>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
@@ -104,7 +168,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       bool ok = true;
       for (int i = 0; ok && i < my_tiles; ++i) {
         const int t = static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x);
-        const int m0 = (t % mt) * 128, n0 = (t / mt) * BN;
+        const int m0 = (t / ntl) * 128, n0 = (t % ntl) * BN;
         for (int kb = 0; kb < nk; ++kb, ++it) {
           const int s = it % STAGES;
           if (it >= STAGES && !mbar_wait(&empty[s], ((it / STAGES) - 1) & 1, abort_flag, DERR_WAIT_SLOT)) {
@@ -158,67 +222,19 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     // epilogue warps 2..9
     const int q = warp & 3;
     const int half = (warp - 2) >> 2;
-    constexpr int CW = BN / 2;                                            // columns per warp per tile
-    constexpr bool F32 = EPI == EPI_BIAS_RESID_F32 || EPI == EPI_BIAS_F32;
-    constexpr int CC = F32 ? 16 : 32;                                     // columns per 64-byte chunk row
-    uint8_t* stg = smem + L::STG_OFF + (warp - 2) * 4096;                 // two 2 KB slots
-    const uint32_t sw = static_cast<uint32_t>((lane >> 1) & 3);           // SWIZZLE_64B phase of row `lane`
+    constexpr int CW = BN / 2;                             // columns per warp per tile
+    uint8_t* stg = smem + L::STG_OFF + (warp - 2) * 4096;  // two 2 KB slots
     if (lane == 0) tma_prefetch_desc(&tmO);
-    int gc = 0;  // chunks this warp has staged
+    int gc = 0;
     for (int i = 0; i < my_tiles; ++i) {
       const int b = i & 1;
       const int t = static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x);
-      const int m0 = (t % mt) * 128, n0 = (t / mt) * BN;
+      const int m0 = (t / ntl) * 128, n0 = (t % ntl) * BN;
       const bool ok = mbar_wait_warp(&acc_full[b], (i >> 1) & 1, abort_flag, DERR_WAIT_MMA);
       if (!ok || *abort_flag) break;
       tc_fence_after();
-#pragma unroll 1
-      for (int c = half * CW; c < (half + 1) * CW; c += CC, ++gc) {
-        const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + b * BN + c;
-        const int col = n0 + c;
-        uint8_t* slot = stg + (gc & 1) * 2048;
-        uint32_t w[16];  // the chunk's 64 bytes of this row
-        if constexpr (F32) {
-          float v[16];
-          tmem_ld16(taddr, v);
-          if (p.bias != nullptr && col < p.N) {
-            const float4* b4 = reinterpret_cast<const float4*>(p.bias + col);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float4 bb = __ldg(b4 + j);
-              v[4 * j] += bb.x; v[4 * j + 1] += bb.y; v[4 * j + 2] += bb.z; v[4 * j + 3] += bb.w;
-            }
-          }
-#pragma unroll
-          for (int j = 0; j < 16; ++j) w[j] = __float_as_uint(v[j]);
-        } else {
-          float v[32];
-          tmem_ld32(taddr, v);
-          if (p.bias != nullptr && col < p.N) f2_add_bias32_global(v, p.bias + col);
-          if constexpr (EPI == EPI_BIAS_GELU_F16) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 2) gelu_as2(v[j], v[j + 1]);
-          }
-#pragma unroll
-          for (int j = 0; j < 16; ++j) w[j] = pack_half2(v[2 * j], v[2 * j + 1]);
-        }
-        // the slot's previous chunk (two chunks ago) must have been read by its store
-        if (lane == 0) bulk_wait_read_1();
-        __syncwarp();
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          *reinterpret_cast<uint4*>(slot + lane * 64 + ((j ^ sw) << 4)) =
-              make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          if constexpr (EPI == EPI_BIAS_RESID_F32)
-            tma_reduce_add_2d(&tmO, slot, col, m0 + q * 32);
-          else
-            tma_store_2d(&tmO, slot, col, m0 + q * 32);
-          bulk_commit();
-        }
-      }
+      gemm_epilogue_cols<EPI>(&tmO, p, tmem + (static_cast<uint32_t>(q * 32) << 16) + b * BN, half * CW,
+                              (half + 1) * CW, n0, m0 + q * 32, stg, gc, lane);
       // every tcgen05.ld of buffer b has completed (each waits for its data)
       tc_fence_before();
       mbar_arrive(&acc_empty[b]);

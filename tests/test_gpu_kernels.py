@@ -260,3 +260,39 @@ def test_flash_noncausal_with_key_lengths_vs_torch(rt, B, H, S, hd):
     ref = (torch.softmax(s_, -1) @ t[2]).permute(0, 2, 1, 3).reshape(B * S, d)
     torch.cuda.synchronize()
     assert (out.float() - ref).abs().max().item() < 4e-3
+
+
+@pytest.mark.parametrize("mode", ["0", "1"])
+def test_gemm_both_kernels_exact_in_subprocess(mode):
+    """The one-SM and the CTA-pair GEMM (B200_GEMM_PAIR forces the choice; it is
+    read once per process, hence the child process) give exact integer results,
+    fp16 and in-place residual epilogues, on aligned and ragged shapes."""
+    import os
+    import subprocess
+    import sys
+    code = r'''
+import torch, sys
+import torch_transformer_benchmark as T
+rt = T._pkg.runtime
+dev = "cuda"
+for (M, N, K) in ((256, 256, 64), (512, 768, 256), (300, 96, 520), (777, 1280, 4096), (4096, 2048, 1024)):
+    g = torch.Generator().manual_seed(M + N + K)
+    a = torch.randint(-1, 2, (M, K), generator=g).half().to(dev)
+    w = torch.randint(-1, 2, (N, K), generator=g).half().to(dev)
+    bias = torch.randint(-4, 5, (N,), generator=g).float().to(dev)
+    out = torch.empty(M, N, dtype=torch.float16, device=dev)
+    rt.gemm(rt.EPI_BIAS_F16, a, w, bias, out)
+    ref = a.double() @ w.double().T + bias.double()
+    resid = torch.randint(-100, 101, (M, N), generator=g).float().to(dev)
+    ref2 = ref + resid.double()
+    rt.gemm(rt.EPI_BIAS_RESID_F32, a, w, bias, resid, resid=resid)
+    torch.cuda.synchronize()
+    assert torch.equal(out.double(), ref), (M, N, K)
+    assert torch.equal(resid.double(), ref2), (M, N, K)
+assert rt.device_error(clear=True) == 0
+print("OK")
+'''
+    env = dict(os.environ, B200_GEMM_PAIR=mode)
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "OK" in r.stdout, r.stdout + r.stderr
