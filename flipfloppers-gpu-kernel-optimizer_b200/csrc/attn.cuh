@@ -13,7 +13,9 @@
 //              2-deep ring (kv_full / kv_empty mbarriers);
 //   warp 1     TMEM owner + MMA issuer: S_j = Q.K_j^T into TMEM columns
 //              [0,BN); O += P_j.V_j into columns [BN, BN+HD) with V read
-//              MN-major (head_dim contiguous) straight from the TMA tile;
+//              MN-major (head_dim contiguous) straight from the TMA tile.
+//              S_j+1 is issued as soon as the softmax has read S_j into
+//              registers (s_free), so it overlaps the softmax of tile j;
 //   warps 2-5  softmax: one query row per thread (TMEM lane = row), running
 //              max / sum in the log2 domain, P_j (fp16) written to shared
 //              memory in the 128B-swizzled K-major layout UMMA reads, O rescaled
@@ -25,6 +27,54 @@
 #include "ptx.cuh"
 
 namespace b200 {
+
+// ---- row softmax pieces shared by the attention kernels (one row per thread)
+
+// this thread's TMEM row, N fp32 columns, one load instruction and one wait
+template <int N>
+__device__ __forceinline__ void tmem_ld_row(uint32_t taddr, float (&s)[N]) {
+  if constexpr (N == 128) {
+    tmem_ld128(taddr, s);
+  } else {
+    static_assert(N == 64, "rows of 64 or 128 columns");
+    tmem_ld64(taddr, s);
+  }
+}
+// max of N values: eight independent chains of three-input maxima (short
+// dependency chains; two warps per SMSP cannot hide a 64-deep chain)
+template <int N>
+__device__ __forceinline__ float row_max(const float (&s)[N]) {
+  static_assert(N % 16 == 0, "N multiple of 16");
+  float m[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) m[k] = fmaxf(s[2 * k], s[2 * k + 1]);
+#pragma unroll
+  for (int c = 16; c < N; c += 16)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) m[k] = fmax3(m[k], s[c + 2 * k], s[c + 2 * k + 1]);
+  return fmaxf(fmax3(m[0], m[1], m[2]), fmaxf(fmax3(m[3], m[4], m[5]), fmaxf(m[6], m[7])));
+}
+// s[c] = 2^(s[c]*scale - m) in place; returns the sum (f32x2 pairs: the
+// scale/subtract and the four running sums take half the issue slots)
+template <int N>
+__device__ __forceinline__ float row_exp2_sum(float (&s)[N], float scale, float m) {
+  const uint64_t sc = f2pk(scale, scale), nm = f2pk(-m, -m);
+  uint64_t acc[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) acc[k] = f2pk(0.f, 0.f);
+#pragma unroll
+  for (int c = 0; c < N; c += 2) {
+    float a, b;
+    f2upk(f2fma(f2pk(s[c], s[c + 1]), sc, nm), a, b);
+    s[c] = fast_exp2(a);
+    s[c + 1] = fast_exp2(b);
+    acc[(c >> 1) & 3] = f2add(acc[(c >> 1) & 3], f2pk(s[c], s[c + 1]));
+  }
+  float t[8];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) f2upk(acc[k], t[2 * k], t[2 * k + 1]);
+  return ((t[0] + t[1]) + (t[2] + t[3])) + ((t[4] + t[5]) + (t[6] + t[7]));
+}
 
 struct AttnParams {
   int H;
@@ -86,7 +136,8 @@ __global__ void __launch_bounds__(192, 2)  // two CTAs per SM (registers <= 170)
   uint64_t* p_full = bars + 6;
   uint64_t* pv_done = bars + 7;
   uint64_t* drain = bars + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+  uint64_t* s_free = bars + 9;  // softmax has read S into registers
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -108,6 +159,7 @@ __global__ void __launch_bounds__(192, 2)  // two CTAs per SM (registers <= 170)
     mbar_init(p_full, 128);
     mbar_init(pv_done, 1);
     mbar_init(drain, 1);
+    mbar_init(s_free, 128);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -175,6 +227,13 @@ __global__ void __launch_bounds__(192, 2)  // two CTAs per SM (registers <= 170)
         issue_s(0);
       }
       for (int j = 0; ok && j < nkt; ++j) {
+        // S of key tile j+1 as soon as the softmax has read S of tile j (runs during its softmax)
+        if (j + 1 < nkt) {
+          if (!mbar_wait(s_free, j & 1, abort_flag, DERR_WAIT_SOFTMAX)) break;
+          if (!mbar_wait(&kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag, DERR_WAIT_TMA)) break;
+          tc_fence_after();
+          issue_s(j + 1);
+        }
         if (!mbar_wait(p_full, j & 1, abort_flag, DERR_WAIT_SOFTMAX)) break;
         tc_fence_after();
         const uint32_t v_addr = smem_u32(smem + ((j & 1) ? C::OFF_V1 : C::OFF_V0));
@@ -186,11 +245,6 @@ __global__ void __launch_bounds__(192, 2)  // two CTAs per SM (registers <= 170)
         }
         tc_commit(pv_done);
         tc_commit(&kv_empty[j & 1]);
-        if (j + 1 < nkt) {
-          if (!mbar_wait(&kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag, DERR_WAIT_TMA)) break;
-          tc_fence_after();
-          issue_s(j + 1);
-        }
       }
       if (*abort_flag) {
         tc_commit(drain);
@@ -211,36 +265,22 @@ __global__ void __launch_bounds__(192, 2)  // two CTAs per SM (registers <= 170)
       if (!ok) break;
       tc_fence_after();
       float s[BN];
-#pragma unroll
-      for (int c = 0; c < BN; c += 32) {
-        float t[32];
-        tmem_ld32(trow + c, t);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[c + i] = t[i];
-      }
+      tmem_ld_row<BN>(trow, s);
+      tc_fence_before();
+      mbar_arrive(s_free);  // the MMA warp may now overwrite S with the next key tile
       const int k0 = j * BN;
       const int klim = p.non_causal ? kv_eff - 1 : min(qpos, kv_eff - 1);  // last visible key of this row
       const bool need_mask = (k0 + BN - 1) > (p.non_causal ? kv_eff - 1 : min(q_first, kv_eff - 1));
-      float mx0 = -INFINITY, mx1 = -INFINITY;
+      if (need_mask) {  // raw scores; the positive scale is applied in the exponent
 #pragma unroll
-      for (int c = 0; c < BN; c += 2) {  // raw scores; the positive scale is applied in the exponent
-        if (need_mask && (k0 + c) > klim) s[c] = -INFINITY;
-        if (need_mask && (k0 + c + 1) > klim) s[c + 1] = -INFINITY;
-        mx0 = fmaxf(mx0, s[c]);
-        mx1 = fmaxf(mx1, s[c + 1]);
+        for (int c = 0; c < BN; ++c)
+          if (k0 + c > klim) s[c] = -INFINITY;
       }
-      const float m_new = fmaxf(m, fmaxf(mx0, mx1) * p.scale_log2);
+      const float m_new = fmaxf(m, row_max<BN>(s) * p.scale_log2);
       // rows with nothing visible yet keep p = 0 (cannot happen for real rows: key 0 is always visible)
       const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
       const float alpha = fast_exp2(m - m_use);  // m = -inf on the first tile -> 0
-      float s4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int c = 0; c < BN; ++c) {
-        const float e = fast_exp2(fmaf(s[c], p.scale_log2, -m_use));
-        s[c] = e;
-        s4[c & 3] += e;
-      }
-      const float sum = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+      const float sum = row_exp2_sum<BN>(s, p.scale_log2, m_use);
       l = l * alpha + sum;
       m = m_new;
       if (j > 0) {

@@ -7,13 +7,17 @@
 //               into a 3-deep ring shared by both query tiles;
 //   warp 1      TMEM owner and MMA issuer, ping-ponging the two tiles:
 //               S_t,j = Q_t.K_j^T into TMEM columns [128t, 128t+128) and
-//               O_t += P_t,j.V_j into [256 + t*HD, ...), so tile 1's QK^T and
-//               tile 0's PV run while the other tile's softmax runs;
+//               O_t += P_t,j.V_j into [256 + t*HD, ...).  S_t,j+1 is issued as
+//               soon as the softmax has read S_t,j into registers (s_free), so
+//               the next tile's QK^T runs during this tile's softmax and the
+//               softmax never waits for an MMA round trip;
 //   warps 2-5   softmax of query tile 0, warps 6-9 of tile 1: one row per
 //               thread, log2-domain running max with lazy rescaling (the max
 //               used for the exponentials moves only when a new tile raises it
 //               by more than 8, i.e. P <= 2^8; only then is O rescaled in TMEM),
-//               P in fp16 to shared memory (128B-swizzled K-major).
+//               P in fp16 into TMEM columns [384 + 64t, 448 + 64t) (two keys
+//               per 32-bit column), which the PV MMA reads as its A operand.
+// TMEM: S_0 [0,128) | S_1 [128,256) | O_0, O_1 [256, 256+2*HD) | P_0, P_1 [384,512).
 // Key tiles past a query tile's diagonal are skipped; query tile 1 may need
 // one more key tile than tile 0.
 #pragma once
@@ -31,12 +35,11 @@ struct Attn2Cfg {
   static constexpr int ST = 3;                          // K/V ring depth
   static constexpr int Q_BYTES = 128 * HD * 2;
   static constexpr int KV_BYTES = BN * HD * 2;
-  static constexpr int P_BYTES = 128 * BN * 2;
   static constexpr int OFF_Q = 0;                       // [2]
   static constexpr int OFF_K = 2 * Q_BYTES;             // [ST] K, then [ST] V
   static constexpr int OFF_V = OFF_K + ST * KV_BYTES;
-  static constexpr int OFF_P = OFF_V + ST * KV_BYTES;   // [2]
-  static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
+  static constexpr int OFF_BAR = OFF_V + ST * KV_BYTES;
+  static constexpr uint32_t TM_P = 384;                 // P_t at TM_P + 64 t
   static constexpr int TOTAL = OFF_BAR + 256 + 1024;
   static constexpr float RESCALE_THRESHOLD = 8.0f;      // log2 units
   static_assert(HD == 32 || HD == 64, "two-tile kernel covers head_dim 32 and 64");
@@ -56,7 +59,8 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* s_full = kv_empty + C::ST;     // [2]
   uint64_t* p_full = s_full + 2;           // [2]
   uint64_t* pv_done = p_full + 2;          // [2]
-  uint64_t* drain = pv_done + 2;
+  uint64_t* s_free = pv_done + 2;          // [2] softmax has read S_t into registers
+  uint64_t* drain = s_free + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -90,6 +94,7 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(&s_full[t], 1);
       mbar_init(&p_full[t], 128);
       mbar_init(&pv_done[t], 1);
+      mbar_init(&s_free[t], 128);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -136,7 +141,6 @@ __global__ void __launch_bounds__(320, 1)
       const uint32_t q_addr = smem_u32(smem + C::OFF_Q);
       const uint32_t k_addr = smem_u32(smem + C::OFF_K);
       const uint32_t v_addr = smem_u32(smem + C::OFF_V);
-      const uint32_t p_addr = smem_u32(smem + C::OFF_P);
       int kv_seen = 0;  // key tiles whose TMA load has been waited for
       bool ok = mbar_wait(q_full, 0, abort_flag, DERR_WAIT_TMA);
       auto need_kv = [&](int j) {
@@ -160,6 +164,17 @@ __global__ void __launch_bounds__(320, 1)
         if (ntile[1] > 0) issue_s(1, 0);
       }
       for (int j = 0; ok && j < n_all; ++j) {
+        // S of key tile j+1 as soon as the softmax has read S of tile j
+        for (int t = 0; t < 2; ++t) {
+          if (j + 1 >= ntile[t]) continue;
+          if (!mbar_wait(&s_free[t], j & 1, abort_flag, DERR_WAIT_SOFTMAX)) {
+            ok = false;
+            break;
+          }
+          if (!need_kv(j + 1)) break;
+          issue_s(t, j + 1);
+        }
+        if (!ok) break;
         const uint32_t vb = v_addr + (j % C::ST) * C::KV_BYTES;
         for (int t = 0; t < 2; ++t) {
           if (j >= ntile[t]) continue;
@@ -168,17 +183,13 @@ __global__ void __launch_bounds__(320, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t pb = p_addr + t * C::P_BYTES;
+          const uint32_t pt = tmem + C::TM_P + 64 * t;  // P_t: 16 keys per 8 columns
 #pragma unroll
           for (int kk = 0; kk < C::BN / 16; ++kk)
-            umma_f16_ss(tmem + 256 + t * HD, make_sdesc(pb + (kk >> 2) * (128 * 128) + (kk & 3) * 32, 16, 1024, UMMA_SW128),
+            umma_f16_ts(tmem + 256 + t * HD, pt + 8 * kk,
                         make_sdesc(vb + kk * 16 * C::ROWB, C::BN * C::ROWB, 8 * C::ROWB, C::SWZ), idesc_o,
                         (j > 0 || kk > 0) ? 1u : 0u);
           tc_commit(&pv_done[t]);
-          if (j + 1 < ntile[t]) {
-            if (!need_kv(j + 1)) break;
-            issue_s(t, j + 1);
-          }
         }
         if (!ok) break;
         tc_commit(&kv_empty[j % C::ST]);
@@ -197,7 +208,6 @@ __global__ void __launch_bounds__(320, 1)
     const int qpos = p.q_offset + row_in_seq;
     const int q_first = p.q_offset + qp * 256 + t * 128;
     const uint32_t trow = tmem + (static_cast<uint32_t>(qd * 32) << 16);
-    uint8_t* ps = smem + C::OFF_P + t * C::P_BYTES;
     const int nt = ntile[t];
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
@@ -206,51 +216,35 @@ __global__ void __launch_bounds__(320, 1)
       if (!ok) break;
       tc_fence_after();
       float s[C::BN];
-#pragma unroll
-      for (int c = 0; c < C::BN; c += 32) {
-        float tt[32];
-        tmem_ld32(trow + t * 128 + c, tt);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[c + i] = tt[i];
-      }
+      tmem_ld_row<C::BN>(trow + t * 128, s);
+      tc_fence_before();
+      mbar_arrive(&s_free[t]);  // the MMA warp may now overwrite S_t with the next key tile
       const int k0 = j * C::BN;
       const int klim = p.non_causal ? kv_eff - 1 : min(qpos, kv_eff - 1);  // last visible key of this row
       const bool need_mask = (k0 + C::BN - 1) > (p.non_causal ? kv_eff - 1 : min(q_first, kv_eff - 1));
-      float mx0 = -INFINITY, mx1 = -INFINITY;
+      if (need_mask) {  // raw scores; the positive scale is applied in the exponent
 #pragma unroll
-      for (int c = 0; c < C::BN; c += 2) {  // raw scores; the positive scale is applied in the exponent
-        if (need_mask) {
+        for (int c = 0; c < C::BN; ++c)
           if (k0 + c > klim) s[c] = -INFINITY;
-          if (k0 + c + 1 > klim) s[c + 1] = -INFINITY;
-        }
-        mx0 = fmaxf(mx0, s[c]);
-        mx1 = fmaxf(mx1, s[c + 1]);
       }
-      const float mx = fmaxf(mx0, mx1) * p.scale_log2;
+      const float mx = row_max<C::BN>(s) * p.scale_log2;
       // lazy rescale: move the reference max only when this tile raises it by more than the threshold
       const bool grow = mx > m_used + C::RESCALE_THRESHOLD;
       const float m_new = grow ? mx : m_used;
       const float alpha = grow ? fast_exp2(m_used - m_new) : 1.f;  // 0 on the first tile
       const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-      float s4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int c = 0; c < C::BN; ++c) {
-        const float e = fast_exp2(fmaf(s[c], p.scale_log2, -m_use));
-        s[c] = e;
-        s4[c & 3] += e;
-      }
-      l = l * alpha + ((s4[0] + s4[1]) + (s4[2] + s4[3]));
+      l = l * alpha + row_exp2_sum<C::BN>(s, p.scale_log2, m_use);
       m_used = m_new;
       if (j > 0) {
         ok = mbar_wait_warp(&pv_done[t], (j - 1) & 1, abort_flag, DERR_WAIT_MMA);
         if (!ok) break;
         tc_fence_after();
       }
+      {
+        uint32_t pk[C::BN / 2];  // keys 2i, 2i+1 -> column i (low, high half)
 #pragma unroll
-      for (int ch = 0; ch < C::BN / 8; ++ch) {
-        const uint4 v = make_uint4(pack_half2(s[8 * ch + 0], s[8 * ch + 1]), pack_half2(s[8 * ch + 2], s[8 * ch + 3]),
-                                   pack_half2(s[8 * ch + 4], s[8 * ch + 5]), pack_half2(s[8 * ch + 6], s[8 * ch + 7]));
-        *reinterpret_cast<uint4*>(ps + (ch >> 3) * (128 * 128) + sw128_off(rl, ch & 7)) = v;
+        for (int i = 0; i < C::BN / 2; ++i) pk[i] = pack_half2(s[2 * i], s[2 * i + 1]);
+        tmem_st64(trow + C::TM_P + 64 * t, pk);
       }
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
@@ -262,7 +256,6 @@ __global__ void __launch_bounds__(320, 1)
           tmem_st32(trow + 256 + t * HD + c, o);
         }
       }
-      fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&p_full[t]);
     }
