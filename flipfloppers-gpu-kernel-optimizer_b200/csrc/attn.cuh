@@ -55,7 +55,10 @@ __device__ __forceinline__ float row_max(const float (&s)[N]) {
   return fmaxf(fmax3(m[0], m[1], m[2]), fmaxf(fmax3(m[3], m[4], m[5]), fmaxf(m[6], m[7])));
 }
 // s[c] = 2^(s[c]*scale - m) in place; returns the sum (f32x2 pairs: the
-// scale/subtract and the four running sums take half the issue slots)
+// scale/subtract and the four running sums take half the issue slots).
+// (Computing part of the exponentials with a polynomial on the FMA pipe was
+// measured here and did not pay: these softmax loops are latency-bound, not
+// bound by the SFU.)
 template <int N>
 __device__ __forceinline__ float row_exp2_sum(float (&s)[N], float scale, float m) {
   const uint64_t sc = f2pk(scale, scale), nm = f2pk(-m, -m);
@@ -117,6 +120,10 @@ struct AttnCfg {
   static constexpr int OFF_BAR = OFF_P + P_BYTES;
   static constexpr int TOTAL = OFF_BAR + 256 + 1024;
   static constexpr uint32_t TMEM_COLS = (BN + HD) <= 256 ? 256 : 512;
+  // P (fp16 pairs, BN/2 columns) in TMEM at column TM_P when it fits beside S
+  // and O in the 256 columns each of the two resident CTAs owns; else in smem
+  static constexpr bool P_TMEM = BN == 128 && HD <= 64;
+  static constexpr uint32_t TM_P = 192;
   static_assert(HD % ATOM_E == 0, "head_dim must tile the swizzle atom");
   static_assert(BN % 64 == 0, "key tile must be a multiple of 64");
 };
@@ -239,9 +246,13 @@ __global__ void __launch_bounds__(192, 2)  // two CTAs per SM (registers <= 170)
         const uint32_t v_addr = smem_u32(smem + ((j & 1) ? C::OFF_V1 : C::OFF_V0));
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t ad = make_sdesc(p_addr + (kk >> 2) * (128 * 128) + (kk & 3) * 32, 16, 1024, UMMA_SW128);
           const uint64_t bd = make_sdesc(v_addr + kk * 16 * C::ROWB, BN * C::ROWB, 8 * C::ROWB, C::SWZ);
-          umma_f16_ss(tmem + BN, ad, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          if constexpr (C::P_TMEM) {
+            umma_f16_ts(tmem + BN, tmem + C::TM_P + 8 * kk, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          } else {
+            const uint64_t ad = make_sdesc(p_addr + (kk >> 2) * (128 * 128) + (kk & 3) * 32, 16, 1024, UMMA_SW128);
+            umma_f16_ss(tmem + BN, ad, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          }
         }
         tc_commit(pv_done);
         tc_commit(&kv_empty[j & 1]);
@@ -288,12 +299,20 @@ __global__ void __launch_bounds__(192, 2)  // two CTAs per SM (registers <= 170)
         if (!ok) break;
         tc_fence_after();
       }
-      // P_j -> shared memory, 128B-swizzled K-major (keys contiguous), 64 keys per swizzle atom
+      if constexpr (C::P_TMEM) {
+        // P_j -> TMEM, keys 2i, 2i+1 in column TM_P + i (the PV MMA's A operand)
+        uint32_t pk[BN / 2];
 #pragma unroll
-      for (int ch = 0; ch < BN / 8; ++ch) {
-        const uint4 v = make_uint4(pack_half2(s[8 * ch + 0], s[8 * ch + 1]), pack_half2(s[8 * ch + 2], s[8 * ch + 3]),
-                                   pack_half2(s[8 * ch + 4], s[8 * ch + 5]), pack_half2(s[8 * ch + 6], s[8 * ch + 7]));
-        *reinterpret_cast<uint4*>(ps + (ch >> 3) * (128 * 128) + sw128_off(rl, ch & 7)) = v;
+        for (int i = 0; i < BN / 2; ++i) pk[i] = pack_half2(s[2 * i], s[2 * i + 1]);
+        tmem_st64(trow + C::TM_P, pk);
+      } else {
+        // P_j -> shared memory, 128B-swizzled K-major (keys contiguous), 64 keys per swizzle atom
+#pragma unroll
+        for (int ch = 0; ch < BN / 8; ++ch) {
+          const uint4 v = make_uint4(pack_half2(s[8 * ch + 0], s[8 * ch + 1]), pack_half2(s[8 * ch + 2], s[8 * ch + 3]),
+                                     pack_half2(s[8 * ch + 4], s[8 * ch + 5]), pack_half2(s[8 * ch + 6], s[8 * ch + 7]));
+          *reinterpret_cast<uint4*>(ps + (ch >> 3) * (128 * 128) + sw128_off(rl, ch & 7)) = v;
+        }
       }
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
@@ -305,7 +324,7 @@ __global__ void __launch_bounds__(192, 2)  // two CTAs per SM (registers <= 170)
           tmem_st32(trow + BN + c, o);
         }
       }
-      fence_proxy_async_smem();
+      if constexpr (!C::P_TMEM) fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_full);
     }
