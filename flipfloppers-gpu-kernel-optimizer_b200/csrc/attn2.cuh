@@ -209,55 +209,80 @@ __global__ void __launch_bounds__(320, 1)
     const int q_first = p.q_offset + qp * 256 + t * 128;
     const uint32_t trow = tmem + (static_cast<uint32_t>(qd * 32) << 16);
     const int nt = ntile[t];
+    // The two softmax warps that share an SMSP (quadrant qd of tile 0 and of
+    // tile 1) take turns on the exponentials: tile 0 waits for token A, tile 1
+    // for token B, each passes the other's token on when its exp loop is done.
+    // Alternating keeps the SFU busy while the other warp loads S, reduces the
+    // max and writes P.  Token k of each kind is passed only when its receiver
+    // has a k-th exp phase (tile 1 may have one key tile more, or none), and
+    // the sequence never depends on data or errors, so no wait is left
+    // unmatched.
+    const int n0 = ntile[0], n1 = ntile[1];
+    const int bar_a = 1 + qd, bar_b = 5 + qd;
+    if (t == 1 && n0 > 0) nbar_arrive(bar_a, 64);
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nt; ++j) {
-      ok = mbar_wait_warp(&s_full[t], j & 1, abort_flag, DERR_WAIT_MMA);
-      if (!ok) break;
-      tc_fence_after();
+      if (ok) ok = mbar_wait_warp(&s_full[t], j & 1, abort_flag, DERR_WAIT_MMA);
       float s[C::BN];
-      tmem_ld_row<C::BN>(trow + t * 128, s);
-      tc_fence_before();
-      mbar_arrive(&s_free[t]);  // the MMA warp may now overwrite S_t with the next key tile
-      const int k0 = j * C::BN;
-      const int klim = p.non_causal ? kv_eff - 1 : min(qpos, kv_eff - 1);  // last visible key of this row
-      const bool need_mask = (k0 + C::BN - 1) > (p.non_causal ? kv_eff - 1 : min(q_first, kv_eff - 1));
-      if (need_mask) {  // raw scores; the positive scale is applied in the exponent
-#pragma unroll
-        for (int c = 0; c < C::BN; ++c)
-          if (k0 + c > klim) s[c] = -INFINITY;
-      }
-      const float mx = row_max<C::BN>(s) * p.scale_log2;
-      // lazy rescale: move the reference max only when this tile raises it by more than the threshold
-      const bool grow = mx > m_used + C::RESCALE_THRESHOLD;
-      const float m_new = grow ? mx : m_used;
-      const float alpha = grow ? fast_exp2(m_used - m_new) : 1.f;  // 0 on the first tile
-      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-      l = l * alpha + row_exp2_sum<C::BN>(s, p.scale_log2, m_use);
-      m_used = m_new;
-      if (j > 0) {
-        ok = mbar_wait_warp(&pv_done[t], (j - 1) & 1, abort_flag, DERR_WAIT_MMA);
-        if (!ok) break;
+      float alpha = 1.f, m_use = 0.f;
+      if (ok) {
         tc_fence_after();
+        tmem_ld_row<C::BN>(trow + t * 128, s);
+        tc_fence_before();
+        mbar_arrive(&s_free[t]);  // the MMA warp may now overwrite S_t with the next key tile
+        const int k0 = j * C::BN;
+        const int klim = p.non_causal ? kv_eff - 1 : min(qpos, kv_eff - 1);  // last visible key of this row
+        const bool need_mask = (k0 + C::BN - 1) > (p.non_causal ? kv_eff - 1 : min(q_first, kv_eff - 1));
+        if (need_mask) {  // raw scores; the positive scale is applied in the exponent
+#pragma unroll
+          for (int c = 0; c < C::BN; ++c)
+            if (k0 + c > klim) s[c] = -INFINITY;
+        }
+        const float mx = row_max<C::BN>(s) * p.scale_log2;
+        // lazy rescale: move the reference max only when this tile raises it by more than the threshold
+        const bool grow = mx > m_used + C::RESCALE_THRESHOLD;
+        const float m_new = grow ? mx : m_used;
+        alpha = grow ? fast_exp2(m_used - m_new) : 1.f;  // 0 on the first tile
+        m_use = (m_new == -INFINITY) ? 0.f : m_new;
+        m_used = m_new;
+      } else {
+#pragma unroll
+        for (int c = 0; c < C::BN; ++c) s[c] = 0.f;  // keeps the exp phase unconditional
       }
-      {
+      if (t == 0) {
+        if (j == 0 || j - 1 < n1) nbar_sync(bar_a, 64);
+      } else {
+        if (j < n0) nbar_sync(bar_b, 64);
+      }
+      l = l * alpha + row_exp2_sum<C::BN>(s, p.scale_log2, m_use);
+      if (t == 0) {
+        if (j < n1) nbar_arrive(bar_b, 64);
+      } else {
+        if (j + 1 < n0) nbar_arrive(bar_a, 64);
+      }
+      if (ok && j > 0) {
+        ok = mbar_wait_warp(&pv_done[t], (j - 1) & 1, abort_flag, DERR_WAIT_MMA);
+        if (ok) tc_fence_after();
+      }
+      if (ok) {
         uint32_t pk[C::BN / 2];  // keys 2i, 2i+1 -> column i (low, high half)
 #pragma unroll
         for (int i = 0; i < C::BN / 2; ++i) pk[i] = pack_half2(s[2 * i], s[2 * i + 1]);
         tmem_st64(trow + C::TM_P + 64 * t, pk);
-      }
-      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
-        for (int c = 0; c < HD; c += 32) {
-          float o[32];
-          tmem_ld32(trow + 256 + t * HD + c, o);
+          for (int c = 0; c < HD; c += 32) {
+            float o[32];
+            tmem_ld32(trow + 256 + t * HD + c, o);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] *= alpha;
-          tmem_st32(trow + 256 + t * HD + c, o);
+            for (int i = 0; i < 32; ++i) o[i] *= alpha;
+            tmem_st32(trow + 256 + t * HD + c, o);
+          }
         }
+        tc_fence_before();
+        mbar_arrive(&p_full[t]);
       }
-      tc_fence_before();
-      mbar_arrive(&p_full[t]);
     }
     if (ok && nt > 0) ok = mbar_wait_warp(&pv_done[t], (nt - 1) & 1, abort_flag, DERR_WAIT_MMA);
     if (ok && nt > 0 && !*abort_flag) {

@@ -122,6 +122,18 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, v
 }
 
 
+// ---------------------------------------------------------------- named barriers
+// bar.sync waits until `count` threads (whole warps) have arrived on barrier
+// `id`; bar.arrive adds this warp without waiting.  Used as a token between
+// warps.  Neither has a timeout: callers keep their sequence of these calls
+// independent of data and errors, so every wait is matched by an arrival.
+__device__ __forceinline__ void nbar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ void nbar_arrive(int id, int count) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // ---------------------------------------------------------------- fences
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
