@@ -368,7 +368,7 @@ def main():
         if rank == 0:
             xp = x[:1].contiguous() if strong else x
             roof = roofline_pass(model, xp, mask, flush if flushes(args.config) else None, cfg,
-                                 steps=3 if strong else max(20, min(args.steps, 200)))
+                                 steps=3 if strong else max(20, min(args.steps, 200)), cfg_name=args.config)
             del xp
         e2e_serial_ms = None
         if strong:
@@ -455,7 +455,20 @@ def kernels_per_forward(model):
     return 8 * nl if nl == 1 else 7 * nl + 1
 
 
-def roofline_pass(model, x, mask, flush, cfg, steps):
+def measured_traffic(cfg_name, kernel):
+    """DRAM bytes per launch of `kernel` at `cfg_name` from the committed ncu summaries
+    (profiles/traffic.json), or (None, None) when no capture covers it."""
+    try:
+        with open(os.path.join(REPO, "profiles", "traffic.json")) as f:
+            t = json.load(f).get(cfg_name)
+    except (OSError, ValueError):
+        return None, None
+    if not t or t.get("kernel") != kernel:
+        return None, None
+    return int(t["bytes"]), "profiles/" + t["source"]
+
+
+def roofline_pass(model, x, mask, flush, cfg, steps, cfg_name=None):
     """Dominant-kernel roofline: per-stage CUDA-event timing of an eager pass on the same inputs."""
     import torch
     peaks = load_peaks()
@@ -480,7 +493,9 @@ def roofline_pass(model, x, mask, flush, cfg, steps):
     else:
         ach = by / (ms * 1e-3) / 1e9
         out = {"bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s"}
-    out.update(frac=out["achieved"] / out["peak"], traffic=None, kernel=name, ms_per_launch=ms,
+    traffic, traffic_src = measured_traffic(cfg_name, name)
+    out.update(frac=out["achieved"] / out["peak"], traffic=traffic, traffic_src=traffic_src, kernel=name,
+               ms_per_launch=ms,
                peak_src=f"{peaks['src']} (MEASURED_PEAKS.json burst)" if peaks["src"] == "measured" else "fallback",
                stage_ms=timing, algorithmic={"flops": fl, "bytes": by})
     return out
