@@ -18,6 +18,7 @@
  *                                                  -> b200_flash_causal_launch
  *   - F.layer_norm of norm1 / norm2 / final_norm
  *       (torch_transformer_benchmark.py:1293, 1348, 1373) -> b200_layernorm_launch
+ *       (norm1 together with the residual copy: b200_layernorm_residual_launch)
  *   - the per-layer body of _optimized_forward_causal
  *       (torch_transformer_benchmark.py:1282-1373)  -> b200_block_forward
  *   - the unwired causal megakernel mega_causal_forward
