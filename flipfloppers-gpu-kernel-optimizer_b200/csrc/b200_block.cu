@@ -456,11 +456,15 @@ int launch_attn2_t(const B200AttnArgs& a, cudaStream_t st) {
   return launch_status();
 }
 
-// B200_ATTN_ONE_TILE=1 selects the one-query-tile kernel for every shape (A/B comparisons).
-bool attn_one_tile_forced() {
-  static const bool forced = [] {
-    const char* e = getenv("B200_ATTN_ONE_TILE");
-    return e != nullptr && e[0] == '1';
+// B200_ATTN_TILES=1 / =2 forces the one- / two-query-tile kernel (head_dim 32
+// and 64) for every shape (A/B comparisons); unset: by sequence length.
+constexpr int ATTN_TWO_TILE_MIN_Q = 2048;
+constexpr int ATTN_TWO_TILE_MIN_Q_HD64 = 512;
+
+int attn_tiles_forced() {
+  static const int forced = [] {
+    const char* e = getenv("B200_ATTN_TILES");
+    return (e != nullptr && (e[0] == '1' || e[0] == '2')) ? e[0] - '0' : 0;
   }();
   return forced;
 }
@@ -485,10 +489,14 @@ int attn_impl(const B200AttnArgs* a, cudaStream_t st) {
     return B200_ERR_ARG;
   if (a->heads > 65535 || a->batch > 65535) return B200_ERR_TILE;
   if (int rc = check_arch()) return rc;
-  // Two query tiles per CTA pay off on long sequences (shared K/V loads, MMA of
-  // one tile under the other's softmax: 1.44x at S=8K-16K, head_dim 64); short
-  // sequences keep one tile per CTA and two CTAs per SM (1.2x at S=1024).
-  if (!attn_one_tile_forced() && a->q_len >= 2048) {
+  // Two query tiles per CTA (shared K/V loads, one tile's MMA under the other's
+  // softmax, alternating exp phases) against one tile per CTA with two CTAs per
+  // SM, measured (L2 flushed): head_dim 64 favours two tiles from short
+  // sequences on (B=16 S=1024 H=16: 107 vs 146 us; B=8 S=2048: 158 vs 223 us);
+  // head_dim 32 keeps one tile below S=2048 (B=64 S=1024 H=4: 86 vs 99 us).
+  const int forced = attn_tiles_forced();
+  const int min_q = hd == 64 ? ATTN_TWO_TILE_MIN_Q_HD64 : ATTN_TWO_TILE_MIN_Q;
+  if (forced == 2 || (forced == 0 && a->q_len >= min_q)) {
     if (hd == 32) return launch_attn2_t<32>(*a, st);
     if (hd == 64) return launch_attn2_t<64>(*a, st);
   }

@@ -296,3 +296,62 @@ print("OK")
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     r = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0 and "OK" in r.stdout, r.stdout + r.stderr
+
+
+@pytest.mark.parametrize("tiles", ["1", "2"])
+def test_flash_both_kernels_in_subprocess(tiles):
+    """The one- and the two-query-tile attention kernel (B200_ATTN_TILES forces
+    the choice for head_dim 32/64; read once per process) against torch fp32 on
+    shapes where the second query tile of a CTA is empty (S=300, S=384), where
+    both tiles need the same number of key tiles (non-causal) and where the
+    second needs one more (causal), with and without a prefix offset."""
+    import os
+    import subprocess
+    import sys
+    code = r'''
+import torch
+import torch_transformer_benchmark as T
+rt = T._pkg.runtime
+dev = "cuda"
+def ref_attn(q, k, v, q_offset, causal, lens=None):
+    hd = q.shape[-1]
+    s = (q @ k.transpose(-1, -2)) * hd ** -0.5
+    Sq, Sk = q.shape[-2], k.shape[-2]
+    if causal:
+        qpos = q_offset + torch.arange(Sq, device=dev)[:, None]
+        s = s.masked_fill(torch.arange(Sk, device=dev)[None, :] > qpos, float("-inf"))
+    if lens is not None:
+        km = torch.arange(Sk, device=dev)[None, :] >= lens[:, None].long()
+        s = s.masked_fill(km[:, None, None, :], float("-inf"))
+    return torch.softmax(s, -1) @ v
+worst = 0.0
+for (B, H, S, hd) in ((2, 2, 300, 64), (1, 2, 384, 32), (2, 2, 640, 64), (1, 3, 1000, 32), (1, 2, 1536, 64)):
+    d = H * hd
+    g = torch.Generator().manual_seed(S * 3 + hd)
+    qkv = torch.randn(B * S, 3 * d, generator=g).half().to(dev)
+    t = qkv.float().view(B, S, 3, H, hd).permute(2, 0, 3, 1, 4)
+    out = torch.full((B * S, d), float("nan"), dtype=torch.float16, device=dev)
+    rt.flash_causal(qkv, qkv, qkv, out, batch=B, heads=H, head_dim=hd, q_len=S, kv_len=S, k_col0=d, v_col0=2 * d)
+    ref = ref_attn(t[0], t[1], t[2], 0, True).permute(0, 2, 1, 3).reshape(B * S, d)
+    worst = max(worst, (out.float() - ref).abs().max().item())
+    lens = torch.tensor([S - 29 * (i + 1) for i in range(B)], dtype=torch.int32, device=dev)
+    rt.flash_causal(qkv, qkv, qkv, out, batch=B, heads=H, head_dim=hd, q_len=S, kv_len=S, k_col0=d, v_col0=2 * d,
+                    non_causal=True, kv_lens=lens)
+    ref = ref_attn(t[0], t[1], t[2], 0, False, lens).permute(0, 2, 1, 3).reshape(B * S, d)
+    worst = max(worst, (out.float() - ref).abs().max().item())
+    c0 = S // 3  # queries [c0, S) over keys [0, S): prefix offset c0
+    part = torch.full((B * S, d), float("nan"), dtype=torch.float16, device=dev)
+    rt.flash_causal(qkv, qkv, qkv, part, batch=B, heads=H, head_dim=hd, q_len=S - c0, q_offset=c0, kv_len=S,
+                    q_seq_rows=S, kv_seq_rows=S, q_row0=c0, k_col0=d, v_col0=2 * d, out_seq_rows=S, out_row0=c0)
+    ref = ref_attn(t[0], t[1], t[2], 0, True).permute(0, 2, 1, 3)
+    got = part.float().view(B, S, H, hd)[:, c0:]
+    worst = max(worst, (got - ref[:, c0:]).abs().max().item())
+torch.cuda.synchronize()
+assert worst < 4e-3, worst
+assert rt.device_error(clear=True) == 0
+print("OK", worst)
+'''
+    env = dict(os.environ, B200_ATTN_TILES=tiles)
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "OK" in r.stdout, r.stdout + r.stderr
