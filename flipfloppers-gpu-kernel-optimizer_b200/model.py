@@ -442,11 +442,12 @@ class UserOptimizedTransformer(nn.Module):
         """Forward of a HOST tensor into a host tensor, pipelined across calls.
 
         Three CUDA streams carry call i's upload (pinned H2D of x into device
-        slot i % 2), its forward (graph replay on that slot) and its download
+        slot i % n), its forward (graph replay on that slot) and its download
         (D2H of y into ``out``), ordered by events, so that consecutive calls
         overlap one call's download, the next call's forward and the one
         after's upload -- the way a serving loop keeps PCIe busy in both
-        directions.  ``wait=False`` returns as soon as the work is queued;
+        directions.  n = 2 slots (a third slot was measured and did not
+        shorten the steady-state step: the copies bound it).  ``wait=False`` returns as soon as the work is queued;
         ``out`` is valid after ``synchronize_host()``.  Pass pinned tensors for
         the copies to be asynchronous.  ``flush`` (a device buffer) is zeroed on
         the forward stream before the forward, for benchmarks that flush L2.
@@ -459,19 +460,20 @@ class UserOptimizedTransformer(nn.Module):
             out = torch.empty(x_host.shape, dtype=torch.float32, pin_memory=True)
         i = pipe["calls"]
         pipe["calls"] += 1
-        slot = i % 2
+        nslot = len(pipe["x"])
+        slot = i % nslot
         xd, yd = pipe["x"][slot], pipe["y"][slot]
         ev = pipe["ev"][slot]
         with torch.cuda.device(dev):
             up, comp, down = pipe["streams"]
             with torch.cuda.stream(up):
-                if i >= 2:
+                if i >= nslot:
                     up.wait_event(ev["comp"])      # slot's previous forward has read x
                 xd.copy_(x_host, non_blocking=True)
                 ev["up"].record(up)
             with torch.cuda.stream(comp):
                 comp.wait_event(ev["up"])
-                if i >= 2:
+                if i >= nslot:
                     comp.wait_event(ev["down"])    # slot's previous y has been downloaded
                 if flush is not None:
                     flush.zero_()
@@ -489,7 +491,13 @@ class UserOptimizedTransformer(nn.Module):
         """Event recorded after the last queued ``forward_host`` download of ``shape``."""
         dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         pipe = self._pipe_state(tuple(shape), dev)
-        return pipe["ev"][(pipe["calls"] - 1) % 2]["down"]
+        return pipe["ev"][(pipe["calls"] - 1) % len(pipe["x"])]["down"]
+
+    def host_pipe_wait(self, event: "torch.cuda.Event", shape, device=None) -> None:
+        """Make the next ``forward_host`` upload of ``shape`` wait for ``event``
+        (e.g. a timing event recorded on another stream)."""
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        self._pipe_state(tuple(shape), dev)["streams"][0].wait_event(event)
 
     def synchronize_host(self) -> None:
         """Wait until every queued ``forward_host`` download has landed."""
@@ -501,13 +509,14 @@ class UserOptimizedTransformer(nn.Module):
         key = (shape, dev.index)
         pipe = pipes.get(key)
         if pipe is None:
+            nslot = 2
             with torch.cuda.device(dev):
                 pipe = {
                     "calls": 0,
-                    "x": [torch.empty(shape, dtype=torch.float32, device=dev) for _ in range(2)],
-                    "y": [torch.empty(shape, dtype=torch.float32, device=dev) for _ in range(2)],
+                    "x": [torch.empty(shape, dtype=torch.float32, device=dev) for _ in range(nslot)],
+                    "y": [torch.empty(shape, dtype=torch.float32, device=dev) for _ in range(nslot)],
                     "streams": [torch.cuda.Stream(device=dev) for _ in range(3)],
-                    "ev": [{k: torch.cuda.Event() for k in ("up", "comp", "down")} for _ in range(2)],
+                    "ev": [{k: torch.cuda.Event() for k in ("up", "comp", "down")} for _ in range(nslot)],
                 }
             pipes[key] = pipe
         return pipe
