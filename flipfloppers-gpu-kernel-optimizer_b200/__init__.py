@@ -8,9 +8,11 @@ name is not a Python identifier):
   LayerNorm, and the C ABI (``include/b200_block.h``) in one translation unit;
 * ``build.py`` -- nvcc recipe producing ``lib/libb200block.so`` in-tree;
 * ``runtime.py`` -- ctypes binding of the C ABI;
+* ``ops.py`` -- the PyTorch op layer (``torch.ops.b200.*`` custom ops with fake
+  implementations, for torch.compile and graph capture);
 * ``model.py`` -- the drop-in ``UserOptimizedTransformer`` and its arbiter;
 * ``parallel.py`` -- one-process-per-GPU batch sharding and tensor parallelism.
 """
 
-from . import build, parallel, runtime  # noqa: F401
+from . import build, ops, parallel, runtime  # noqa: F401
 from .model import TransformerConfig, UserOptimizedTransformer  # noqa: F401
