@@ -73,6 +73,11 @@ def rank_batch(cfg_name, rank, world):
     return B
 
 
+# exact sampled-row check of the multi-GB configuration: rows of sequence 0 (causal,
+# one layer: row t depends only on rows 0..t)
+SAMPLED_PREFIX = 16384
+SAMPLED_ROWS = sorted(SAMPLED_PREFIX - 1 - 2047 * i for i in range(8))  # ascending, as the oracle returns them
+
 # ~20 ms of device-side spinning queued ahead of the timed steps
 QUEUE_PREFILL_CYCLES = 40_000_000
 
@@ -183,7 +188,7 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- CPU baseline (oracle port)
-def cpu_sampled_rows_estimate(cfg_name):
+def cpu_sampled_rows_estimate(cfg_name, x_seq=None):
     """C5 cannot run on the CPU unchunked (its score tensor alone is ~20 TB): time the exact
     sampled-row restatement (oracle.sampled_rows_forward) on one sequence and extrapolate a
     full forward as B x (K/V-prefix projection + sum over rows of the per-row cost, which
@@ -196,14 +201,14 @@ def cpu_sampled_rows_estimate(cfg_name):
     except Exception:  # noqa: BLE001
         cores = os.cpu_count() or 1
     B, S, d, H, F, L = CONFIGS[cfg_name]
-    T = 16384  # prefix sampled
+    T = SAMPLED_PREFIX  # prefix sampled
     params = oracle.params_from_state_dict(oracle.init_state_dict(1, d, F, 1234))
-    x = oracle.generate_chunked_input(1, S, d, seed=1234, rows=T)[0].numpy()
+    x = oracle.generate_chunked_input(1, S, d, seed=1234, rows=T)[0].numpy() if x_seq is None else x_seq[:T]
     t0 = time.perf_counter()
     oracle.sampled_rows_forward(params, H, x, [T - 1], key_block=8192)
     t_one = time.perf_counter() - t0             # K/V prefix of T rows + one row at position T-1
     t0 = time.perf_counter()
-    oracle.sampled_rows_forward(params, H, x, [T - 1 - i for i in range(8)], key_block=8192)
+    y_rows = oracle.sampled_rows_forward(params, H, x, SAMPLED_ROWS, key_block=8192)
     t_nine = time.perf_counter() - t0
     per_row_at_T = max((t_nine - t_one) / 7, 1e-6)  # marginal cost of a row with a T-key prefix
     kv = max(t_one - per_row_at_T, 1e-6) * S / T     # K/V projections scale with the prefix length
@@ -212,7 +217,13 @@ def cpu_sampled_rows_estimate(cfg_name):
     return {"value": B * S / est, "unit": "tokens/s", "cores": int(cores), "kind": "port",
             "sample": f"ESTIMATE: oracle.sampled_rows_forward on one sequence prefix of {T} rows "
                       f"(K/V prefix {t_one:.1f} s, marginal row {per_row_at_T * 1e3:.1f} ms at {T} keys), "
-                      f"extrapolated to B={B} x S={S}: {est / 60:.1f} min per forward"}, est, 1
+                      f"extrapolated to B={B} x S={S}: {est / 60:.1f} min per forward"}, est, 1, y_rows
+
+
+def cpu_sample_batch(cfg_name):
+    """Sequences in the CPU leg's bounded sample of the workload (the first ones of the timed input)."""
+    B, S = CONFIGS[cfg_name][:2]
+    return B if B * S <= 16384 else max(1, 16384 // S)
 
 
 def cpu_forward_rate(cfg_name, budget_s=12.0, min_reps=1):
@@ -227,24 +238,25 @@ def cpu_forward_rate(cfg_name, budget_s=12.0, min_reps=1):
     except Exception:  # noqa: BLE001
         cores = os.cpu_count() or 1
     B, S, d, H, F, L = CONFIGS[cfg_name]
-    Bs = B if B * S <= 16384 else max(1, 16384 // S)   # bounded sample of the workload
+    Bs = cpu_sample_batch(cfg_name)
     params = oracle.params_from_state_dict(oracle.init_state_dict(L, d, F, 1234))
     x, _ = oracle.generate_random_case(Bs, S, d, 1234 + 100000)
     xn = x.numpy()
     cfg = oracle.OracleConfig(Bs, S, d, H, F, L, True)
     oracle.model_forward(params, cfg, xn[:1])  # warm BLAS
     times = []
+    y_ref = None
     t_end = time.perf_counter() + budget_s
     while len(times) < min_reps or time.perf_counter() < t_end:
         t0 = time.perf_counter()
-        oracle.model_forward(params, cfg, xn)
+        y_ref = oracle.model_forward(params, cfg, xn)
         times.append(time.perf_counter() - t0)
         if len(times) >= 50:
             break
     med = statistics.median(times)
     return {"value": Bs * S / med, "unit": "tokens/s", "cores": int(cores), "kind": "port",
             "sample": f"{len(times)} forwards of B={Bs} x S={S} (NumPy fp32 restatement of the reference "
-                      f"module, oracle/), median {med * 1e3:.1f} ms"}, med, Bs
+                      f"module, oracle/), median {med * 1e3:.1f} ms"}, med, Bs, y_ref
 
 
 def run_reference(args, rank, world):
@@ -254,7 +266,7 @@ def run_reference(args, rank, world):
     import numpy as np
     import oracle
     if args.config in STRONG:
-        base, est, _ = cpu_sampled_rows_estimate(args.config)
+        base, est, _, _ = cpu_sampled_rows_estimate(args.config)
         line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": "tokens/s",
                 "n_gpus": args.gpus, "steps": 1, "warmup": 0, "ms_per_step": est * 1e3, "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "f32",
@@ -263,7 +275,7 @@ def run_reference(args, rank, world):
                 "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return 0
-    base, med, Bs = cpu_forward_rate(args.config, budget_s=0.0, min_reps=1)
+    base, med, Bs, _ = cpu_forward_rate(args.config, budget_s=0.0, min_reps=1)
     params = oracle.params_from_state_dict(oracle.init_state_dict(L, d, F, 1234))
     x, _ = oracle.generate_random_case(Bs, S, d, 1234 + 100000)
     xn = x.numpy()
@@ -370,6 +382,13 @@ def main():
             roof = roofline_pass(model, xp, mask, flush if flushes(args.config) else None, cfg,
                                  steps=3 if strong else max(20, min(args.steps, 200)), cfg_name=args.config)
             del xp
+        # GPU outputs compared with the oracle in the CPU leg (rank 0, one GPU)
+        y_check = None
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            if strong:
+                y_check = model(x[:1].contiguous(), mask[:1])[0, SAMPLED_ROWS].float().cpu()
+            else:
+                y_check = model(x, mask)[:cpu_sample_batch(args.config)].float().cpu()
         e2e_serial_ms = None
         if strong:
             del x  # make room for the two pipeline slots
@@ -421,8 +440,20 @@ def main():
     launches_per_step = kernels_per_forward(model)
 
     cpu = None
+    accuracy = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_forward_rate(args.config)[0]
+        import oracle
+        if strong:
+            cpu, _, _, y_ref = cpu_sampled_rows_estimate(args.config, x_seq=x_host[0].numpy())
+            acc = oracle.compare_outputs(y_ref, y_check.numpy())
+            sample = f"rows {SAMPLED_ROWS} of sequence 0 (exact sampled-row restatement)"
+        else:
+            cpu, _, Bs, y_ref = cpu_forward_rate(args.config)
+            acc = oracle.compare_outputs(y_ref, y_check.numpy())
+            sample = f"sequences 0..{Bs - 1} of the timed input"
+        accuracy = {"max_abs": acc.max_abs_error, "max_rel": acc.max_relative_error, "failed": acc.failed_elements,
+                    "total": acc.total_elements, "rule": "atol 0.002 OR rtol 0.02 (reference harness)",
+                    "vs": "oracle/ (NumPy fp32 restatement of the reference module)", "sample": sample}
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_total / args.steps, "higher_is_better": True,
@@ -439,7 +470,7 @@ def main():
                             "value": tokens_all * args.steps / (e2e_serial_ms / 1e3),
                             "ms_per_step": e2e_serial_ms / args.steps,
                             "api": "UserOptimizedTransformer.__call__ with H2D/D2H on one stream"}},
-                "roofline": roof, "cpu_baseline": cpu, "clocks": clocks,
+                "roofline": roof, "cpu_baseline": cpu, "accuracy": accuracy, "clocks": clocks,
                 "gpu_launches": launches_per_step * args.steps}
         print(json.dumps(line), flush=True)
     if world > 1:

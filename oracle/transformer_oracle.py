@@ -184,7 +184,7 @@ def sampled_rows_forward(params: Dict[str, np.ndarray], num_heads: int, x_seq: n
     operations as :func:`model_forward`, restricted to the needed rows.  Used
     for the S=100000 configuration, whose score tensor cannot be materialised.
 
-    x_seq: [S, d] one sequence.  Returns [len(rows), d].
+    x_seq: [S, d] one sequence.  Returns [len(set(rows)), d], rows in ascending order.
     """
     rows = np.asarray(sorted(set(int(r) for r in rows)), dtype=np.int64)
     x_seq = np.asarray(x_seq)
