@@ -128,6 +128,9 @@ def stage_work(B, S, d, H, F):
         "ffn_in": (2 * M * d * F, M * d * 2 + F * d * 2 + M * F * 2 + 4 * F),
         "ffn_out": (2 * M * F * d, M * F * 2 + F * d * 2 + M * d * 4 * 2 + 4 * d),
         "ln_f": (8 * M * d, M * d * 4 * 2 + 8 * d),
+        # residual projections with the following LayerNorm in the epilogue (d == 128)
+        "out_proj_ln2": (2 * M * d * d + 8 * M * d, M * d * 2 + d * d * 2 + M * d * 4 * 2 + M * d * 2 + 12 * d),
+        "ffn_out_lnf": (2 * M * F * d + 8 * M * d, M * F * 2 + F * d * 2 + M * d * 4 * 2 + 12 * d),
     }
 
 

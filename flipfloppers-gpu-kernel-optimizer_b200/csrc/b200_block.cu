@@ -170,13 +170,13 @@ int make_map_f32_seq(CUtensorMap* m, const void* base, uint64_t num_seq, uint64_
 // ------------------------------------------------------------------ GEMM
 template <int BN, int STAGES, int EPI>
 int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const GemmParams& p,
-                  cudaStream_t st) {
+                  cudaStream_t st, const CUtensorMap* tn = nullptr) {
   auto kern = k_gemm_tn<BN, STAGES, EPI>;
-  const int smem = GemmSmem<BN, STAGES>::TOTAL;
+  const int smem = GemmSmem<BN, STAGES, EPI>::TOTAL;
   if (int rc = set_smem(reinterpret_cast<const void*>(kern), smem)) return rc;
   const long long tiles = static_cast<long long>((p.M + 127) / 128) * ((p.N + BN - 1) / BN);
   const int grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
-  kern<<<grid, GEMM_THREADS, smem, st>>>(ta, tw, to, p);
+  kern<<<grid, GEMM_THREADS, smem, st>>>(ta, tw, to, tn ? *tn : to, p);
   return launch_status();
 }
 
@@ -305,6 +305,60 @@ int gemm_impl(int epi, const void* A, long long lda, const void* W, long long ld
   }
   if (BN == 256) return launch_gemm_bn<256, 4>(epi, ta, tw, to, p, st);
   return launch_gemm_bn<128, 6>(epi, ta, tw, to, p, st);
+}
+
+// The chain fuses the residual projections with the following LayerNorm when a
+// 128-column tile holds the whole row (d == 128); B200_GEMM_LN=0 keeps the
+// separate LayerNorm kernel (A/B comparisons).
+bool fuse_ln(int d) {
+  static const bool on = [] {
+    const char* e = std::getenv("B200_GEMM_LN");
+    return e == nullptr || e[0] != '0';
+  }();
+  return on && d == 128;
+}
+
+// out_proj / ffn_out with the residual add and the following LayerNorm in the
+// epilogue (one 128-column tile holds a whole row, so N must be 128):
+//   res[M,N] holds the residual on entry;  v = res + A.W^T + bias;
+//   ln_f16:  res = v (x1, in place) and ln_out = LN(v)*gamma + beta in fp16;
+//   !ln_f16: ln_out = LN(v)*gamma + beta in fp32 (res is left unchanged).
+int gemm_ln_impl(const void* A, long long lda, const void* W, long long ldw, const float* bias, float* res,
+                 long long ld_res, const float* gamma, const float* beta, float eps, void* ln_out, long long ld_ln,
+                 int ln_f16, int M, int N, int K, cudaStream_t st) {
+  if (!A || !W || !res || !gamma || !beta || !ln_out || M < 0 || K <= 0) return B200_ERR_ARG;
+  if (M == 0) return B200_OK;
+  if (N != 128) return B200_ERR_CONFIG;
+  if (K % 8 || lda % 8 || ldw % 8 || lda < K || ldw < K) return B200_ERR_TILE;
+  if (ld_res < N || ld_res % 4 || ld_ln < N || ld_ln % (ln_f16 ? 8 : 4)) return B200_ERR_ALIGN;
+  if (!al16(A) || !al16(W) || !al16(res) || !al16(ln_out) || !al16(gamma) || !al16(beta) || (bias && !al16(bias)))
+    return B200_ERR_ALIGN;
+  if (int rc = check_arch()) return rc;
+  CUtensorMap ta, tw, tx, tn;
+  if (int rc = make_map_f16(&ta, A, M, K, lda, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
+  if (int rc = make_map_f16(&tw, W, N, K, ldw, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
+  if (int rc = make_map_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, res, M, N, ld_res, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B))
+    return rc;
+  if (ln_f16) {
+    if (int rc = make_map_2d(&tn, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ln_out, M, N, ld_ln, 64, 32,
+                             CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+  } else {
+    if (int rc = make_map_2d(&tn, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ln_out, M, N, ld_ln, 32, 32,
+                             CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+  }
+  GemmParams p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.a_row0 = 0;
+  p.bias = bias;
+  p.gamma = gamma;
+  p.beta = beta;
+  p.eps = eps;
+  if (ln_f16) return launch_gemm_t<128, 3, EPI_BIAS_RESID_LN16>(ta, tw, tx, p, st, &tn);
+  return launch_gemm_t<128, 3, EPI_BIAS_RESID_LN32>(ta, tw, tx, p, st, &tn);
 }
 
 // ------------------------------------------------------------------ LayerNorm
@@ -641,17 +695,27 @@ int block_impl(const B200BlockArgs* a, cudaStream_t st) {
   at.non_causal = a->non_causal;
   at.kv_lens = a->kv_lens;
   if ((rc = attn_impl(&at, st))) return rc;
-  // 4. x1 = x + ctx . Wo^T + bo  (res += ...)
-  if ((rc = gemm_impl(EPI_BIAS_RESID_F32, w.ctx, d, a->w_o, d, a->b_o, res, d, res, d, static_cast<int>(M), d, d,
-                      st)))
-    return rc;
-  // 5. n = LN2(x1)
-  if ((rc = ln_impl(res, d, a->ln2_w, a->ln2_b, w.n, d, 1, static_cast<int>(M), d, a->eps, st))) return rc;
+  // 4. x1 = x + ctx . Wo^T + bo  (res += ...);  5. n = LN2(x1) -- one kernel when d == 128
+  if (fuse_ln(d)) {
+    if ((rc = gemm_ln_impl(w.ctx, d, a->w_o, d, a->b_o, res, d, a->ln2_w, a->ln2_b, a->eps, w.n, d, 1,
+                           static_cast<int>(M), d, d, st)))
+      return rc;
+  } else {
+    if ((rc = gemm_impl(EPI_BIAS_RESID_F32, w.ctx, d, a->w_o, d, a->b_o, res, d, res, d, static_cast<int>(M), d, d,
+                        st)))
+      return rc;
+    if ((rc = ln_impl(res, d, a->ln2_w, a->ln2_b, w.n, d, 1, static_cast<int>(M), d, a->eps, st))) return rc;
+  }
   // 6. h = gelu(n . W1^T + b1)
   if ((rc = gemm_impl(EPI_BIAS_GELU_F16, w.n, d, a->w_in, d, a->b_in, nullptr, 0, w.h, F, static_cast<int>(M), F, d,
                       st)))
     return rc;
-  // 7. x2 = x1 + h . W2^T + b2  (res += ...; without a final norm res is y)
+  // 7. x2 = x1 + h . W2^T + b2  (res += ...; without a final norm res is y);
+  //    8. y = LN_f(x2) in the same kernel when d == 128
+  if (a->lnf_w && fuse_ln(d)) {
+    return gemm_ln_impl(w.h, F, a->w_out, F, a->b_out, res, d, a->lnf_w, a->lnf_b, a->eps, a->y, d, 0,
+                        static_cast<int>(M), d, F, st);
+  }
   if ((rc = gemm_impl(EPI_BIAS_RESID_F32, w.h, F, a->w_out, F, a->b_out, res, d, res, d, static_cast<int>(M), d, F,
                       st)))
     return rc;
@@ -757,9 +821,21 @@ int block_chunked_impl(const B200BlockArgs* a, int chunk_rows, cudaStream_t st) 
       at.out_seq_rows = Rc;
       at.out_row0 = 0;
       if ((rc = attn_impl(&at, st))) return rc;
-      if ((rc = gemm_impl(EPI_BIAS_RESID_F32, w.ctx, d, a->w_o, d, a->b_o, res, d, res, d, Rc, d, d, st))) return rc;
-      if ((rc = ln_impl(res, d, a->ln2_w, a->ln2_b, w.n, d, 1, Rc, d, a->eps, st))) return rc;
+      if (fuse_ln(d)) {
+        if ((rc = gemm_ln_impl(w.ctx, d, a->w_o, d, a->b_o, res, d, a->ln2_w, a->ln2_b, a->eps, w.n, d, 1, Rc, d, d,
+                               st)))
+          return rc;
+      } else {
+        if ((rc = gemm_impl(EPI_BIAS_RESID_F32, w.ctx, d, a->w_o, d, a->b_o, res, d, res, d, Rc, d, d, st))) return rc;
+        if ((rc = ln_impl(res, d, a->ln2_w, a->ln2_b, w.n, d, 1, Rc, d, a->eps, st))) return rc;
+      }
       if ((rc = gemm_impl(EPI_BIAS_GELU_F16, w.n, d, a->w_in, d, a->b_in, nullptr, 0, w.h, F, Rc, F, d, st))) return rc;
+      if (a->lnf_w && fuse_ln(d)) {
+        if ((rc = gemm_ln_impl(w.h, F, a->w_out, F, a->b_out, res, d, a->lnf_w, a->lnf_b, a->eps, yr, d, 0, Rc, d, F,
+                               st)))
+          return rc;
+        continue;
+      }
       if ((rc = gemm_impl(EPI_BIAS_RESID_F32, w.h, F, a->w_out, F, a->b_out, res, d, res, d, Rc, d, F, st))) return rc;
       if (a->lnf_w && (rc = ln_impl(w.x1, d, a->lnf_w, a->lnf_b, yr, d, 0, Rc, d, a->eps, st))) return rc;
     }
@@ -815,6 +891,14 @@ int b200_device_error(int clear) {
 int b200_layernorm_launch(const float* x, long long ld_x, const float* gamma, const float* beta, void* out,
                           long long ld_out, int out_f16, int rows, int d, float eps, b200_stream_t stream) {
   return ln_impl(x, ld_x, gamma, beta, out, ld_out, out_f16, rows, d, eps, static_cast<cudaStream_t>(stream));
+}
+
+int b200_gemm_residual_layernorm_launch(const void* A, long long lda, const void* W, long long ldw, const float* bias,
+                                        float* res, long long ld_res, const float* gamma, const float* beta, float eps,
+                                        void* ln_out, long long ld_ln, int ln_out_f16, int M, int N, int K,
+                                        b200_stream_t stream) {
+  return gemm_ln_impl(A, lda, W, ldw, bias, res, ld_res, gamma, beta, eps, ln_out, ld_ln, ln_out_f16, M, N, K,
+                      static_cast<cudaStream_t>(stream));
 }
 
 int b200_layernorm_residual_launch(const float* x, long long ld_x, const float* gamma, const float* beta, void* out,

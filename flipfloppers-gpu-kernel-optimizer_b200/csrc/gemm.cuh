@@ -34,21 +34,41 @@
 
 namespace b200 {
 
-enum GemmEpilogue : int { EPI_BIAS_F16 = 0, EPI_BIAS_GELU_F16 = 1, EPI_BIAS_RESID_F32 = 2, EPI_BIAS_F32 = 3 };
+enum GemmEpilogue : int {
+  EPI_BIAS_F16 = 0,
+  EPI_BIAS_GELU_F16 = 1,
+  EPI_BIAS_RESID_F32 = 2,
+  EPI_BIAS_F32 = 3,
+  // x1 = out + acc + bias (out holds the residual; x1 written back to out) and
+  // ln_out = LayerNorm(x1)*gamma + beta in fp16 -- out_proj + residual + LN2
+  EPI_BIAS_RESID_LN16 = 4,
+  // ln_out = LayerNorm(out + acc + bias)*gamma + beta in fp32, out untouched --
+  // ffn_out + residual + final norm
+  EPI_BIAS_RESID_LN32 = 5,
+};
+__host__ __device__ constexpr bool epi_is_ln(int e) { return e == EPI_BIAS_RESID_LN16 || e == EPI_BIAS_RESID_LN32; }
 
 struct GemmParams {
   int M, N, K;
   int a_row0;            // first row of A addressed by the tensor map (row offset of this call)
   const float* bias;     // [N] fp32, may be null
+  const float* gamma;    // LayerNorm epilogues: [N] fp32
+  const float* beta;
+  float eps;
 };
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int EPI = EPI_BIAS_F16>
 struct GemmSmem {
   static constexpr int A_BYTES = 128 * 64 * 2;
   static constexpr int B_BYTES = BN * 64 * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STG_OFF = STAGES * STAGE_BYTES;  // epilogue staging: 8 warps x 2 slots x 2 KB
-  static constexpr int BAR_OFF = STG_OFF + 8 * 4096;
+  // epilogue staging per warp: two 2 KB slots, or for the LayerNorm epilogues the
+  // warp's 32 rows x 64 columns of the residual (fp32, two SW128 boxes) + the
+  // fp16 LayerNorm output box
+  static constexpr int STG_WARP = epi_is_ln(EPI) ? 12288 : 4096;
+  static constexpr int STG_OFF = STAGES * STAGE_BYTES;
+  static constexpr int STATS_OFF = STG_OFF + 8 * STG_WARP;             // LN row statistics [2][2][128] fp32
+  static constexpr int BAR_OFF = STATS_OFF + (epi_is_ln(EPI) ? 2048 : 0);
   static constexpr int TOTAL = BAR_OFF + 256 + 1024;  // barriers + 1 KB alignment slack
 };
 
@@ -115,11 +135,110 @@ __device__ __forceinline__ void gemm_epilogue_cols(const CUtensorMap* tmO, const
   }
 }
 
+// LayerNorm epilogue of one 128-column tile (the whole row: N == 128) for one
+// epilogue warp: rows row0 .. row0+31 (TMEM lane quadrant q), columns
+// 64*half .. +64, accumulator already in v.  The warp's residual box pair has
+// been TMA-loaded into stg; v = residual + acc + bias, row mean/variance
+// combined with the other half-warp of the quadrant through `stats` behind
+// named barrier 1+q, then x1 (LN16) and the normalised row leave by TMA store
+// (skipped when !ok; the barriers are always executed, so the partner warp is
+// never left waiting).
+template <int EPI>
+__device__ __forceinline__ void gemm_epilogue_ln(const CUtensorMap* tmX, const CUtensorMap* tmN, const GemmParams& p,
+                                                 float (&v)[64], int row0, int q, int half, uint8_t* stg,
+                                                 float* stats, int lane, bool ok) {
+  const int c0 = 64 * half;
+  const uint32_t sw = static_cast<uint32_t>(lane & 7);
+  // v += residual (two SW128 fp32 boxes of 32 columns) + bias
+#pragma unroll
+  for (int bx = 0; bx < 2; ++bx) {
+    const uint8_t* box = stg + bx * 4096 + lane * 128;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 r = *reinterpret_cast<const float4*>(box + ((j ^ sw) << 4));
+      const float4 bb = p.bias ? __ldg(reinterpret_cast<const float4*>(p.bias + c0 + 32 * bx + 4 * j))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+      float* w = v + 32 * bx + 4 * j;
+      w[0] += r.x + bb.x; w[1] += r.y + bb.y; w[2] += r.z + bb.z; w[3] += r.w + bb.w;
+    }
+  }
+  // row statistics over the 128 columns (two-pass), shared with the other half
+  const int r = q * 32 + lane;
+  float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+  for (int i = 0; i < 64; i += 2) { s0 += v[i]; s1 += v[i + 1]; }
+  stats[half * 128 + r] = s0 + s1;
+  nbar_sync(1 + q, 64);
+  const float mean = (stats[r] + stats[128 + r]) * (1.f / 128.f);
+  float q0 = 0.f, q1 = 0.f;
+#pragma unroll
+  for (int i = 0; i < 64; i += 2) {
+    const float a = v[i] - mean, b = v[i + 1] - mean;
+    q0 += a * a; q1 += b * b;
+  }
+  stats[256 + half * 128 + r] = q0 + q1;
+  nbar_sync(1 + q, 64);
+  const float rstd = rsqrtf((stats[256 + r] + stats[384 + r]) * (1.f / 128.f) + p.eps);
+  if constexpr (EPI == EPI_BIAS_RESID_LN16) {
+    // x1 back into the residual boxes (stored in place), LayerNorm output to the fp16 box
+#pragma unroll
+    for (int bx = 0; bx < 2; ++bx) {
+      uint8_t* box = stg + bx * 4096 + lane * 128;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float* w = v + 32 * bx + 4 * j;
+        *reinterpret_cast<float4*>(box + ((j ^ sw) << 4)) = make_float4(w[0], w[1], w[2], w[3]);
+      }
+    }
+    uint8_t* nbox = stg + 8192 + lane * 128;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float y[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int c = 8 * j + e;
+        y[e] = (v[c] - mean) * rstd * __ldg(p.gamma + c0 + c) + __ldg(p.beta + c0 + c);
+      }
+      *reinterpret_cast<uint4*>(nbox + ((j ^ sw) << 4)) =
+          make_uint4(pack_half2(y[0], y[1]), pack_half2(y[2], y[3]), pack_half2(y[4], y[5]), pack_half2(y[6], y[7]));
+    }
+  } else {
+    // the normalised row, fp32, into the residual boxes
+#pragma unroll
+    for (int bx = 0; bx < 2; ++bx) {
+      uint8_t* box = stg + bx * 4096 + lane * 128;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int c = 32 * bx + 4 * j;
+        const float4 g = __ldg(reinterpret_cast<const float4*>(p.gamma + c0 + c));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(p.beta + c0 + c));
+        *reinterpret_cast<float4*>(box + ((j ^ sw) << 4)) =
+            make_float4((v[c] - mean) * rstd * g.x + b.x, (v[c + 1] - mean) * rstd * g.y + b.y,
+                        (v[c + 2] - mean) * rstd * g.z + b.z, (v[c + 3] - mean) * rstd * g.w + b.w);
+      }
+    }
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0 && ok) {
+    if constexpr (EPI == EPI_BIAS_RESID_LN16) {
+      tma_store_2d(tmX, stg, c0, row0);
+      tma_store_2d(tmX, stg + 4096, c0 + 32, row0);
+      tma_store_2d(tmN, stg + 8192, c0, row0);
+    } else {
+      tma_store_2d(tmN, stg, c0, row0);
+      tma_store_2d(tmN, stg + 4096, c0 + 32, row0);
+    }
+    bulk_commit();
+  }
+}
+
 template <int BN, int STAGES, int EPI>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     k_gemm_tn(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
-              const __grid_constant__ CUtensorMap tmO, const GemmParams p) {
-  using L = GemmSmem<BN, STAGES>;
+              const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmN,
+              const GemmParams p) {
+  using L = GemmSmem<BN, STAGES, EPI>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_align1024(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
@@ -127,7 +246,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   uint64_t* acc_full = empty + STAGES;   // [2]
   uint64_t* acc_empty = acc_full + 2;    // [2]
   uint64_t* drain = acc_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* rbar = drain + 1;            // [8] LayerNorm epilogues: residual box loads, one per epilogue warp
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -148,6 +268,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       mbar_init(&acc_empty[b], 256);  // every epilogue thread arrives once per tile
     }
     mbar_init(drain, 1);
+    for (int w = 0; w < 8; ++w) mbar_init(&rbar[w], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -218,6 +339,52 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         mbar_wait_drain(drain, 0);
       }
     }
+  } else if constexpr (epi_is_ln(EPI)) {
+    // LayerNorm epilogue warps 2..9 (N == BN == 128: every tile holds whole rows).
+    // No early exit: the quadrant's two warps meet at named barriers each tile,
+    // so after a failed wait a warp keeps stepping through the tiles with its
+    // loads, waits and stores switched off.
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    uint8_t* stg = smem + L::STG_OFF + (warp - 2) * L::STG_WARP;
+    float* stats = reinterpret_cast<float*>(smem + L::STATS_OFF);
+    uint64_t* my_rbar = rbar + (warp - 2);
+    if (lane == 0) {
+      tma_prefetch_desc(&tmO);
+      tma_prefetch_desc(&tmN);
+    }
+    bool ok = true;
+    int loads = 0;         // residual loads issued (one phase of my_rbar each)
+    bool pending = false;  // a load not yet waited for
+    for (int i = 0; i < my_tiles; ++i) {
+      const int b = i & 1;
+      const int t = static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x);
+      const int row0 = (t / ntl) * 128 + q * 32;
+      if (ok) {  // the residual rows of this tile, while its MMAs run
+        if (lane == 0) {
+          bulk_wait_read_all();  // the previous tile's stores have read these boxes
+          mbar_arrive_expect_tx(my_rbar, 8192);
+          tma_load_2d(stg, &tmO, my_rbar, 64 * half, row0);
+          tma_load_2d(stg + 4096, &tmO, my_rbar, 64 * half + 32, row0);
+        }
+        ++loads;
+        pending = true;
+      }
+      __syncwarp();
+      if (ok) ok = mbar_wait_warp(&acc_full[b], (i >> 1) & 1, abort_flag, DERR_WAIT_MMA);
+      if (ok) tc_fence_after();
+      float v[64];
+      tmem_ld64(tmem + (static_cast<uint32_t>(q * 32) << 16) + b * BN + 64 * half, v);
+      tc_fence_before();
+      mbar_arrive(&acc_empty[b]);  // the accumulator is in registers: the MMA may reuse the buffer
+      if (ok && pending) {
+        ok = mbar_wait_warp(my_rbar, static_cast<uint32_t>((loads - 1) & 1), abort_flag, DERR_WAIT_TMA);
+        if (ok) pending = false;
+      }
+      gemm_epilogue_ln<EPI>(&tmO, &tmN, p, v, row0, q, half, stg, stats, lane, ok);
+    }
+    if (pending) mbar_wait_drain(my_rbar, static_cast<uint32_t>((loads - 1) & 1));
+    if (lane == 0) bulk_wait_all();
   } else {
     // epilogue warps 2..9
     const int q = warp & 3;

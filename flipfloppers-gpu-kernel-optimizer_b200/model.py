@@ -118,6 +118,12 @@ _GRAPH_CACHE = 8
 _FUSED_SMALL_ON = os.environ.get("B200_FUSED_SMALL", "1") != "0"
 
 
+def _gemm_ln_fused(d: int) -> bool:
+    """Whether the library's chain fuses the residual projections with the following
+    LayerNorm (it does when a 128-column tile holds the whole row; B200_GEMM_LN=0 off)."""
+    return d == 128 and os.environ.get("B200_GEMM_LN", "1") != "0"
+
+
 @dataclass
 class _LayerPack:
     """Device copies of one layer's weights in the layouts the kernels take."""
@@ -597,6 +603,13 @@ class UserOptimizedTransformer(nn.Module):
             ("ffn_out", lambda: rt.gemm(rt.EPI_BIAS_RESID_F32, h, pk.w_out, pk.b_out, x1, resid=x1)),
             ("ln_f", lambda: rt.layernorm(x1, lnf_w, lnf_b, y, eps)),
         ]
+        if _gemm_ln_fused(d):
+            # the chain runs out_proj + LN2 and ffn_out + final norm as one kernel each
+            stages = [st for st in stages if st[0] not in ("out_proj", "ln2", "ffn_out", "ln_f")]
+            stages.insert(3, ("out_proj_ln2", lambda: rt.gemm_residual_layernorm(
+                ctx, pk.w_o, pk.b_o, x1, pk.ln2_w, pk.ln2_b, n, eps)))
+            stages.append(("ffn_out_lnf", lambda: rt.gemm_residual_layernorm(
+                h, pk.w_out, pk.b_out, x1, lnf_w, lnf_b, y, eps)))
         stream = torch.cuda.current_stream()
         tot = {k: 0.0 for k, _ in stages}
         for it in range(steps + 3):

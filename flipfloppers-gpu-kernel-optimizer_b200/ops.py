@@ -13,6 +13,8 @@ library's equivalents:
 * ``b200::linear(a, w, bias, epilogue)`` -- functional GEMM (fp16 out for the
   bias / bias+GELU epilogues, fp32 for ``EPI_BIAS_F32``);
 * ``b200::linear_residual(a, w, bias, resid)`` -- functional ``resid + a.w^T + bias``;
+* ``b200::linear_residual_layernorm(a, w, bias, resid, gamma, beta, eps)`` --
+  ``x1 = resid + a.w^T + bias`` and its LayerNorm (fp16) from one kernel (N = 128);
 * ``b200::layernorm(x, gamma, beta, eps, out_f16)``;
 * ``b200::flash_causal(q, k, v, heads, q_offset, non_causal, kv_lens)`` on
   ``[B, S, H*hd]`` fp16 tensors (prefix-causal when ``q_offset > 0``: query i
@@ -82,6 +84,22 @@ def linear_residual(a: Tensor, w: Tensor, bias: Optional[Tensor], resid: Tensor)
 @linear_residual.register_fake
 def _linear_residual_fake(a, w, bias, resid):
     return resid.new_empty((a.shape[0], w.shape[0]), dtype=torch.float32)
+
+
+@torch.library.custom_op("b200::linear_residual_layernorm", mutates_args=(), device_types="cuda")
+def linear_residual_layernorm(a: Tensor, w: Tensor, bias: Optional[Tensor], resid: Tensor, gamma: Tensor,
+                              beta: Tensor, eps: float) -> tuple[Tensor, Tensor]:
+    """x1 = resid + a.w^T + bias and LayerNorm(x1)*gamma + beta (fp16) in one kernel (N = 128)."""
+    x1 = resid.clone()
+    n = torch.empty(x1.shape, dtype=torch.float16, device=x1.device)
+    rt.gemm_residual_layernorm(a, w, bias, x1, gamma, beta, n, eps=eps)
+    return x1, n
+
+
+@linear_residual_layernorm.register_fake
+def _linear_residual_layernorm_fake(a, w, bias, resid, gamma, beta, eps):
+    shape = (a.shape[0], w.shape[0])
+    return resid.new_empty(shape, dtype=torch.float32), resid.new_empty(shape, dtype=torch.float16)
 
 
 # ------------------------------------------------------------------ LayerNorm

@@ -112,6 +112,9 @@ EXPORTS = [
     ("b200_zero_masked_rows", ctypes.c_int, [_vp, _vp, _c_ll, ctypes.c_int, _vp]),
     ("b200_gemm_launch", ctypes.c_int,
      [ctypes.c_int, _vp, _c_ll, _vp, _c_ll, _vp, _vp, _c_ll, _vp, _c_ll, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
+    ("b200_gemm_residual_layernorm_launch", ctypes.c_int,
+     [_vp, _c_ll, _vp, _c_ll, _vp, _vp, _c_ll, _vp, _vp, ctypes.c_float, _vp, _c_ll, ctypes.c_int, ctypes.c_int,
+      ctypes.c_int, ctypes.c_int, _vp]),
     ("b200_flash_causal_launch", ctypes.c_int, [ctypes.POINTER(AttnArgs), _vp]),
     ("b200_block_workspace_bytes", ctypes.c_size_t, [_c_ll, ctypes.c_int, ctypes.c_int]),
     ("b200_block_forward", ctypes.c_int, [ctypes.POINTER(BlockArgs), _vp]),
@@ -236,6 +239,25 @@ def gemm(epilogue: int, a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.T
                                 M, N, K, _stream(stream))
     check(rc, "b200_gemm_launch")
     return out
+
+
+def gemm_residual_layernorm(a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor], res: torch.Tensor,
+                            gamma: torch.Tensor, beta: torch.Tensor, ln_out: torch.Tensor, eps: float = 1e-5,
+                            stream=None) -> torch.Tensor:
+    """v = res + a @ w.T + bias; ln_out = LayerNorm(v)*gamma + beta (fp16: res = v as well;
+    fp32: res unchanged).  N = w.shape[0] must be 128."""
+    _require_cuda(a, w, bias, res, gamma, beta, ln_out)
+    if a.dtype != torch.float16 or w.dtype != torch.float16 or res.dtype != torch.float32:
+        raise TypeError("gemm_residual_layernorm: fp16 operands, fp32 residual")
+    if ln_out.dtype not in (torch.float16, torch.float32):
+        raise TypeError("gemm_residual_layernorm: ln_out fp16 or fp32")
+    M, K = a.shape
+    N = w.shape[0]
+    rc = lib().b200_gemm_residual_layernorm_launch(
+        _p(a), a.stride(0), _p(w), w.stride(0), _p(bias), _p(res), res.stride(0), _p(gamma), _p(beta), float(eps),
+        _p(ln_out), ln_out.stride(0), int(ln_out.dtype == torch.float16), M, N, K, _stream(stream))
+    check(rc, "b200_gemm_residual_layernorm_launch")
+    return ln_out
 
 
 def flash_causal(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor, *, batch: int, heads: int,

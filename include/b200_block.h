@@ -18,7 +18,9 @@
  *                                                  -> b200_flash_causal_launch
  *   - F.layer_norm of norm1 / norm2 / final_norm
  *       (torch_transformer_benchmark.py:1293, 1348, 1373) -> b200_layernorm_launch
- *       (norm1 together with the residual copy: b200_layernorm_residual_launch)
+ *       (norm1 together with the residual copy: b200_layernorm_residual_launch;
+ *        out_proj / ffn_out + residual + norm2 / final_norm in one kernel:
+ *        b200_gemm_residual_layernorm_launch)
  *   - the per-layer body of _optimized_forward_causal
  *       (torch_transformer_benchmark.py:1282-1373)  -> b200_block_forward
  *   - the unwired causal megakernel mega_causal_forward
@@ -117,6 +119,20 @@ int b200_zero_masked_rows(float* y, const unsigned char* row_valid, long long ro
  * a different resid is first copied into out, so it must not overlap out.
  * Requires N % 32 == 0, K % 8 == 0, lda/ldw % 8 == 0, 16-byte aligned
  * pointers.  fp32 accumulation on the tcgen05 tensor cores. */
+/* The residual projection with the LayerNorm that follows it in the epilogue:
+ * out_proj + residual + norm2 (torch_transformer_benchmark.py:1328-1348) or
+ * ffn_out + residual + final_norm (1368-1373).  res [M, ld_res] fp32 holds the
+ * residual on entry; v = res + A.W^T + bias (fp32 accumulation);
+ * ln_out_f16 != 0: res = v (in place) and ln_out = LayerNorm(v)*gamma + beta
+ * in fp16 (the next GEMM's operand); ln_out_f16 == 0: ln_out = LayerNorm(v)*
+ * gamma + beta in fp32 and res is left unchanged.  One 128-column tile holds a
+ * whole row: requires N == 128, K % 8 == 0, 16-byte aligned pointers and leading
+ * dimensions.  ln_out must not overlap res. */
+int b200_gemm_residual_layernorm_launch(const void* A, long long lda, const void* W, long long ldw, const float* bias,
+                                        float* res, long long ld_res, const float* gamma, const float* beta, float eps,
+                                        void* ln_out, long long ld_ln, int ln_out_f16, int M, int N, int K,
+                                        b200_stream_t stream);
+
 int b200_gemm_launch(int epilogue, const void* A, long long lda, const void* W, long long ldw, const float* bias,
                      const float* resid, long long ld_resid, void* out, long long ld_out, int M, int N, int K,
                      b200_stream_t stream);

@@ -355,3 +355,41 @@ print("OK", worst)
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     r = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0 and "OK" in r.stdout, r.stdout + r.stderr
+
+
+@pytest.mark.parametrize("M,K", [(1000, 128), (300, 512), (65536, 128)])
+@pytest.mark.parametrize("f16", [True, False])
+def test_gemm_residual_layernorm_vs_torch(rt, M, K, f16):
+    """The residual projection with the LayerNorm in its epilogue (N = 128):
+    v = res + a.w^T + bias, ln_out = LN(v)*gamma + beta; fp16 output also writes
+    v back into res, fp32 output leaves res alone."""
+    N = 128
+    g = torch.Generator().manual_seed(M + K + int(f16))
+    a = torch.randn(M, K, generator=g).to(torch.float16).to(DEV)
+    w = (torch.randn(N, K, generator=g) / math.sqrt(K)).to(torch.float16).to(DEV)
+    bias = torch.randn(N, generator=g).to(DEV)
+    res0 = torch.randn(M, N, generator=g).to(DEV)
+    gamma = (1 + 0.1 * torch.randn(N, generator=g)).to(DEV)
+    beta = (0.1 * torch.randn(N, generator=g)).to(DEV)
+    res = res0.clone()
+    out = torch.full((M, N), float("nan"), dtype=torch.float16 if f16 else torch.float32, device=DEV)
+    rt.gemm_residual_layernorm(a, w, bias, res, gamma, beta, out, eps=1e-5)
+    v = res0 + a.float() @ w.float().T + bias
+    ref = torch.nn.functional.layer_norm(v, (N,), gamma, beta, eps=1e-5)
+    torch.cuda.synchronize()
+    tol = 3e-3 if f16 else 2e-4
+    assert (out.float() - ref).abs().max().item() < tol
+    if f16:
+        assert (res - v).abs().max().item() < 1e-4 * math.sqrt(K)
+    else:
+        assert torch.equal(res, res0)
+
+
+def test_gemm_residual_layernorm_rejects_wide_rows(rt):
+    a = torch.zeros(128, 64, dtype=torch.float16, device=DEV)
+    w = torch.zeros(256, 64, dtype=torch.float16, device=DEV)
+    res = torch.zeros(128, 256, device=DEV)
+    g = torch.ones(256, device=DEV)
+    out = torch.empty(128, 256, dtype=torch.float16, device=DEV)
+    with pytest.raises(rt.B200Error):
+        rt.gemm_residual_layernorm(a, w, None, res, g, g, out)

@@ -49,6 +49,14 @@ def test_linear_values(ops):
     out = r.clone()
     torch.ops.b200.gemm_out(a, w, b, ops.EPI_BIAS_RESID_F32, out)
     assert torch.equal(out, y2)
+    w128 = _rand(g, 128, 256, scale=1 / 16, dtype=torch.float16)
+    b128, r128 = _rand(g, 128), _rand(g, 300, 128)
+    gam, bet = _rand(g, 128), _rand(g, 128)
+    x1, n = torch.ops.b200.linear_residual_layernorm(a, w128, b128, r128, gam, bet, 1e-5)
+    ref1 = r128 + a.float() @ w128.float().T + b128
+    assert (x1 - ref1).abs().max().item() < 1e-3
+    ref_n = torch.nn.functional.layer_norm(ref1, (128,), gam, bet, eps=1e-5)
+    assert (n.float() - ref_n).abs().max().item() < 2e-2
 
 
 def test_compiled_block_matches_eager(ops, pkg):

@@ -7,7 +7,8 @@ import torch
 
 
 def test_ops_registered(pkg):
-    for name in ("gemm_out", "linear", "linear_residual", "layernorm", "flash_causal", "block_megakernel"):
+    for name in ("gemm_out", "linear", "linear_residual", "linear_residual_layernorm", "layernorm",
+                 "flash_causal", "block_megakernel"):
         assert hasattr(torch.ops.b200, name), name
 
 
