@@ -175,6 +175,7 @@ __global__ void __launch_bounds__(192, 2)  // two CTAs per SM (registers <= 170)
     tmem_relinquish();
   }
   tc_fence_before();
+  __syncwarp();  // lane-0 roles rejoin their warp: bar.sync is warp-aligned
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
@@ -351,6 +352,7 @@ __global__ void __launch_bounds__(192, 2)  // two CTAs per SM (registers <= 170)
     }
   }
   tc_fence_before();
+  __syncwarp();  // lane-0 roles rejoin their warp: bar.sync is warp-aligned
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();

@@ -105,6 +105,7 @@ __global__ void __launch_bounds__(320, 1)
     tmem_relinquish();
   }
   tc_fence_before();
+  __syncwarp();  // lane-0 roles rejoin their warp: bar.sync is warp-aligned
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
@@ -306,6 +307,7 @@ __global__ void __launch_bounds__(320, 1)
     }
   }
   tc_fence_before();
+  __syncwarp();  // lane-0 roles rejoin their warp: bar.sync is warp-aligned
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();

@@ -111,7 +111,8 @@ enum SmallBar : int {
   SB_FOUT = 22,        // MMA: ffn_out accumulator complete
   SB_DRAIN = 23,
   SB_XFULL = 24,       // TMA: x of the CTA's current sequence in XIN
-  SB_COUNT = 25
+  SB_VFULL = 25,       // bulk copies: the layer's vectors in shared memory
+  SB_COUNT = 26
 };
 
 __device__ __forceinline__ void named_bar(int id, int count) {
@@ -169,6 +170,7 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
     mbar_init(&bar[SB_FOUT], 1);
     mbar_init(&bar[SB_DRAIN], 1);
     mbar_init(&bar[SB_XFULL], 1);
+    mbar_init(&bar[SB_VFULL], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -177,6 +179,7 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
     tmem_relinquish();
   }
   tc_fence_before();
+  __syncwarp();  // lane-0 roles rejoin their warp: bar.sync is warp-aligned
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
@@ -428,22 +431,26 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
       mbar_arrive(&bar[slot]);
     };
 
-    // copy a layer's biases and LayerNorm parameters into shared memory (all 512 workers)
+    // a layer's biases and LayerNorm parameters -> shared memory: ten bulk copies
+    // issued by one worker, completing on SB_VFULL (one HBM/L2 round trip that
+    // overlaps the x load, instead of dependent per-thread loads)
+    int nstaged = 0;  // stagings issued (by worker 0)
     auto stage_vectors = [&](int l) {
-      auto cp = [&](int dst, const float* src, int n) {
-        for (int i = wtid * 4; i < n; i += 512 * 4)
-          *reinterpret_cast<float4*>(vec + dst + i) = __ldg(reinterpret_cast<const float4*>(src + i));
-      };
-      cp(C::V_LN1W, p.ln1_w + l * 128, 128);
-      cp(C::V_LN1B, p.ln1_b + l * 128, 128);
-      cp(C::V_BQKV, p.b_qkv + l * 384, 384);
-      cp(C::V_BO, p.b_o + l * 128, 128);
-      cp(C::V_LN2W, p.ln2_w + l * 128, 128);
-      cp(C::V_LN2B, p.ln2_b + l * 128, 128);
-      cp(C::V_BIN, p.b_in + l * p.ffn, p.ffn);
-      cp(C::V_BOUT, p.b_out + l * 128, 128);
-      cp(C::V_LNFW, p.lnf_w, 128);
-      cp(C::V_LNFB, p.lnf_b, 128);
+      if (wtid != 0) return;
+      ++nstaged;
+      fence_proxy_async_smem();  // the previous layer's reads of these buffers come first
+      const uint32_t fb = 4u * static_cast<uint32_t>(p.ffn);
+      mbar_arrive_expect_tx(&bar[SB_VFULL], 8u * 512u + 1536u + fb);
+      bulk_load(vec + C::V_LN1W, p.ln1_w + l * 128, 512, &bar[SB_VFULL]);
+      bulk_load(vec + C::V_LN1B, p.ln1_b + l * 128, 512, &bar[SB_VFULL]);
+      bulk_load(vec + C::V_BQKV, p.b_qkv + l * 384, 1536, &bar[SB_VFULL]);
+      bulk_load(vec + C::V_BO, p.b_o + l * 128, 512, &bar[SB_VFULL]);
+      bulk_load(vec + C::V_LN2W, p.ln2_w + l * 128, 512, &bar[SB_VFULL]);
+      bulk_load(vec + C::V_LN2B, p.ln2_b + l * 128, 512, &bar[SB_VFULL]);
+      bulk_load(vec + C::V_BIN, p.b_in + static_cast<int64_t>(l) * p.ffn, fb, &bar[SB_VFULL]);
+      bulk_load(vec + C::V_BOUT, p.b_out + l * 128, 512, &bar[SB_VFULL]);
+      bulk_load(vec + C::V_LNFW, p.lnf_w, 512, &bar[SB_VFULL]);
+      bulk_load(vec + C::V_LNFB, p.lnf_b, 512, &bar[SB_VFULL]);
     };
 
     for (int step = 0; step < nsteps; ++step) {
@@ -454,10 +461,10 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
       // this thread's 32 columns of row r in XIN (box g, SW128)
       uint8_t* xin_row = smem + C::OFF_XIN + g * 16384;
       // ---- W1: x -> residual in TMEM [384,512); LN1 -> XA
-      if (step == 0 || p.layers > 1) {
-        named_bar(5, 32 * C::NW);  // every worker is done with the previous layer's vectors
+      const bool restage = step == 0 || p.layers > 1;
+      if (restage) {
+        if (step > 0) named_bar(5, 32 * C::NW);  // every worker is done with the previous layer's vectors
         stage_vectors(l);
-        named_bar(5, 32 * C::NW);
       }
       // layer 0: x arrives by TMA; later layers: this thread wrote its own slice in W7
       if (l == 0) wait_w(SB_XFULL, static_cast<uint32_t>((step / p.layers) & 1));
@@ -467,6 +474,7 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
         v[4 * j] = t.x; v[4 * j + 1] = t.y; v[4 * j + 2] = t.z; v[4 * j + 3] = t.w;
       }
       if (ok) tmem_st32(trow + 384 + c0, v);
+      if (restage) wait_w(SB_VFULL, static_cast<uint32_t>((p.layers > 1 ? step : 0) & 1));
       layer_norm(vec + C::V_LN1W, vec + C::V_LN1B);
       store_sw128(xa);
       // the previous step's y store must have read its staging box before Q/K
@@ -595,8 +603,11 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
       named_bar(bar_id, 128);
     }
     if (lane == 0) bulk_wait_all();  // the last y stores are complete before the CTA exits
+    // after an abort, the last vector copies land before shared memory is released
+    if (wtid == 0 && *abort_flag && nstaged > 0) mbar_wait_drain(&bar[SB_VFULL], static_cast<uint32_t>((nstaged - 1) & 1));
   }
   tc_fence_before();
+  __syncwarp();  // lane-0 roles rejoin their warp: bar.sync is warp-aligned
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();

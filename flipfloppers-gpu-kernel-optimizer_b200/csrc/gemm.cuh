@@ -277,6 +277,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     tmem_relinquish();
   }
   tc_fence_before();
+  __syncwarp();  // lane-0 roles rejoin their warp: bar.sync is warp-aligned
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
@@ -409,6 +410,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     if (lane == 0) bulk_wait_all();  // the last stores are complete before the CTA exits
   }
   tc_fence_before();
+  __syncwarp();  // lane-0 roles rejoin their warp: bar.sync is warp-aligned
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();

@@ -140,6 +140,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     tmem_relinquish_pair();
   }
   tc_fence_before();
+  __syncwarp();  // thread 0 rejoins warp 0: barrier.cluster is warp-aligned
   cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
@@ -227,6 +228,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     if (lane == 0) bulk_wait_all();
   }
   tc_fence_before();
+  __syncwarp();  // lane-0 roles rejoin their warp: bar.sync is warp-aligned
   __syncthreads();
   cluster_sync_all();  // no remote arrival or copy is still headed for either CTA
   if (warp == 1) {
