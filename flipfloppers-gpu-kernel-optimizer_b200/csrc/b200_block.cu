@@ -564,6 +564,17 @@ int attn_impl(const B200AttnArgs* a, cudaStream_t st) {
 }
 
 // ------------------------------------------------------------------ fused small-model kernel
+// 0: one CTA per sequence, 1: the row-split kernel whenever it applies (one
+// layer), -1 (default): row split when every sequence's two CTAs fit on the
+// device at once
+int small_rows_mode() {
+  static const int mode = [] {
+    const char* e = std::getenv("B200_SMALL_ROWS");
+    return e ? std::atoi(e) : -1;
+  }();
+  return mode;
+}
+
 int fused_small_impl(const B200FusedSmallArgs* a, cudaStream_t st) {
   if (!a || !a->x || !a->y || !a->w_qkv || !a->w_o || !a->w_in || !a->w_out) return B200_ERR_ARG;
   if (!a->ln1_w || !a->ln1_b || !a->ln2_w || !a->ln2_b || !a->lnf_w || !a->lnf_b || !a->b_qkv || !a->b_o ||
@@ -612,6 +623,18 @@ int fused_small_impl(const B200FusedSmallArgs* a, cudaStream_t st) {
   p.row_valid = static_cast<const unsigned char*>(a->row_valid);
   p.non_causal = a->non_causal;
   const int smem = SmallCfg::TOTAL;
+  // Two CTAs per sequence (each finishing half of the query rows) halve the
+  // latency-bound per-row phases while the batch leaves SMs idle (measured
+  // at C2: see DESIGN); one layer only, as each CTA rebuilds K/V from x.
+  const int rows_mode = small_rows_mode();
+  if (L == 1 && rows_mode != 0 && (rows_mode == 1 || 2LL * a->batch <= num_sms()) && a->batch <= 0x3fffffff) {
+    CUtensorMap ty16;  // 16-row y boxes: a worker warp's own rows
+    if (int rc = make_map_f32_seq(&ty16, a->y, a->batch, a->seq_len, 128, 16)) return rc;
+    if (int rc = set_smem(reinterpret_cast<const void*>(k_block_rows), smem)) return rc;
+    if (int rc = check_block_fits(reinterpret_cast<const void*>(k_block_rows), SmallCfg::THREADS)) return rc;
+    k_block_rows<<<2 * a->batch, SmallCfg::THREADS, smem, st>>>(tq, to, ti, tout, tx, ty16, p);
+    return launch_status();
+  }
   if (int rc = set_smem(reinterpret_cast<const void*>(k_block_small), smem)) return rc;
   if (int rc = check_block_fits(reinterpret_cast<const void*>(k_block_small), SmallCfg::THREADS)) return rc;
   const int grid = a->batch < num_sms() ? a->batch : num_sms();

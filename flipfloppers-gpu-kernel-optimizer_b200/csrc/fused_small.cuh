@@ -112,7 +112,11 @@ enum SmallBar : int {
   SB_DRAIN = 23,
   SB_XFULL = 24,       // TMA: x of the CTA's current sequence in XIN
   SB_VFULL = 25,       // bulk copies: the layer's vectors in shared memory
-  SB_COUNT = 26
+  // row-split mode only: extra weight slots in areas idle at the time
+  SB_QKF = 26,         // [3] QKV boxes 3-5 in the Q/K area (free until the QKV results are written)
+  SB_VPF = 29,         // [4] ffn_out boxes in the V/P area (free once attention is done): loaded
+  SB_VPE = 33,         // [4] ... and consumed
+  SB_COUNT = 37
 };
 
 __device__ __forceinline__ void named_bar(int id, int count) {
@@ -125,11 +129,15 @@ __device__ __forceinline__ uint32_t par(int step, int per, int idx) {
   return static_cast<uint32_t>((step * per + idx) & 1);
 }
 
-__global__ void __launch_bounds__(SmallCfg::THREADS, 1)
-    k_block_small(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_o,
-                  const __grid_constant__ CUtensorMap tm_in, const __grid_constant__ CUtensorMap tm_out,
-                  const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_y,
-                  const SmallParams p) {
+// The kernel body.  ROWS = false: one CTA per sequence (persistent over
+// sequences and layers).  ROWS = true: two CTAs per sequence, one layer (the
+// row-split mode, see k_block_rows); the producer and MMA roles are the same
+// in both modes, only the workers' phases differ.
+template <bool ROWS>
+__device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, const CUtensorMap* tm_o,
+                                                 const CUtensorMap* tm_in, const CUtensorMap* tm_out,
+                                                 const CUtensorMap* tm_x, const CUtensorMap* tm_y,
+                                                 const SmallParams& p) {
   using C = SmallCfg;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_align1024(smem_raw);
@@ -140,8 +148,10 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nch = p.ffn / 128;                              // ffn chunks of 128
-  const int nseq_cta = (p.num_seq - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
-                       static_cast<int>(gridDim.x);         // sequences this CTA handles
+  // sequences this CTA handles: seq_first, seq_first + gridDim.x, ... (ROWS: its pair's one sequence)
+  const int seq_first = ROWS ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int nseq_cta = ROWS ? (seq_first < p.num_seq ? 1 : 0)
+                            : (p.num_seq - seq_first + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x);
   const int nsteps = nseq_cta * p.layers;
   // completions per step of the ping-pong barriers (buffer b serves chunks b, b+2, ...)
   const int per_b0 = (nch + 1) / 2, per_b1 = nch / 2;
@@ -171,6 +181,11 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
     mbar_init(&bar[SB_DRAIN], 1);
     mbar_init(&bar[SB_XFULL], 1);
     mbar_init(&bar[SB_VFULL], 1);
+    for (int i = 0; i < 3; ++i) mbar_init(&bar[SB_QKF + i], 1);
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(&bar[SB_VPF + i], 1);
+      mbar_init(&bar[SB_VPE + i], 1);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -187,11 +202,11 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      tma_prefetch_desc(&tm_qkv);
-      tma_prefetch_desc(&tm_o);
-      tma_prefetch_desc(&tm_in);
-      tma_prefetch_desc(&tm_out);
-      tma_prefetch_desc(&tm_x);
+      tma_prefetch_desc(tm_qkv);
+      tma_prefetch_desc(tm_o);
+      tma_prefetch_desc(tm_in);
+      tma_prefetch_desc(tm_out);
+      tma_prefetch_desc(tm_x);
       int box = 0;
       bool ok = true;
       // x of sequence `seq` (rows past seq_len are zero-filled) -> XIN
@@ -200,9 +215,9 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
         ++xloads;
         mbar_arrive_expect_tx(&bar[SB_XFULL], 4 * 128 * 128);
         for (int g = 0; g < 4; ++g)
-          tma_load_3d(smem + C::OFF_XIN + g * 16384, &tm_x, &bar[SB_XFULL], 32 * g, 0, seq);
+          tma_load_3d(smem + C::OFF_XIN + g * 16384, tm_x, &bar[SB_XFULL], 32 * g, 0, seq);
       };
-      if (nsteps > 0) load_x(static_cast<int>(blockIdx.x));
+      if (nsteps > 0) load_x(seq_first);
       auto load = [&](const CUtensorMap* m, int col, int row) {
         const int s = box % C::WST;
         if (box >= C::WST && !mbar_wait(&bar[SB_WEMPTY + s], ((box / C::WST) - 1) & 1, abort_flag, DERR_WAIT_SLOT)) {
@@ -213,15 +228,53 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
         tma_load_2d(smem + C::OFF_W + s * C::BOX, m, &bar[SB_WFULL + s], col, row);
         ++box;
       };
-      for (int step = 0; ok && step < nsteps; ++step) {
+      // row-split mode: QKV boxes 3-5 into the Q/K area, ffn_out boxes through a 4-slot ring in V/P
+      int qk = 0, vp = 0;
+      auto load_qk = [&](const CUtensorMap* m, int col, int row) {
+        mbar_arrive_expect_tx(&bar[SB_QKF + qk], C::BOX);
+        tma_load_2d(smem + C::OFF_Q + qk * C::BOX, m, &bar[SB_QKF + qk], col, row);
+        ++qk;
+      };
+      auto load_vp = [&](const CUtensorMap* m, int col, int row) {
+        const int s = vp & 3;
+        if (vp >= 4 && !mbar_wait(&bar[SB_VPE + s], ((vp >> 2) - 1) & 1, abort_flag, DERR_WAIT_SLOT)) {
+          ok = false;
+          return;
+        }
+        mbar_arrive_expect_tx(&bar[SB_VPF + s], C::BOX);
+        tma_load_2d(smem + C::OFF_V + s * C::BOX, m, &bar[SB_VPF + s], col, row);
+        ++vp;
+      };
+      if constexpr (ROWS) {
+        // one step; boxes in the MMA's order within each buffer set
+        load(tm_qkv, 0, 0);
+        if (ok) load(tm_qkv, 64, 0);
+        if (ok) load(tm_qkv, 0, 128);
+        load_qk(tm_qkv, 64, 128);
+        load_qk(tm_qkv, 0, 256);
+        load_qk(tm_qkv, 64, 256);
+        for (int kh = 0; ok && kh < 2; ++kh) load(tm_o, kh * 64, 0);
+        // V and P are free once the context is published
+        if (ok && nsteps > 0 && !mbar_wait(&bar[SB_CTX], 0, abort_flag, DERR_WAIT_SOFTMAX)) ok = false;
+        for (int c = 0; ok && c < nch && c < 2; ++c)
+          for (int kh = 0; ok && kh < 2; ++kh) load_vp(tm_out, c * 128 + kh * 64, 0);
+        // ffn_in chunk c waits only for ring slots that earlier ffn_in MMAs free;
+        // ffn_out chunk c (c >= 2) for the V/P slot of chunk c-2's ffn_out
+        for (int c = 0; ok && c < nch; ++c) {
+          for (int kh = 0; ok && kh < 2; ++kh) load(tm_in, kh * 64, c * 128);
+          if (c >= 2)
+            for (int kh = 0; ok && kh < 2; ++kh) load_vp(tm_out, c * 128 + kh * 64, 0);
+        }
+      }
+      for (int step = 0; !ROWS && ok && step < nsteps; ++step) {
         const int l = step % p.layers;
         for (int nt = 0; ok && nt < 3; ++nt)
-          for (int kh = 0; ok && kh < 2; ++kh) load(&tm_qkv, kh * 64, l * 384 + nt * 128);
-        for (int kh = 0; ok && kh < 2; ++kh) load(&tm_o, kh * 64, l * 128);
-        for (int kh = 0; ok && kh < 2; ++kh) load(&tm_in, kh * 64, l * p.ffn);
+          for (int kh = 0; ok && kh < 2; ++kh) load(tm_qkv, kh * 64, l * 384 + nt * 128);
+        for (int kh = 0; ok && kh < 2; ++kh) load(tm_o, kh * 64, l * 128);
+        for (int kh = 0; ok && kh < 2; ++kh) load(tm_in, kh * 64, l * p.ffn);
         // after the last layer's attention (V and P consumed, CTX published) the
         // next sequence's x can overwrite XIN while this one runs its FFN
-        const int next_seq = static_cast<int>(blockIdx.x) + (step / p.layers + 1) * static_cast<int>(gridDim.x);
+        const int next_seq = ROWS ? p.num_seq : seq_first + (step / p.layers + 1) * static_cast<int>(gridDim.x);
         if (ok && l == p.layers - 1 && next_seq < p.num_seq) {
           if (!mbar_wait(&bar[SB_CTX], par(step, 1, 0), abort_flag, DERR_WAIT_SOFTMAX)) {
             ok = false;
@@ -231,14 +284,16 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
         }
         for (int c = 0; ok && c < nch; ++c) {
           if (c + 1 < nch)
-            for (int kh = 0; ok && kh < 2; ++kh) load(&tm_in, kh * 64, l * p.ffn + (c + 1) * 128);
-          for (int kh = 0; ok && kh < 2; ++kh) load(&tm_out, c * 128 + kh * 64, l * 128);
+            for (int kh = 0; ok && kh < 2; ++kh) load(tm_in, kh * 64, l * p.ffn + (c + 1) * 128);
+          for (int kh = 0; ok && kh < 2; ++kh) load(tm_out, c * 128 + kh * 64, l * 128);
         }
       }
       if (*abort_flag) {
         for (int b = (box > C::WST ? box - C::WST : 0); b < box; ++b)
           mbar_wait_drain(&bar[SB_WFULL + b % C::WST], (b / C::WST) & 1);
         if (xloads > 0) mbar_wait_drain(&bar[SB_XFULL], (xloads - 1) & 1);
+        for (int i = 0; i < qk; ++i) mbar_wait_drain(&bar[SB_QKF + i], 0);
+        for (int b = (vp > 4 ? vp - 4 : 0); b < vp; ++b) mbar_wait_drain(&bar[SB_VPF + (b & 3)], (b >> 2) & 1);
       }
     }
   } else if (warp == 1) {
@@ -250,24 +305,49 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
       const uint32_t qs = smem_u32(smem + C::OFF_Q), ks = smem_u32(smem + C::OFF_K), vs = smem_u32(smem + C::OFF_V);
       const uint32_t ps = smem_u32(smem + C::OFF_P);
       const uint32_t ws = smem_u32(smem + C::OFF_W);
-      int box = 0;
+      int box = 0, qk = 0, vp = 0;
       bool ok = true;
+      // where a weight box comes from: the ring, or (row-split mode) a Q/K or V/P slot
+      enum { FROM_RING = 0, FROM_QK = 1, FROM_VP = 2 };
+      auto acquire = [&](int src) -> uint32_t {
+        uint64_t* full;
+        uint32_t parity, w;
+        if (src == FROM_RING) {
+          full = &bar[SB_WFULL + box % C::WST], parity = (box / C::WST) & 1, w = ws + (box % C::WST) * C::BOX;
+        } else if (src == FROM_QK) {
+          full = &bar[SB_QKF + qk], parity = 0, w = qs + qk * C::BOX;
+        } else {
+          full = &bar[SB_VPF + (vp & 3)], parity = (vp >> 2) & 1, w = vs + (vp & 3) * C::BOX;
+        }
+        if (!mbar_wait(full, parity, abort_flag, DERR_WAIT_TMA)) {
+          ok = false;
+          return 0;
+        }
+        tc_fence_after();
+        return w;
+      };
+      auto release = [&](int src) {  // after the MMAs reading the box are issued
+        if (src == FROM_RING) {
+          tc_commit(&bar[SB_WEMPTY + box % C::WST]);
+          ++box;
+        } else if (src == FROM_QK) {
+          ++qk;  // read once, never refilled
+        } else {
+          tc_commit(&bar[SB_VPE + (vp & 3)]);
+          ++vp;
+        }
+      };
       // D[tmem_col] (+)= A(128x128, SW128 K-major at a) . W-box^T over two 64-wide K halves
-      auto gemm_k128 = [&](uint32_t a, uint32_t dcol, bool acc_in) {
+      auto gemm_k128 = [&](uint32_t a, uint32_t dcol, bool acc_in, int src0 = FROM_RING, int src1 = FROM_RING) {
         for (int kh = 0; kh < 2 && ok; ++kh) {
-          const int s = box % C::WST;
-          if (!mbar_wait(&bar[SB_WFULL + s], (box / C::WST) & 1, abort_flag, DERR_WAIT_TMA)) {
-            ok = false;
-            return;
-          }
-          tc_fence_after();
-          const uint32_t w = ws + s * C::BOX;
+          const int src = kh ? src1 : src0;
+          const uint32_t w = acquire(src);
+          if (!ok) return;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
             umma_f16_ss(tmem + dcol, make_sdesc(a + kh * 16384 + kk * 32, 16, 1024, UMMA_SW128),
                         make_sdesc(w + kk * 32, 16, 1024, UMMA_SW128), ID_N128, (acc_in || kh || kk) ? 1u : 0u);
-          tc_commit(&bar[SB_WEMPTY + s]);
-          ++box;
+          release(src);
         }
       };
       auto issue_s = [&](int h) {
@@ -281,7 +361,13 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
         // QKV projection
         if (!mbar_wait(&bar[SB_N1], par(step, 1, 0), abort_flag, DERR_WAIT_SOFTMAX)) break;
         tc_fence_after();
-        for (int nt = 0; nt < 3 && ok; ++nt) gemm_k128(xa, nt * 128, false);
+        if constexpr (ROWS) {
+          gemm_k128(xa, 0, false);
+          if (ok) gemm_k128(xa, 128, false, FROM_RING, FROM_QK);
+          if (ok) gemm_k128(xa, 256, false, FROM_QK, FROM_QK);
+        } else {
+          for (int nt = 0; nt < 3 && ok; ++nt) gemm_k128(xa, nt * 128, false);
+        }
         if (!ok) break;
         tc_commit(&bar[SB_QKV_DONE]);
         // attention: S of heads 0 and 1, then per head PV and the S two heads ahead
@@ -328,7 +414,9 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
             break;
           }
           tc_fence_after();
-          gemm_k128(smem_u32(smem + (b ? C::OFF_K : C::OFF_Q)), 384, true);  // onto x1
+          // onto the residual; row-split mode reads these boxes from the V/P ring
+          gemm_k128(smem_u32(smem + (b ? C::OFF_K : C::OFF_Q)), 384, true, ROWS ? FROM_VP : FROM_RING,
+                    ROWS ? FROM_VP : FROM_RING);
           if (!ok) break;
           tc_commit(&bar[SB_HFREE + b]);
         }
@@ -372,8 +460,10 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
       return fmaxf(fmaxf(buf[r], buf[128 + r]), fmaxf(buf[256 + r], buf[384 + r]));
     };
     // LayerNorm of v (32 columns of this row) in place, two-pass statistics
-    // (f32x2 pairs throughout: the statistics use 2 pair accumulators each)
-    auto layer_norm = [&](const float* gamma, const float* beta) {  // gamma/beta: shared memory
+    // (f32x2 pairs throughout: the statistics use 2 pair accumulators each);
+    // vec_parity >= 0: wait for that phase of the vector copies (SB_VFULL)
+    // only before gamma and beta are read
+    auto layer_norm = [&](const float* gamma, const float* beta, int vec_parity = -1) {  // gamma/beta: shared memory
       uint64_t a0 = f2pk(0.f, 0.f), a1 = a0;
 #pragma unroll
       for (int i = 0; i < 32; i += 4) {
@@ -399,6 +489,7 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
       f2upk(a1, t2, t3);
       const float rstd = rsqrtf(row_sum((t0 + t2) + (t1 + t3), st1) * (1.f / 128.f) + p.eps);
       const uint64_t rs = f2pk(rstd, rstd);
+      if (vec_parity >= 0) wait_w(SB_VFULL, static_cast<uint32_t>(vec_parity));
 #pragma unroll
       for (int i = 0; i < 32; i += 4) {
         const float4 gg = *reinterpret_cast<const float4*>(gamma + c0 + i);
@@ -453,154 +544,393 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
       bulk_load(vec + C::V_LNFB, p.lnf_b, 512, &bar[SB_VFULL]);
     };
 
-    for (int step = 0; step < nsteps; ++step) {
-      const int l = step % p.layers;
-      const int seq = static_cast<int>(blockIdx.x) + (step / p.layers) * static_cast<int>(gridDim.x);
-      const bool row_ok = r < p.seq_len;
-      const int64_t grow = static_cast<int64_t>(seq) * p.seq_len + r;
-      // this thread's 32 columns of row r in XIN (box g, SW128)
-      uint8_t* xin_row = smem + C::OFF_XIN + g * 16384;
-      // ---- W1: x -> residual in TMEM [384,512); LN1 -> XA
-      const bool restage = step == 0 || p.layers > 1;
-      if (restage) {
-        if (step > 0) named_bar(5, 32 * C::NW);  // every worker is done with the previous layer's vectors
-        stage_vectors(l);
-      }
-      // layer 0: x arrives by TMA; later layers: this thread wrote its own slice in W7
-      if (l == 0) wait_w(SB_XFULL, static_cast<uint32_t>((step / p.layers) & 1));
+    if constexpr (!ROWS) {
+      for (int step = 0; step < nsteps; ++step) {
+        const int l = step % p.layers;
+        const int seq = seq_first + (step / p.layers) * static_cast<int>(gridDim.x);
+        const bool row_ok = r < p.seq_len;
+        const int64_t grow = static_cast<int64_t>(seq) * p.seq_len + r;
+        // this thread's 32 columns of row r in XIN (box g, SW128)
+        uint8_t* xin_row = smem + C::OFF_XIN + g * 16384;
+        // ---- W1: x -> residual in TMEM [384,512); LN1 -> XA
+        const bool restage = step == 0 || p.layers > 1;
+        if (restage) {
+          if (step > 0) named_bar(5, 32 * C::NW);  // every worker is done with the previous layer's vectors
+          stage_vectors(l);
+        }
+        // layer 0: x arrives by TMA; later layers: this thread wrote its own slice in W7
+        if (l == 0) wait_w(SB_XFULL, static_cast<uint32_t>((step / p.layers) & 1));
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float4 t = *reinterpret_cast<const float4*>(xin_row + sw128_off(r, j));
-        v[4 * j] = t.x; v[4 * j + 1] = t.y; v[4 * j + 2] = t.z; v[4 * j + 3] = t.w;
+        for (int j = 0; j < 8; ++j) {
+          const float4 t = *reinterpret_cast<const float4*>(xin_row + sw128_off(r, j));
+          v[4 * j] = t.x; v[4 * j + 1] = t.y; v[4 * j + 2] = t.z; v[4 * j + 3] = t.w;
+        }
+        if (ok) tmem_st32(trow + 384 + c0, v);
+        layer_norm(vec + C::V_LN1W, vec + C::V_LN1B, restage ? ((p.layers > 1 ? step : 0) & 1) : -1);
+        store_sw128(xa);
+        // the previous step's y store must have read its staging box before Q/K
+        // (which it aliases) are rewritten, and they are rewritten only after N1
+        if (lane == 0) bulk_wait_read_all();
+        __syncwarp();
+        publish(SB_N1);
+        // ---- W2: QKV accumulator -> Q/K/V tiles (head g = column group g)
+        wait_w(SB_QKV_DONE, par(step, 1, 0));
+#pragma unroll 1
+        for (int nt = 0; nt < 3; ++nt) {
+          if (ok) tmem_ld32(trow + nt * 128 + c0, v);
+          f2_add_bias32(v, vec + C::V_BQKV + nt * 128 + c0);
+          store_sw64(smem + (nt == 0 ? C::OFF_Q : nt == 1 ? C::OFF_K : C::OFF_V) + g * 8192);
+        }
+        publish(SB_QKV_SMEM);
+        // ---- W3: softmax per head (this thread: row r, keys c0..c0+31)
+        // bit i: key c0+i exists and is not padding (the causal bound is applied per row below);
+        // lane i of the warp tests key c0+i (one coalesced byte load) and the ballot gathers them
+        uint32_t kvalid;
+        {
+          const int k = c0 + lane;
+          bool v_ok = k < p.seq_len;
+          if (v_ok && p.row_valid != nullptr) v_ok = p.row_valid[static_cast<int64_t>(seq) * p.seq_len + k] != 0;
+          kvalid = __ballot_sync(0xffffffffu, v_ok);
+        }
+        if (!p.non_causal) kvalid &= (r >= c0 + 31) ? 0xffffffffu : (r < c0 ? 0u : (0xffffffffu >> (31 - (r - c0))));
+        float my_l = 1.f;  // softmax denominator of head g (this thread's head in the context step)
+#pragma unroll 1
+        for (int h = 0; h < 4; ++h) {
+          wait_w(SB_S_FULL + (h & 1), par(step, 2, h >> 1));
+          if (ok) tmem_ld32(trow + (h & 1) * 128 + c0, v);
+          if (kvalid != 0xffffffffu) {  // raw scores; the positive scale is applied in the exponent
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (!((kvalid >> i) & 1u)) v[i] = -INFINITY;
+          }
+          float mx = -INFINITY;
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) mx = fmax3(mx, v[i], v[i + 1]);
+          const float m = row_max(mx, st0) * p.scale_log2;  // reductions alternate st0/st1 strictly
+          const uint64_t sc = f2pk(p.scale_log2, p.scale_log2), nm = f2pk(-m, -m);
+          uint64_t a0 = f2pk(0.f, 0.f), a1 = a0;
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            float e0, e1, e2, e3;
+            f2upk(f2fma(f2pk(v[i], v[i + 1]), sc, nm), e0, e1);
+            f2upk(f2fma(f2pk(v[i + 2], v[i + 3]), sc, nm), e2, e3);
+            v[i] = fast_exp2(e0); v[i + 1] = fast_exp2(e1); v[i + 2] = fast_exp2(e2); v[i + 3] = fast_exp2(e3);
+            a0 = f2add(a0, f2pk(v[i], v[i + 1]));
+            a1 = f2add(a1, f2pk(v[i + 2], v[i + 3]));
+          }
+          float t0, t1, t2, t3;
+          f2upk(a0, t0, t1);
+          f2upk(a1, t2, t3);
+          const float sum = (t0 + t2) + (t1 + t3);
+          // P of the previous head must have been consumed before P is overwritten
+          if (h > 0) wait_w(SB_PV_DONE, par(step, 4, h - 1));
+          store_sw128(smem + C::OFF_P);
+          publish(SB_P_FULL);
+          const float lh = row_sum(sum, st1);
+          if (h == g) my_l = lh;
+        }
+        // ---- W4: context = O_g / l_g -> XA (head g's 32 columns)
+        wait_w(SB_PV_DONE, par(step, 4, 3));
+        if (ok) tmem_ld32(trow + 256 + c0, v);
+        {
+          const float inv = 1.f / my_l;
+          const uint64_t iv = f2pk(inv, inv);
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) f2upk(f2mul(f2pk(v[i], v[i + 1]), iv), v[i], v[i + 1]);
+        }
+        store_sw128(xa);
+        publish(SB_CTX);
+        // ---- W5: x1 = (x + ctx.Wo^T, accumulated in TMEM) + bo, back into TMEM ; LN2 -> XA
+        wait_w(SB_OP_DONE, par(step, 1, 0));
+        if (ok) tmem_ld32(trow + 384 + c0, v);
+        f2_add_bias32(v, vec + C::V_BO + c0);
+        if (ok) tmem_st32(trow + 384 + c0, v);
+        layer_norm(vec + C::V_LN2W, vec + C::V_LN2B);
+        store_sw128(xa);
+        publish(SB_N2);
+        // ---- W6: GELU chunks -> H ping-pong
+#pragma unroll 1
+        for (int c = 0; c < nch; ++c) {
+          const int b = c & 1;
+          wait_w(SB_FIN + b, par(step, b ? per_b1 : per_b0, c >> 1));
+          if (ok) tmem_ld32(trow + b * 128 + c0, v);
+          f2_add_bias32(v, vec + C::V_BIN + c * 128 + c0);
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) gelu_as2(v[i], v[i + 1]);
+          // the buffer's previous chunk (c-2) must have been consumed by ffn_out
+          if (c >= 2) wait_w(SB_HFREE + b, par(step, b ? per_b1 : per_b0, (c >> 1) - 1));
+          store_sw128(smem + (b ? C::OFF_K : C::OFF_Q));
+          publish(SB_H + b);
+        }
+        // ---- W7: x2 = (x1 + h.W2^T, accumulated in TMEM) + b2 ; final LayerNorm (last layer) -> y
+        wait_w(SB_FOUT, par(step, 1, 0));
+        if (ok) tmem_ld32(trow + 384 + c0, v);
+        f2_add_bias32(v, vec + C::V_BOUT + c0);
+        if (l == p.layers - 1) {
+          layer_norm(vec + C::V_LNFW, vec + C::V_LNFB);
+          // padded rows of the model output are zero (with causal attention and prefix-valid
+          // padding the valid rows never see a padded key, so only the output needs masking)
+          const bool zero = row_ok && p.row_valid != nullptr && p.row_valid[grow] == 0;
+          // this warp's 32x32 box of y (rows 32q.., columns c0..), staged SW128 and stored
+          // by TMA; rows past seq_len fall outside the tensor map and are not written
+          uint8_t* ybox = smem + C::OFF_YST + (q * 4 + g) * 4096;
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<float4*>(ybox + sw128_off(lane, j)) =
+                zero ? make_float4(0.f, 0.f, 0.f, 0.f) : make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && ok) {
+            tma_store_3d(tm_y, ybox, c0, 32 * q, seq);
+            bulk_commit();
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<float4*>(xin_row + sw128_off(r, j)) = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        }
+        // the next step's LN1 (which reuses the statistics buffers) must not race
+        // this step's final row reduction
+        named_bar(bar_id, 128);
       }
+    } else if (nsteps > 0) {
+      // ---- row-split mode (one layer): this CTA owns 64 query rows of its
+      // sequence -- half 0 rows 0-31 and 96-127, half 1 rows 32-95, equal
+      // causal work.  Own row k (0..63) sits in TMEM lanes 32(k/16) + k%16 and
+      // the lane 16 above it: the tiles the MMAs read for Q, P, the context,
+      // LN2 and the GELU chunks hold every own row twice, so lanes j and j+16
+      // of a warp share a row and split its 32 columns, 16 each.  LN1, K and V
+      // cover all 128 rows (every own row attends to keys of the other half).
+      const int half = static_cast<int>(blockIdx.x & 1);
+      const int hh = lane >> 4;                    // which 16 of the warp's 32 columns
+      const int k = q * 16 + (lane & 15);          // own row held by this TMEM lane
+      const int srow = half ? k + 32 : (k < 32 ? k : k + 64);  // its sequence row
+      const int cc = c0 + 16 * hh;                 // this thread's 16 columns
+      // own index of natural row r (natural-layout accumulators: LN1, QKV), -1 if not own
+      const int kn = half ? ((r >= 32 && r < 96) ? r - 32 : -1) : (r < 32 ? r : (r >= 96 ? r - 64 : -1));
+      const int seq = seq_first;
+      const int64_t srow_g = static_cast<int64_t>(seq) * p.seq_len + srow;
+      uint8_t* xin_box = smem + C::OFF_XIN + g * 16384;
+      float u[16];
+      auto take_half = [&]() {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) u[i] = hh ? v[16 + i] : v[i];
+      };
+      auto add16 = [&](const float* b) {  // u += b[0..15] (shared memory)
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) {
+          const float4 bb = *reinterpret_cast<const float4*>(b + i);
+          f2upk(f2add(f2pk(u[i], u[i + 1]), f2pk(bb.x, bb.y)), u[i], u[i + 1]);
+          f2upk(f2add(f2pk(u[i + 2], u[i + 3]), f2pk(bb.z, bb.w)), u[i + 2], u[i + 3]);
+        }
+      };
+      // row statistics over the 8 threads of an own row: the lane pair, then the 4
+      // column groups (slot: the pair's lower TMEM lane, inside this quadrant's
+      // 32 slots like every other reduction of the quadrant)
+      const int ks = r & ~16;
+      auto own_sum = [&](float part, float* buf) {
+        part += __shfl_xor_sync(0xffffffffu, part, 16);
+        buf[g * 128 + ks] = part;
+        named_bar(bar_id, 128);
+        return buf[ks] + buf[128 + ks] + buf[256 + ks] + buf[384 + ks];
+      };
+      auto own_max = [&](float part, float* buf) {
+        part = fmaxf(part, __shfl_xor_sync(0xffffffffu, part, 16));
+        buf[g * 128 + ks] = part;
+        named_bar(bar_id, 128);
+        return fmaxf(fmaxf(buf[ks], buf[128 + ks]), fmaxf(buf[256 + ks], buf[384 + ks]));
+      };
+      // LayerNorm of u (columns cc.. of an own row) in place, two-pass statistics
+      auto layer_norm16 = [&](const float* gamma, const float* beta) {
+        uint64_t a0 = f2pk(0.f, 0.f), a1 = a0;
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) {
+          a0 = f2add(a0, f2pk(u[i], u[i + 1]));
+          a1 = f2add(a1, f2pk(u[i + 2], u[i + 3]));
+        }
+        float t0, t1, t2, t3;
+        f2upk(a0, t0, t1);
+        f2upk(a1, t2, t3);
+        const float mean = own_sum((t0 + t2) + (t1 + t3), st0) * (1.f / 128.f);
+        const uint64_t nm = f2pk(-mean, -mean);
+        a0 = f2pk(0.f, 0.f);
+        a1 = a0;
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) {
+          const uint64_t d0 = f2add(f2pk(u[i], u[i + 1]), nm), d1 = f2add(f2pk(u[i + 2], u[i + 3]), nm);
+          a0 = f2fma(d0, d0, a0);
+          a1 = f2fma(d1, d1, a1);
+          f2upk(d0, u[i], u[i + 1]);
+          f2upk(d1, u[i + 2], u[i + 3]);
+        }
+        f2upk(a0, t0, t1);
+        f2upk(a1, t2, t3);
+        const float rstd = rsqrtf(own_sum((t0 + t2) + (t1 + t3), st1) * (1.f / 128.f) + p.eps);
+        const uint64_t rs = f2pk(rstd, rstd);
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) {
+          const float4 gg = *reinterpret_cast<const float4*>(gamma + cc + i);
+          const float4 bb = *reinterpret_cast<const float4*>(beta + cc + i);
+          f2upk(f2fma(f2mul(f2pk(u[i], u[i + 1]), rs), f2pk(gg.x, gg.y), f2pk(bb.x, bb.y)), u[i], u[i + 1]);
+          f2upk(f2fma(f2mul(f2pk(u[i + 2], u[i + 3]), rs), f2pk(gg.z, gg.w), f2pk(bb.z, bb.w)), u[i + 2], u[i + 3]);
+        }
+      };
+      // u as 16 fp16 values at columns cc of a 128-wide SW128 tile, into both lanes of the own row
+      auto store16_sw128 = [&](uint8_t* base) {
+        uint8_t* atom = base + (cc >> 6) * 16384;
+        const int ch = (cc & 63) >> 3;
+        const uint4 a = make_uint4(pack_half2(u[0], u[1]), pack_half2(u[2], u[3]), pack_half2(u[4], u[5]),
+                                   pack_half2(u[6], u[7]));
+        const uint4 b = make_uint4(pack_half2(u[8], u[9]), pack_half2(u[10], u[11]), pack_half2(u[12], u[13]),
+                                   pack_half2(u[14], u[15]));
+        *reinterpret_cast<uint4*>(atom + sw128_off(r, ch)) = a;
+        *reinterpret_cast<uint4*>(atom + sw128_off(r, ch + 1)) = b;
+        *reinterpret_cast<uint4*>(atom + sw128_off(r ^ 16, ch)) = a;
+        *reinterpret_cast<uint4*>(atom + sw128_off(r ^ 16, ch + 1)) = b;
+      };
+      // v (32 values) as fp16 row `row` of a 128x32 SW64 tile
+      auto store_sw64_row = [&](uint8_t* base, int row) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          *reinterpret_cast<uint4*>(base + row * 64 + ((j ^ ((row >> 1) & 3)) << 4)) =
+              make_uint4(pack_half2(v[8 * j], v[8 * j + 1]), pack_half2(v[8 * j + 2], v[8 * j + 3]),
+                         pack_half2(v[8 * j + 4], v[8 * j + 5]), pack_half2(v[8 * j + 6], v[8 * j + 7]));
+      };
+      auto load_x_row = [&](int row) {  // 32 fp32 columns c0.. of sequence row `row` from XIN
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float4 t = *reinterpret_cast<const float4*>(xin_box + sw128_off(row, j));
+          v[4 * j] = t.x; v[4 * j + 1] = t.y; v[4 * j + 2] = t.z; v[4 * j + 3] = t.w;
+        }
+      };
+
+      // ---- W1: the own row's x -> residual in TMEM [384,512); LN1 of natural row r -> XA
+      stage_vectors(0);
+      wait_w(SB_XFULL, 0);
+      load_x_row(srow);
       if (ok) tmem_st32(trow + 384 + c0, v);
-      if (restage) wait_w(SB_VFULL, static_cast<uint32_t>((p.layers > 1 ? step : 0) & 1));
-      layer_norm(vec + C::V_LN1W, vec + C::V_LN1B);
+      load_x_row(r);
+      layer_norm(vec + C::V_LN1W, vec + C::V_LN1B, 0);
       store_sw128(xa);
-      // the previous step's y store must have read its staging box before Q/K
-      // (which it aliases) are rewritten, and they are rewritten only after N1
-      if (lane == 0) bulk_wait_read_all();
-      __syncwarp();
       publish(SB_N1);
-      // ---- W2: QKV accumulator -> Q/K/V tiles (head g = column group g)
-      wait_w(SB_QKV_DONE, par(step, 1, 0));
+      // ---- W2: QKV (natural rows) -> K, V tiles; Q of own rows into both of their tile rows
+      wait_w(SB_QKV_DONE, 0);
 #pragma unroll 1
       for (int nt = 0; nt < 3; ++nt) {
         if (ok) tmem_ld32(trow + nt * 128 + c0, v);
         f2_add_bias32(v, vec + C::V_BQKV + nt * 128 + c0);
-        store_sw64(smem + (nt == 0 ? C::OFF_Q : nt == 1 ? C::OFF_K : C::OFF_V) + g * 8192);
+        uint8_t* tile = smem + (nt == 0 ? C::OFF_Q : nt == 1 ? C::OFF_K : C::OFF_V) + g * 8192;
+        if (nt > 0) {
+          store_sw64_row(tile, r);
+        } else if (kn >= 0) {
+          const int i1 = (kn >> 4) * 32 + (kn & 15);
+          store_sw64_row(tile, i1);
+          store_sw64_row(tile, i1 + 16);
+        }
       }
       publish(SB_QKV_SMEM);
-      // ---- W3: softmax per head (this thread: row r, keys c0..c0+31)
-      // bit i: key c0+i exists and is not padding (the causal bound is applied per row below);
-      // lane i of the warp tests key c0+i (one coalesced byte load) and the ballot gathers them
+      // ---- W3: softmax per head (own row srow, keys cc..cc+15)
       uint32_t kvalid;
       {
-        const int k = c0 + lane;
-        bool v_ok = k < p.seq_len;
-        if (v_ok && p.row_valid != nullptr) v_ok = p.row_valid[static_cast<int64_t>(seq) * p.seq_len + k] != 0;
-        kvalid = __ballot_sync(0xffffffffu, v_ok);
+        const int key = c0 + lane;
+        bool v_ok = key < p.seq_len;
+        if (v_ok && p.row_valid != nullptr) v_ok = p.row_valid[static_cast<int64_t>(seq) * p.seq_len + key] != 0;
+        kvalid = (__ballot_sync(0xffffffffu, v_ok) >> (16 * hh)) & 0xffffu;
       }
-      if (!p.non_causal) kvalid &= (r >= c0 + 31) ? 0xffffffffu : (r < c0 ? 0u : (0xffffffffu >> (31 - (r - c0))));
-      float my_l = 1.f;  // softmax denominator of head g (this thread's head in the context step)
+      if (!p.non_causal) kvalid &= (srow >= cc + 15) ? 0xffffu : (srow < cc ? 0u : (0xffffu >> (15 - (srow - cc))));
+      float my_l = 1.f;  // softmax denominator of head g
 #pragma unroll 1
       for (int h = 0; h < 4; ++h) {
-        wait_w(SB_S_FULL + (h & 1), par(step, 2, h >> 1));
+        wait_w(SB_S_FULL + (h & 1), par(0, 2, h >> 1));
         if (ok) tmem_ld32(trow + (h & 1) * 128 + c0, v);
-        if (kvalid != 0xffffffffu) {  // raw scores; the positive scale is applied in the exponent
+        take_half();
+        if (kvalid != 0xffffu) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (!((kvalid >> i) & 1u)) v[i] = -INFINITY;
+          for (int i = 0; i < 16; ++i)
+            if (!((kvalid >> i) & 1u)) u[i] = -INFINITY;
         }
         float mx = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) mx = fmax3(mx, v[i], v[i + 1]);
-        const float m = row_max(mx, st0) * p.scale_log2;  // reductions alternate st0/st1 strictly
+        for (int i = 0; i < 16; i += 2) mx = fmax3(mx, u[i], u[i + 1]);
+        const float m = own_max(mx, st0) * p.scale_log2;  // reductions alternate st0/st1 strictly
         const uint64_t sc = f2pk(p.scale_log2, p.scale_log2), nm = f2pk(-m, -m);
         uint64_t a0 = f2pk(0.f, 0.f), a1 = a0;
 #pragma unroll
-        for (int i = 0; i < 32; i += 4) {
+        for (int i = 0; i < 16; i += 4) {
           float e0, e1, e2, e3;
-          f2upk(f2fma(f2pk(v[i], v[i + 1]), sc, nm), e0, e1);
-          f2upk(f2fma(f2pk(v[i + 2], v[i + 3]), sc, nm), e2, e3);
-          v[i] = fast_exp2(e0); v[i + 1] = fast_exp2(e1); v[i + 2] = fast_exp2(e2); v[i + 3] = fast_exp2(e3);
-          a0 = f2add(a0, f2pk(v[i], v[i + 1]));
-          a1 = f2add(a1, f2pk(v[i + 2], v[i + 3]));
+          f2upk(f2fma(f2pk(u[i], u[i + 1]), sc, nm), e0, e1);
+          f2upk(f2fma(f2pk(u[i + 2], u[i + 3]), sc, nm), e2, e3);
+          u[i] = fast_exp2(e0); u[i + 1] = fast_exp2(e1); u[i + 2] = fast_exp2(e2); u[i + 3] = fast_exp2(e3);
+          a0 = f2add(a0, f2pk(u[i], u[i + 1]));
+          a1 = f2add(a1, f2pk(u[i + 2], u[i + 3]));
         }
         float t0, t1, t2, t3;
         f2upk(a0, t0, t1);
         f2upk(a1, t2, t3);
         const float sum = (t0 + t2) + (t1 + t3);
-        // P of the previous head must have been consumed before P is overwritten
-        if (h > 0) wait_w(SB_PV_DONE, par(step, 4, h - 1));
-        store_sw128(smem + C::OFF_P);
+        if (h > 0) wait_w(SB_PV_DONE, par(0, 4, h - 1));  // P of the previous head consumed
+        store16_sw128(smem + C::OFF_P);
         publish(SB_P_FULL);
-        const float lh = row_sum(sum, st1);
+        const float lh = own_sum(sum, st1);
         if (h == g) my_l = lh;
       }
-      // ---- W4: context = O_g / l_g -> XA (head g's 32 columns)
-      wait_w(SB_PV_DONE, par(step, 4, 3));
+      // ---- W4: context (16 columns of head g) = O / l -> XA
+      wait_w(SB_PV_DONE, par(0, 4, 3));
       if (ok) tmem_ld32(trow + 256 + c0, v);
+      take_half();
       {
         const float inv = 1.f / my_l;
         const uint64_t iv = f2pk(inv, inv);
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) f2upk(f2mul(f2pk(v[i], v[i + 1]), iv), v[i], v[i + 1]);
+        for (int i = 0; i < 16; i += 2) f2upk(f2mul(f2pk(u[i], u[i + 1]), iv), u[i], u[i + 1]);
       }
-      store_sw128(xa);
+      store16_sw128(xa);
       publish(SB_CTX);
-      // ---- W5: x1 = (x + ctx.Wo^T, accumulated in TMEM) + bo, back into TMEM ; LN2 -> XA
-      wait_w(SB_OP_DONE, par(step, 1, 0));
+      // ---- W5: x1 = (x + ctx.Wo^T, in TMEM) + bo, kept in TMEM without bo (ffn_out
+      // accumulates onto it; W7 adds bo and b2) ; LN2 -> XA
+      wait_w(SB_OP_DONE, 0);
       if (ok) tmem_ld32(trow + 384 + c0, v);
-      f2_add_bias32(v, vec + C::V_BO + c0);
-      if (ok) tmem_st32(trow + 384 + c0, v);
-      layer_norm(vec + C::V_LN2W, vec + C::V_LN2B);
-      store_sw128(xa);
+      take_half();
+      add16(vec + C::V_BO + cc);
+      layer_norm16(vec + C::V_LN2W, vec + C::V_LN2B);
+      store16_sw128(xa);
       publish(SB_N2);
       // ---- W6: GELU chunks -> H ping-pong
 #pragma unroll 1
       for (int c = 0; c < nch; ++c) {
         const int b = c & 1;
-        wait_w(SB_FIN + b, par(step, b ? per_b1 : per_b0, c >> 1));
+        wait_w(SB_FIN + b, par(0, b ? per_b1 : per_b0, c >> 1));
         if (ok) tmem_ld32(trow + b * 128 + c0, v);
-        f2_add_bias32(v, vec + C::V_BIN + c * 128 + c0);
+        take_half();
+        add16(vec + C::V_BIN + c * 128 + cc);
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) gelu_as2(v[i], v[i + 1]);
-        // the buffer's previous chunk (c-2) must have been consumed by ffn_out
-        if (c >= 2) wait_w(SB_HFREE + b, par(step, b ? per_b1 : per_b0, (c >> 1) - 1));
-        store_sw128(smem + (b ? C::OFF_K : C::OFF_Q));
+        for (int i = 0; i < 16; i += 2) gelu_as2(u[i], u[i + 1]);
+        if (c >= 2) wait_w(SB_HFREE + b, par(0, b ? per_b1 : per_b0, (c >> 1) - 1));
+        store16_sw128(smem + (b ? C::OFF_K : C::OFF_Q));
         publish(SB_H + b);
       }
-      // ---- W7: x2 = (x1 + h.W2^T, accumulated in TMEM) + b2 ; final LayerNorm (last layer) -> y
-      wait_w(SB_FOUT, par(step, 1, 0));
+      // ---- W7: x2 = (x + attn + ffn, in TMEM) + bo + b2 ; final LayerNorm -> y (16 rows x 32 columns per warp)
+      wait_w(SB_FOUT, 0);
       if (ok) tmem_ld32(trow + 384 + c0, v);
-      f2_add_bias32(v, vec + C::V_BOUT + c0);
-      if (l == p.layers - 1) {
-        layer_norm(vec + C::V_LNFW, vec + C::V_LNFB);
-        // padded rows of the model output are zero (with causal attention and prefix-valid
-        // padding the valid rows never see a padded key, so only the output needs masking)
-        const bool zero = row_ok && p.row_valid != nullptr && p.row_valid[grow] == 0;
-        // this warp's 32x32 box of y (rows 32q.., columns c0..), staged SW128 and stored
-        // by TMA; rows past seq_len fall outside the tensor map and are not written
-        uint8_t* ybox = smem + C::OFF_YST + (q * 4 + g) * 4096;
+      take_half();
+      add16(vec + C::V_BO + cc);
+      add16(vec + C::V_BOUT + cc);
+      layer_norm16(vec + C::V_LNFW, vec + C::V_LNFB);
+      {
+        const bool zero = srow < p.seq_len && p.row_valid != nullptr && p.row_valid[srow_g] == 0;
+        // the warp's own rows are 16 consecutive sequence rows: one 16x32 box, staged SW128
+        uint8_t* ybox = smem + C::OFF_YST + (q * 4 + g) * 2048;
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-          *reinterpret_cast<float4*>(ybox + sw128_off(lane, j)) =
-              zero ? make_float4(0.f, 0.f, 0.f, 0.f) : make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        for (int j = 0; j < 4; ++j)
+          *reinterpret_cast<float4*>(ybox + sw128_off(lane & 15, 4 * hh + j)) =
+              zero ? make_float4(0.f, 0.f, 0.f, 0.f) : make_float4(u[4 * j], u[4 * j + 1], u[4 * j + 2], u[4 * j + 3]);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0 && ok) {
-          tma_store_3d(&tm_y, ybox, c0, 32 * q, seq);
+          tma_store_3d(tm_y, ybox, c0, half ? 32 + 16 * q : (q < 2 ? 16 * q : 64 + 16 * q), seq);
           bulk_commit();
         }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          *reinterpret_cast<float4*>(xin_row + sw128_off(r, j)) = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
       }
-      // the next step's LN1 (which reuses the statistics buffers) must not race
-      // this step's final row reduction
-      named_bar(bar_id, 128);
     }
     if (lane == 0) bulk_wait_all();  // the last y stores are complete before the CTA exits
     // after an abort, the last vector copies land before shared memory is released
@@ -613,6 +943,26 @@ __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+}
+
+__global__ void __launch_bounds__(SmallCfg::THREADS, 1)
+    k_block_small(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_o,
+                  const __grid_constant__ CUtensorMap tm_in, const __grid_constant__ CUtensorMap tm_out,
+                  const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_y,
+                  const SmallParams p) {
+  block_small_body<false>(&tm_qkv, &tm_o, &tm_in, &tm_out, &tm_x, &tm_y, p);
+}
+
+// Row-split mode for one layer and at most one sequence per two SMs: CTAs 2s
+// and 2s+1 both run sequence s, each finishing 64 of its query rows (tm_y has
+// 16-row boxes).  No data moves between the two CTAs: each computes LN1, K and
+// V for all 128 rows itself, which costs less than exchanging them.
+__global__ void __launch_bounds__(SmallCfg::THREADS, 1)
+    k_block_rows(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_o,
+                 const __grid_constant__ CUtensorMap tm_in, const __grid_constant__ CUtensorMap tm_out,
+                 const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_y,
+                 const SmallParams p) {
+  block_small_body<true>(&tm_qkv, &tm_o, &tm_in, &tm_out, &tm_x, &tm_y, p);
 }
 
 }  // namespace b200

@@ -93,3 +93,47 @@ def test_fused_small_noncausal(tt, B, S, F, L):
                                    oracle.OracleConfig(B, S, 128, 4, F, L, False), x.numpy(),
                                    None if m is None else m.numpy())
         assert oracle.compare_outputs(ref, y, rtol=RTOL, atol=ATOL).passed
+
+
+@pytest.mark.parametrize("mode", ["0", "1"])
+def test_fused_single_and_row_split_in_subprocess(mode):
+    """The one-CTA-per-sequence kernel and the row-split kernel (two CTAs per
+    sequence, each finishing half of the query rows; B200_SMALL_ROWS forces the
+    choice and is read once per process, hence the child process) against the
+    oracle: ffn 128-512, ragged S, key padding, non-causal, more sequences than
+    SMs, and a two-layer model (always the one-CTA kernel)."""
+    import os
+    import subprocess
+    import sys
+    code = r'''
+import torch
+import oracle
+import torch_transformer_benchmark as tt
+rt = tt._pkg.runtime
+DEV = "cuda"
+for (B, S, F, L, causal, pad) in ((4, 128, 512, 1, True, 0.0), (64, 128, 512, 1, True, 0.0),
+                                  (3, 100, 512, 1, True, 0.0), (2, 37, 256, 1, True, 0.0),
+                                  (5, 128, 128, 1, True, 0.25), (6, 120, 384, 1, True, 0.2),
+                                  (3, 70, 512, 1, False, 0.3), (4, 128, 256, 1, False, 0.0),
+                                  (300, 128, 512, 1, True, 0.0), (3, 128, 512, 2, True, 0.0)):
+    cfg = tt.TransformerConfig(B, S, 128, 4, F, L, causal)
+    torch.manual_seed(B * 7 + L + F)
+    model = tt.UserOptimizedTransformer(cfg).to(DEV).eval()
+    x, mask = oracle.generate_random_case(B, S, 128, B + S + F, padding_ratio=pad)
+    m = mask if pad > 0 else None
+    with torch.inference_mode():
+        y = model(x.to(DEV), None if m is None else m.to(DEV)).cpu()
+    assert model.last_strategy == "fused_small"
+    assert rt.device_error(clear=True) == 0
+    params = oracle.params_from_state_dict(model.state_dict())
+    for lo, hi in ((0, min(B, 8)), (max(B - 4, 0), B)):
+        ref = oracle.model_forward(params, oracle.OracleConfig(hi - lo, S, 128, 4, F, L, causal), x[lo:hi].numpy(),
+                                   None if m is None else m[lo:hi].numpy())
+        res = oracle.compare_outputs(ref, y[lo:hi], rtol=0.02, atol=0.002)
+        assert res.passed, (B, S, F, L, causal, pad, res)
+print("OK")
+'''
+    env = dict(os.environ, B200_SMALL_ROWS=mode)
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and "OK" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
