@@ -164,14 +164,33 @@ class UserOptimizedTransformer(nn.Module):
         self._plan: Dict[Tuple, str] = {}
         self._graphs: "OrderedDict[Tuple, torch.cuda.CUDAGraph]" = OrderedDict()
         self._warm: set = set()
+        self._slots: Optional[list] = None  # (module._parameters, name) of every parameter
+        self._edges: list = []              # (module._modules, name, child) of every submodule
         self.last_strategy: Optional[str] = None
 
     # ------------------------------------------------------------------ weights
     def _param_key(self, device) -> tuple:
-        # Inference tensors (a model built under torch.inference_mode) carry no
-        # version counter; their identity and storage stand in for it.
-        return (device, tuple((id(p), p.data_ptr(), -1 if p.is_inference() else p._version)
-                              for p in self.parameters()))
+        """Identity, storage and version of every parameter: the packs are rebuilt when it changes.
+
+        The parameters are read through their (owning module, name) slots, found once
+        and found again only when a submodule was replaced (walking ``parameters()`` on
+        every call cost more than the whole kernel launch of a small forward), so a
+        replaced Parameter object or submodule, an in-place update (version counter)
+        and a device move (storage) are all seen.  Inference tensors (a model built
+        under torch.inference_mode) carry no version counter; their identity and
+        storage stand in for it."""
+        ps = None
+        if self._slots is not None and all(mods.get(name) is child for mods, name, child in self._edges):
+            try:
+                ps = [params[name] for params, name in self._slots]
+            except KeyError:  # a parameter was deleted
+                ps = None
+        if ps is None:
+            mods = list(self.modules())
+            self._edges = [(m._modules, name, c) for m in mods for name, c in m._modules.items()]
+            self._slots = [(m._parameters, name) for m in mods for name, prm in m._parameters.items() if prm is not None]
+            ps = [params[name] for params, name in self._slots]
+        return (device, tuple((id(p), p.data_ptr(), -1 if p.is_inference() else p._version) for p in ps))
 
     def _ensure_packs(self, device: torch.device) -> None:
         key = self._param_key(device)
@@ -343,9 +362,12 @@ class UserOptimizedTransformer(nn.Module):
         out_dtype = x.dtype
         xin = x if (x.dtype == torch.float32 and x.is_contiguous()) else x.to(torch.float32).contiguous()
         dev = xin.device
-        with torch.cuda.device(dev):
-            y = torch.empty_like(xin)
+        y = torch.empty_like(xin)
+        if dev.index == torch.cuda.current_device():
             self._forward_into(xin, y, rows_valid, kv_lens)
+        else:
+            with torch.cuda.device(dev):
+                self._forward_into(xin, y, rows_valid, kv_lens)
         return y if out_dtype == torch.float32 else y.to(out_dtype)
 
     def _run_graphed(self, x: torch.Tensor, y: torch.Tensor, ws: torch.Tensor, strat: str,
