@@ -20,6 +20,7 @@
 #include "gemm2.cuh"
 #include "attn.cuh"
 #include "attn2.cuh"
+#include "attn_small.cuh"
 #include "fused_small.cuh"
 
 using namespace b200;
@@ -439,14 +440,9 @@ int add_ln_impl(const float* a, const float* b, const float* bias, float* sum_ou
 }
 
 // ------------------------------------------------------------------ attention
-template <int HD, int BN>
-int launch_attn_t(const B200AttnArgs& a, cudaStream_t st) {
-  using C = AttnCfg<HD, BN>;
-  constexpr CUtensorMapSwizzle SW = C::ATOM_E == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-  CUtensorMap tq, tk, tv;
-  if (int rc = make_map_f16(&tq, a.q, a.q_rows, a.ld_q, a.ld_q, C::ATOM_E, 128, SW)) return rc;
-  if (int rc = make_map_f16(&tk, a.k, a.kv_rows, a.ld_k, a.ld_k, C::ATOM_E, BN, SW)) return rc;
-  if (int rc = make_map_f16(&tv, a.v, a.kv_rows, a.ld_v, a.ld_v, C::ATOM_E, BN, SW)) return rc;
+// Kernel parameters of one launch (every attention kernel takes the same ones)
+template <int HD>
+AttnParams attn_params(const B200AttnArgs& a) {
   AttnParams p{};
   p.H = a.heads;
   p.q_len = a.q_len;
@@ -465,6 +461,18 @@ int launch_attn_t(const B200AttnArgs& a, cudaStream_t st) {
   p.scale_log2 = static_cast<float>(1.4426950408889634 / __builtin_sqrt(static_cast<double>(HD)));
   p.non_causal = a.non_causal;
   p.kv_lens = a.kv_lens;
+  return p;
+}
+
+template <int HD, int BN>
+int launch_attn_t(const B200AttnArgs& a, cudaStream_t st) {
+  using C = AttnCfg<HD, BN>;
+  constexpr CUtensorMapSwizzle SW = C::ATOM_E == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  CUtensorMap tq, tk, tv;
+  if (int rc = make_map_f16(&tq, a.q, a.q_rows, a.ld_q, a.ld_q, C::ATOM_E, 128, SW)) return rc;
+  if (int rc = make_map_f16(&tk, a.k, a.kv_rows, a.ld_k, a.ld_k, C::ATOM_E, BN, SW)) return rc;
+  if (int rc = make_map_f16(&tv, a.v, a.kv_rows, a.ld_v, a.ld_v, C::ATOM_E, BN, SW)) return rc;
+  const AttnParams p = attn_params<HD>(a);
   // TMEM: at most two 256-column CTAs per SM, so request enough shared memory
   // that a third cannot be co-resident and block in tcgen05.alloc.
   int smem = C::TOTAL;
@@ -476,6 +484,17 @@ int launch_attn_t(const B200AttnArgs& a, cudaStream_t st) {
   return launch_status();
 }
 
+// head_dim 8 / 16: CUDA-core kernel (attn_small.cuh), no tensor maps
+template <int HD>
+int launch_attn_small_t(const B200AttnArgs& a, cudaStream_t st) {
+  const AttnParams p = attn_params<HD>(a);
+  dim3 grid((a.q_len + ATTN_SMALL_ROWS - 1) / ATTN_SMALL_ROWS, a.heads, a.batch);
+  k_attn_small<HD><<<grid, ATTN_SMALL_ROWS, 0, st>>>(static_cast<const __half*>(a.q), a.ld_q,
+                                                     static_cast<const __half*>(a.k), a.ld_k,
+                                                     static_cast<const __half*>(a.v), a.ld_v, p);
+  return launch_status();
+}
+
 template <int HD>
 int launch_attn2_t(const B200AttnArgs& a, cudaStream_t st) {
   using C = Attn2Cfg<HD>;
@@ -484,24 +503,7 @@ int launch_attn2_t(const B200AttnArgs& a, cudaStream_t st) {
   if (int rc = make_map_f16(&tq, a.q, a.q_rows, a.ld_q, a.ld_q, HD, 128, SW)) return rc;
   if (int rc = make_map_f16(&tk, a.k, a.kv_rows, a.ld_k, a.ld_k, HD, C::BN, SW)) return rc;
   if (int rc = make_map_f16(&tv, a.v, a.kv_rows, a.ld_v, a.ld_v, HD, C::BN, SW)) return rc;
-  AttnParams p{};
-  p.H = a.heads;
-  p.q_len = a.q_len;
-  p.q_offset = a.q_offset;
-  p.kv_len = a.kv_len;
-  p.q_seq_rows = a.q_seq_rows;
-  p.kv_seq_rows = a.kv_seq_rows;
-  p.q_row0 = a.q_row0;
-  p.kv_row0 = a.kv_row0;
-  p.q_col0 = a.q_col0;
-  p.k_col0 = a.k_col0;
-  p.v_col0 = a.v_col0;
-  p.out = static_cast<__half*>(a.out) + static_cast<int64_t>(a.out_row0) * a.ld_out;
-  p.ld_out = a.ld_out;
-  p.out_seq_rows = a.out_seq_rows;
-  p.scale_log2 = static_cast<float>(1.4426950408889634 / __builtin_sqrt(static_cast<double>(HD)));
-  p.non_causal = a.non_causal;
-  p.kv_lens = a.kv_lens;
+  const AttnParams p = attn_params<HD>(a);
   auto kern = k_flash_causal2<HD>;
   const int smem = C::TOTAL;
   if (int rc = set_smem(reinterpret_cast<const void*>(kern), smem)) return rc;
@@ -529,7 +531,7 @@ int attn_impl(const B200AttnArgs* a, cudaStream_t st) {
   if (a->q_len == 0) return B200_OK;
   if (a->q_offset + a->q_len > a->kv_len) return B200_ERR_ARG;
   const int hd = a->head_dim;
-  if (hd != 32 && hd != 64 && hd != 128 && hd != 256) return B200_ERR_HEAD_DIM;
+  if (hd != 8 && hd != 16 && hd != 32 && hd != 64 && hd != 128 && hd != 256) return B200_ERR_HEAD_DIM;
   if (a->ld_q % 8 || a->ld_k % 8 || a->ld_v % 8 || a->ld_out % 8) return B200_ERR_ALIGN;
   if (!al16(a->q) || !al16(a->k) || !al16(a->v) || !al16(a->out)) return B200_ERR_ALIGN;
   if (a->q_col0 % 8 || a->k_col0 % 8 || a->v_col0 % 8) return B200_ERR_ALIGN;
@@ -548,6 +550,8 @@ int attn_impl(const B200AttnArgs* a, cudaStream_t st) {
   // SM, measured (L2 flushed): head_dim 64 favours two tiles from short
   // sequences on (B=16 S=1024 H=16: 107 vs 146 us; B=8 S=2048: 158 vs 223 us);
   // head_dim 32 keeps one tile below S=2048 (B=64 S=1024 H=4: 86 vs 99 us).
+  if (hd == 8) return launch_attn_small_t<8>(*a, st);
+  if (hd == 16) return launch_attn_small_t<16>(*a, st);
   const int forced = attn_tiles_forced();
   const int min_q = hd == 64 ? ATTN_TWO_TILE_MIN_Q_HD64 : ATTN_TWO_TILE_MIN_Q;
   if (forced == 2 || (forced == 0 && a->q_len >= min_q)) {
@@ -681,7 +685,7 @@ int block_impl(const B200BlockArgs* a, cudaStream_t st) {
   if (a->x == a->y) return B200_ERR_ARG;
   const long long M = static_cast<long long>(a->batch) * a->seq_len;
   const int d = a->d_model, F = a->ffn_dim, H = a->num_heads, hd = d / H;
-  if (hd != 32 && hd != 64 && hd != 128 && hd != 256) return B200_ERR_HEAD_DIM;
+  if (hd != 8 && hd != 16 && hd != 32 && hd != 64 && hd != 128 && hd != 256) return B200_ERR_HEAD_DIM;
   if (M > 0x7fffffffLL) return B200_ERR_TILE;
   BlockWs w = carve(a->workspace, M, d, F);
   if (!a->workspace || a->workspace_bytes < w.bytes) return B200_ERR_WORKSPACE;
@@ -796,7 +800,7 @@ int block_chunked_impl(const B200BlockArgs* a, int chunk_rows, cudaStream_t st) 
   if (a->non_causal) return B200_ERR_CONFIG;  // prefix chunking is a causal construction
   const long long M = static_cast<long long>(a->batch) * a->seq_len;
   const int d = a->d_model, F = a->ffn_dim, H = a->num_heads, hd = d / H, S = a->seq_len;
-  if (hd != 32 && hd != 64 && hd != 128 && hd != 256) return B200_ERR_HEAD_DIM;
+  if (hd != 8 && hd != 16 && hd != 32 && hd != 64 && hd != 128 && hd != 256) return B200_ERR_HEAD_DIM;
   if (M > 0x7fffffffLL) return B200_ERR_TILE;
   const int R = chunk_rows < S ? chunk_rows : S;
   ChunkWs w = carve_chunked(a->workspace, M, R, d, F);

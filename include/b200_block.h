@@ -52,7 +52,7 @@ enum {
   B200_ERR_SPLIT = -3,     /* (reserved: the reference's K % SPLIT check)            */
   B200_ERR_SMEM = -4,      /* dynamic shared-memory opt-in refused                   */
   B200_ERR_ALIGN = -5,     /* pointer or leading dimension not 16-byte aligned       */
-  B200_ERR_HEAD_DIM = -6,  /* head_dim not in {32, 64, 128, 256}                     */
+  B200_ERR_HEAD_DIM = -6,  /* head_dim not in {8, 16, 32, 64, 128, 256}             */
   B200_ERR_DEVICE = -7,    /* a device-side wait timed out (see b200_device_error)   */
   B200_ERR_LAUNCH = -8,    /* the CUDA launch itself failed                          */
   B200_ERR_ARG = -9,       /* null pointer, negative size or inconsistent arguments  */

@@ -189,6 +189,7 @@ ATTN_CASES = [  # B, H, S, hd
     (2, 4, 128, 32), (3, 2, 100, 32), (2, 4, 384, 64), (1, 2, 300, 128), (2, 4, 128, 256), (1, 2, 200, 256),
     (2, 4, 1024, 32),
     (1, 2, 2304, 64), (2, 2, 2100, 32),  # q_len >= 2048: two query tiles per CTA
+    (2, 4, 128, 8), (3, 16, 100, 8), (2, 8, 300, 16), (1, 4, 1000, 8),  # head_dim 8 / 16: CUDA-core kernel
 ]
 
 
@@ -207,7 +208,7 @@ def test_flash_causal_vs_torch(rt, B, H, S, hd):
 
 
 @pytest.mark.parametrize("hd,chunk,S", [(64, 256, 640), (32, 128, 640), (64, 192, 640), (256, 128, 640),
-                                        (64, 2048, 4352), (32, 2176, 4352)])
+                                        (64, 2048, 4352), (32, 2176, 4352), (8, 192, 640), (16, 256, 700)])
 def test_flash_prefix_chunks_equal_full(rt, hd, chunk, S):
     """Query chunks [c0:c1) over the K/V prefix [0:c1) (q_offset=c0) reproduce
     full causal attention row for row -- the chunked forward's identity."""
@@ -243,7 +244,8 @@ def test_launch_rejects_unsupported_shapes(rt):
         rt.flash_causal(qkv, qkv, qkv, o, batch=1, heads=2, head_dim=48, q_len=128, kv_len=128)
 
 
-@pytest.mark.parametrize("B,H,S,hd", [(2, 2, 200, 64), (2, 4, 128, 32), (1, 2, 2200, 64), (2, 2, 300, 256)])
+@pytest.mark.parametrize("B,H,S,hd", [(2, 2, 200, 64), (2, 4, 128, 32), (1, 2, 2200, 64), (2, 2, 300, 256),
+                                      (2, 16, 128, 8), (2, 4, 300, 16)])
 def test_flash_noncausal_with_key_lengths_vs_torch(rt, B, H, S, hd):
     """Full attention with per-sequence valid key counts (key padding)."""
     g = torch.Generator().manual_seed(S + hd)

@@ -102,6 +102,30 @@ def test_baseline_configs(tt, name, B, S, d, H, sample):
     print(f"{name}: max_abs={worst:.4g}")
 
 
+# The reference's official matrix (causal, 4 layers, ffn_dim = d_model; run_eval.sh:44-58,
+# README.md:46-58), rows 1-13: (row, B, S, d, H, sampled batches or None).  Rows 7 and 11
+# have head_dim 8.
+MATRIX = [
+    (1, 64, 128, 128, 4, None), (2, 1, 128, 128, 4, None), (3, 4, 128, 128, 4, None), (4, 16, 128, 128, 4, None),
+    (5, 128, 128, 128, 4, 16), (6, 10000, 128, 128, 4, 8), (7, 64, 128, 32, 4, None), (8, 64, 128, 1024, 4, 4),
+    (9, 64, 128, 128, 1, None), (10, 64, 128, 128, 2, None), (11, 64, 128, 128, 16, None),
+    (12, 64, 32, 128, 4, None), (13, 64, 1024, 128, 4, 4),
+]
+
+
+@pytest.mark.parametrize("row,B,S,d,H,sample", MATRIX, ids=[f"row{m[0]}" for m in MATRIX])
+def test_official_matrix_rows(tt, row, B, S, d, H, sample):
+    model, _ = _model(tt, B, S, d, H, d, 4, seed=1234)
+    x, _ = oracle.generate_random_case(B, S, d, 1234 + row)
+    y = _run(model, x)
+    bsel = np.arange(B) if sample is None else np.sort(np.random.default_rng(row).choice(B, size=sample, replace=False))
+    ref = oracle.model_forward(oracle.params_from_state_dict(model.state_dict()),
+                               oracle.OracleConfig(len(bsel), S, d, H, d, 4, True), x[bsel].numpy())
+    res = oracle.compare_outputs(ref, y[bsel], rtol=RTOL, atol=ATOL)
+    print(f"row {row} ({model.last_strategy}): max_abs={res.max_abs_error:.3g}")
+    assert res.passed, (row, res)
+
+
 def test_harness_contract(tt):
     """No mutation of the fp32 input, repeat calls agree bitwise, the output
     depends on the input (experiments/g7_0_chunked_oversize.py:667-742)."""
