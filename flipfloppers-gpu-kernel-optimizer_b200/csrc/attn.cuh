@@ -179,6 +179,7 @@ __global__ void __launch_bounds__(192, 2)  // two CTAs per SM (registers <= 170)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  griddep_sync();  // the previous kernel's outputs are complete from here on
 
   if (warp == 0) {
     if (lane == 0) {

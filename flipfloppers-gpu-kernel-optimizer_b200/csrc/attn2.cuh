@@ -109,6 +109,7 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  griddep_sync();  // the previous kernel's outputs are complete from here on
 
   if (warp == 0) {
     if (lane == 0) {

@@ -31,6 +31,7 @@ __global__ void __launch_bounds__(ATTN_SMALL_ROWS)
   __shared__ uint4 ks[ATTN_SMALL_KEYS][CH];
   __shared__ uint4 vs[ATTN_SMALL_KEYS][CH];
 
+  griddep_sync();
   const int tile = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int i = tile * ATTN_SMALL_ROWS + threadIdx.x;  // query row within this call
   const bool active = i < p.q_len;

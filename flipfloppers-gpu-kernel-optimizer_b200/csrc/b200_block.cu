@@ -105,6 +105,34 @@ int launch_status() {
   return B200_ERR_LAUNCH;
 }
 
+// Programmatic dependent launch: a kernel may start its prologue while the
+// previous kernel of the stream finishes (each kernel waits for it in
+// griddep_sync before touching global data).  B200_PDL=0 launches with plain
+// stream order instead.
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("B200_PDL");
+    return !(e != nullptr && e[0] == '0');
+  }();
+  return on;
+}
+
+// (errors are left for the caller's launch_status(), like a <<<>>> launch)
+template <typename... Params, typename... Args>
+void launch_kernel(void (*kern)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 // Refuse a launch the kernel's compiled resources cannot satisfy, with the reason recorded.
 int check_block_fits(const void* fn, int threads) {
   cudaFuncAttributes fa{};
@@ -177,7 +205,7 @@ int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMa
   if (int rc = set_smem(reinterpret_cast<const void*>(kern), smem)) return rc;
   const long long tiles = static_cast<long long>((p.M + 127) / 128) * ((p.N + BN - 1) / BN);
   const int grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
-  kern<<<grid, GEMM_THREADS, smem, st>>>(ta, tw, to, tn ? *tn : to, p);
+  launch_kernel(kern, dim3(grid), dim3(GEMM_THREADS), smem, st, ta, tw, to, tn ? *tn : to, p);
   return launch_status();
 }
 
@@ -227,7 +255,7 @@ int launch_gemm2_t(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorM
   }
   const long long tiles = static_cast<long long>((p.M + 255) / 256) * ((p.N + 255) / 256);
   const int clusters = static_cast<int>(tiles < maxcl ? tiles : maxcl);
-  kern<<<2 * clusters, GEMM_THREADS, smem, st>>>(ta, tw, to, p);
+  launch_kernel(kern, dim3(2 * clusters), dim3(GEMM_THREADS), smem, st, ta, tw, to, p);
   return launch_status();
 }
 
@@ -369,9 +397,11 @@ int launch_ln_t(const float* x, long long ldx, const float* g, const float* b, v
   const int warps = 8;
   dim3 grid((rows + warps - 1) / warps);
   if (f16)
-    k_layernorm<VPL, VEC4, true><<<grid, 32 * warps, 0, st>>>(x, ldx, g, b, out, ldo, rows, d, eps, copy, ldc);
+    launch_kernel(k_layernorm<VPL, VEC4, true>, dim3(grid), dim3(32 * warps), 0, st, x, ldx, g, b, out, ldo, rows, d,
+                  eps, copy, ldc);
   else
-    k_layernorm<VPL, VEC4, false><<<grid, 32 * warps, 0, st>>>(x, ldx, g, b, out, ldo, rows, d, eps, copy, ldc);
+    launch_kernel(k_layernorm<VPL, VEC4, false>, dim3(grid), dim3(32 * warps), 0, st, x, ldx, g, b, out, ldo, rows, d,
+                  eps, copy, ldc);
   return launch_status();
 }
 
@@ -414,9 +444,11 @@ int launch_add_ln_t(const float* a, const float* b, const float* bias, float* su
                     const float* be, void* out, bool f16, int rows, int d, float eps, cudaStream_t st) {
   dim3 grid((rows + 7) / 8);
   if (f16)
-    k_add_layernorm<VPL, true><<<grid, 256, 0, st>>>(a, b, bias, sum_out, g, be, out, rows, d, eps);
+    launch_kernel(k_add_layernorm<VPL, true>, dim3(grid), dim3(256), 0, st, a, b, bias, sum_out, g, be, out, rows, d,
+                  eps);
   else
-    k_add_layernorm<VPL, false><<<grid, 256, 0, st>>>(a, b, bias, sum_out, g, be, out, rows, d, eps);
+    launch_kernel(k_add_layernorm<VPL, false>, dim3(grid), dim3(256), 0, st, a, b, bias, sum_out, g, be, out, rows, d,
+                  eps);
   return launch_status();
 }
 
@@ -480,7 +512,7 @@ int launch_attn_t(const B200AttnArgs& a, cudaStream_t st) {
   auto kern = k_flash_causal<HD, BN>;
   if (int rc = set_smem(reinterpret_cast<const void*>(kern), smem)) return rc;
   dim3 grid((a.q_len + 127) / 128, a.heads, a.batch);
-  kern<<<grid, 192, smem, st>>>(tq, tk, tv, p);
+  launch_kernel(kern, dim3(grid), dim3(192), smem, st, tq, tk, tv, p);
   return launch_status();
 }
 
@@ -489,9 +521,8 @@ template <int HD>
 int launch_attn_small_t(const B200AttnArgs& a, cudaStream_t st) {
   const AttnParams p = attn_params<HD>(a);
   dim3 grid((a.q_len + ATTN_SMALL_ROWS - 1) / ATTN_SMALL_ROWS, a.heads, a.batch);
-  k_attn_small<HD><<<grid, ATTN_SMALL_ROWS, 0, st>>>(static_cast<const __half*>(a.q), a.ld_q,
-                                                     static_cast<const __half*>(a.k), a.ld_k,
-                                                     static_cast<const __half*>(a.v), a.ld_v, p);
+  launch_kernel(k_attn_small<HD>, dim3(grid), dim3(ATTN_SMALL_ROWS), 0, st, static_cast<const __half*>(a.q), a.ld_q,
+                static_cast<const __half*>(a.k), a.ld_k, static_cast<const __half*>(a.v), a.ld_v, p);
   return launch_status();
 }
 
@@ -508,7 +539,7 @@ int launch_attn2_t(const B200AttnArgs& a, cudaStream_t st) {
   const int smem = C::TOTAL;
   if (int rc = set_smem(reinterpret_cast<const void*>(kern), smem)) return rc;
   dim3 grid((a.q_len + 255) / 256, a.heads, a.batch);
-  kern<<<grid, 320, smem, st>>>(tq, tk, tv, p);
+  launch_kernel(kern, dim3(grid), dim3(320), smem, st, tq, tk, tv, p);
   return launch_status();
 }
 
@@ -636,13 +667,14 @@ int fused_small_impl(const B200FusedSmallArgs* a, cudaStream_t st) {
     if (int rc = make_map_f32_seq(&ty16, a->y, a->batch, a->seq_len, 128, 16)) return rc;
     if (int rc = set_smem(reinterpret_cast<const void*>(k_block_rows), smem)) return rc;
     if (int rc = check_block_fits(reinterpret_cast<const void*>(k_block_rows), SmallCfg::THREADS)) return rc;
-    k_block_rows<<<2 * a->batch, SmallCfg::THREADS, smem, st>>>(tq, to, ti, tout, tx, ty16, p);
+    launch_kernel(k_block_rows, dim3(2 * a->batch), dim3(SmallCfg::THREADS), smem, st, tq, to, ti, tout, tx, ty16,
+                  p);
     return launch_status();
   }
   if (int rc = set_smem(reinterpret_cast<const void*>(k_block_small), smem)) return rc;
   if (int rc = check_block_fits(reinterpret_cast<const void*>(k_block_small), SmallCfg::THREADS)) return rc;
   const int grid = a->batch < num_sms() ? a->batch : num_sms();
-  k_block_small<<<grid, SmallCfg::THREADS, smem, st>>>(tq, to, ti, tout, tx, ty, p);
+  launch_kernel(k_block_small, dim3(grid), dim3(SmallCfg::THREADS), smem, st, tq, to, ti, tout, tx, ty, p);
   return launch_status();
 }
 
@@ -946,8 +978,8 @@ int b200_zero_masked_rows(float* y, const unsigned char* row_valid, long long ro
   if (!y || !row_valid || rows < 0 || d <= 0) return B200_ERR_ARG;
   if (rows == 0) return B200_OK;
   if (int rc = check_arch()) return rc;
-  k_zero_masked_rows<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      y, row_valid, rows, d);
+  launch_kernel(k_zero_masked_rows, dim3(static_cast<unsigned>((rows + 7) / 8)), dim3(256), 0,
+                static_cast<cudaStream_t>(stream), y, row_valid, rows, d);
   return launch_status();
 }
 

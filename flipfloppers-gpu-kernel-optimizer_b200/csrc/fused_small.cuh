@@ -198,6 +198,7 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  griddep_sync();  // the previous kernel's outputs are complete from here on
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer

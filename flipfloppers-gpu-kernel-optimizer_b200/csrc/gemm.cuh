@@ -281,6 +281,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  griddep_sync();  // the previous kernel's outputs are complete from here on
 
   if (warp == 0) {
     if (lane == 0) {

@@ -144,6 +144,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
   cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  griddep_sync();  // the previous kernel's outputs are complete from here on
 
   if (warp == 0) {
     if (lane == 0) {

@@ -25,6 +25,7 @@ __global__ void __launch_bounds__(256)
     k_layernorm(const float* __restrict__ x, int64_t ld_x, const float* __restrict__ gamma,
                 const float* __restrict__ beta, void* __restrict__ out, int64_t ld_out, int rows, int d, float eps,
                 float* __restrict__ copy_out, int64_t ld_copy) {
+  griddep_sync();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + warp;
   if (row >= rows) return;
@@ -95,6 +96,7 @@ __global__ void __launch_bounds__(256)
     k_add_layernorm(const float* a, const float* __restrict__ b, const float* __restrict__ bias,
                     float* sum_out, const float* __restrict__ gamma, const float* __restrict__ beta,
                     void* __restrict__ out, int rows, int d, float eps) {
+  griddep_sync();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + warp;
   if (row >= rows) return;
@@ -141,6 +143,7 @@ __global__ void __launch_bounds__(256)
 // query rows of the model output, TTB:190-191).  One warp per row.
 __global__ void __launch_bounds__(256)
     k_zero_masked_rows(float* __restrict__ y, const unsigned char* __restrict__ valid, long long rows, int d) {
+  griddep_sync();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long row = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + warp;
   if (row >= rows || valid[row]) return;

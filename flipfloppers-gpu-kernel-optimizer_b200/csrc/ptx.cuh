@@ -145,6 +145,19 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// Every kernel of the library is launched with programmatic stream
+// serialization: it may start (barrier init, TMEM allocation, descriptor
+// prefetch) while the previous kernel of the stream finishes.  griddep_sync()
+// waits until that kernel has completed and its writes are visible, then lets
+// the next kernel start its own prologue; it must precede every global read or
+// write of data another kernel produces or consumes.  No-op without a
+// programmatic dependency.
+__device__ __forceinline__ void griddep_sync() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- TMA (no multicast anywhere)
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
