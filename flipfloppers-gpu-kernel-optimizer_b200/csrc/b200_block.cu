@@ -22,6 +22,7 @@
 #include "attn2.cuh"
 #include "attn_small.cuh"
 #include "fused_small.cuh"
+#include "fused_tiny.cuh"
 
 using namespace b200;
 
@@ -610,12 +611,63 @@ int small_rows_mode() {
   return mode;
 }
 
+// d_model = 32: the CUDA-core kernel of fused_tiny.cuh (head_dim 8 / 16 / 32)
+int fused_tiny_impl(const B200FusedSmallArgs* a, cudaStream_t st) {
+  const int H = a->num_heads;
+  if (H != 1 && H != 2 && H != 4) return B200_ERR_CONFIG;
+  if (a->ffn_dim <= 0 || a->ffn_dim % 32 || a->ffn_dim > TinyCfg::FMAX || a->seq_len > TinyCfg::S)
+    return B200_ERR_CONFIG;
+  if (a->batch > 0x7fffffff / TinyCfg::S) return B200_ERR_TILE;
+  TinyParams p{};
+  p.num_seq = a->batch;
+  p.seq_len = a->seq_len;
+  p.layers = a->num_layers;
+  p.heads = H;
+  p.ffn = a->ffn_dim;
+  p.x = a->x;
+  p.y = a->y;
+  p.ln1_w = a->ln1_w;
+  p.ln1_b = a->ln1_b;
+  p.w_qkv = static_cast<const __half*>(a->w_qkv);
+  p.b_qkv = a->b_qkv;
+  p.w_o = static_cast<const __half*>(a->w_o);
+  p.b_o = a->b_o;
+  p.ln2_w = a->ln2_w;
+  p.ln2_b = a->ln2_b;
+  p.w_in = static_cast<const __half*>(a->w_in);
+  p.b_in = a->b_in;
+  p.w_out = static_cast<const __half*>(a->w_out);
+  p.b_out = a->b_out;
+  p.lnf_w = a->lnf_w;
+  p.lnf_b = a->lnf_b;
+  p.eps = a->eps;
+  p.scale_log2 = static_cast<float>(1.4426950408889634 / __builtin_sqrt(static_cast<double>(32 / H)));
+  p.row_valid = static_cast<const unsigned char*>(a->row_valid);
+  p.non_causal = a->non_causal;
+  const int smem = TinyCfg::TOTAL;
+  auto launch = [&](auto kern) {
+    if (int rc = set_smem(reinterpret_cast<const void*>(kern), smem)) return rc;
+    launch_kernel(kern, dim3(a->batch), dim3(TinyCfg::THREADS), smem, st, p);
+    return launch_status();
+  };
+  if (H == 4) return launch(k_block_tiny<8>);
+  if (H == 2) return launch(k_block_tiny<16>);
+  return launch(k_block_tiny<32>);
+}
+
 int fused_small_impl(const B200FusedSmallArgs* a, cudaStream_t st) {
   if (!a || !a->x || !a->y || !a->w_qkv || !a->w_o || !a->w_in || !a->w_out) return B200_ERR_ARG;
   if (!a->ln1_w || !a->ln1_b || !a->ln2_w || !a->ln2_b || !a->lnf_w || !a->lnf_b || !a->b_qkv || !a->b_o ||
       !a->b_in || !a->b_out)
     return B200_ERR_ARG;
   if (a->batch <= 0 || a->seq_len <= 0 || a->num_layers <= 0) return B200_ERR_ARG;
+  if (a->d_model == 32) {
+    if (a->x == a->y) return B200_ERR_ARG;
+    if (!al16(a->x) || !al16(a->y) || !al16(a->w_qkv) || !al16(a->w_o) || !al16(a->w_in) || !al16(a->w_out))
+      return B200_ERR_ALIGN;
+    if (int rc = check_arch()) return rc;
+    return fused_tiny_impl(a, st);
+  }
   if (a->d_model != 128 || a->num_heads != 4 || a->ffn_dim <= 0 || a->ffn_dim % 128 || a->ffn_dim > 512 ||
       a->seq_len > 128)
     return B200_ERR_CONFIG;

@@ -15,6 +15,9 @@ library's equivalents:
 * ``b200::linear_residual(a, w, bias, resid)`` -- functional ``resid + a.w^T + bias``;
 * ``b200::linear_residual_layernorm(a, w, bias, resid, gamma, beta, eps)`` --
   ``x1 = resid + a.w^T + bias`` and its LayerNorm (fp16) from one kernel (N = 128);
+* ``b200::kv_write(a, w_kv, b_kv, kv_cache, row0)`` -- the chunked forward's
+  K/V cache update fused into the projection: the K|V projection of a chunk's
+  normalised rows written in place into cache rows ``[row0, row0 + rows)``;
 * ``b200::layernorm(x, gamma, beta, eps, out_f16)``;
 * ``b200::flash_causal(q, k, v, heads, q_offset, non_causal, kv_lens)`` on
   ``[B, S, H*hd]`` fp16 tensors (prefix-causal when ``q_offset > 0``: query i
@@ -100,6 +103,35 @@ def linear_residual_layernorm(a: Tensor, w: Tensor, bias: Optional[Tensor], resi
 def _linear_residual_layernorm_fake(a, w, bias, resid, gamma, beta, eps):
     shape = (a.shape[0], w.shape[0])
     return resid.new_empty(shape, dtype=torch.float32), resid.new_empty(shape, dtype=torch.float16)
+
+
+# ------------------------------------------------------------------ K/V cache
+def _check_kv_write(a: Tensor, w_kv: Tensor, kv_cache: Tensor, row0: int) -> None:
+    if kv_cache.dim() != 2 or kv_cache.dtype != torch.float16 or kv_cache.shape[1] != w_kv.shape[0]:
+        raise ValueError("b200::kv_write: kv_cache must be fp16 [tokens, n] with n = w_kv.shape[0] (K | V columns)")
+    if a.dim() != 2 or a.shape[1] != w_kv.shape[1]:
+        raise ValueError("b200::kv_write: a must be [rows, d] with d = w_kv.shape[1]")
+    if row0 < 0 or row0 + a.shape[0] > kv_cache.shape[0]:
+        raise ValueError(f"b200::kv_write: rows [{row0}, {row0 + a.shape[0]}) outside the cache's {kv_cache.shape[0]}")
+
+
+@torch.library.custom_op("b200::kv_write", mutates_args=("kv_cache",), device_types="cuda")
+def kv_write(a: Tensor, w_kv: Tensor, b_kv: Optional[Tensor], kv_cache: Tensor, row0: int) -> None:
+    """kv_cache[row0 + i] = a[i] . w_kv^T + b_kv (fp16), for the rows of one query chunk.
+
+    The reference's chunked forward projects each chunk's K and V and stores them
+    into a preallocated fp16 cache that later chunks attend over (TTB:1463-1500);
+    here the projection's epilogue writes the cache rows directly, as the
+    library's own chunked forward does."""
+    _check_kv_write(a, w_kv, kv_cache, row0)
+    rows = a.shape[0]
+    rt.gemm(EPI_BIAS_F16, a, w_kv, b_kv, kv_cache[row0:row0 + rows])
+
+
+@kv_write.register_fake
+def _kv_write_fake(a, w_kv, b_kv, kv_cache, row0) -> None:
+    _check_kv_write(a, w_kv, kv_cache, row0)
+    return None
 
 
 # ------------------------------------------------------------------ LayerNorm

@@ -211,9 +211,12 @@ size_t b200_block_chunked_workspace_bytes(long long tokens, int chunk_rows, int 
 int b200_block_forward_chunked(const B200BlockArgs* args, int chunk_rows, b200_stream_t stream);
 
 /* Whole causal model (num_layers pre-LN blocks + final LayerNorm) in ONE
- * persistent kernel, for small models: d_model == 128, num_heads == 4,
- * ffn_dim a multiple of 128 up to 512, seq_len <= 128.  Every intermediate
- * stays on chip (TMEM / shared memory); per layer the weights are stacked
+ * kernel, for small models: d_model == 128, num_heads == 4, ffn_dim a
+ * multiple of 128 up to 512, seq_len <= 128 (tensor-core kernels: one
+ * persistent CTA per sequence, or two CTAs per sequence for one layer and few
+ * sequences), or d_model == 32, num_heads 1, 2 or 4, ffn_dim a multiple of 32
+ * up to 128, seq_len <= 128 (a CUDA-core kernel, one CTA per sequence).  Every
+ * intermediate stays on chip (TMEM / shared memory); per layer the weights are stacked
  * along rows: w_qkv [L*3d, d], w_o [L*d, d], w_in [L*ffn, d], w_out [L*d, ffn]
  * (fp16), biases / LayerNorm parameters [L, n] (fp32).  y must not alias x (y
  * carries the residual between layers).  Other shapes return B200_ERR_CONFIG. */

@@ -137,3 +137,34 @@ print("OK")
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     r = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0 and "OK" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+TINY_CASES = [  # B, S, H, ffn, L, causal, padding ratio
+    (64, 128, 4, 32, 4, True, 0.0),   # the reference's official matrix row 7
+    (3, 100, 2, 64, 2, True, 0.0),
+    (5, 128, 1, 128, 1, True, 0.25),
+    (4, 77, 4, 96, 3, False, 0.3),
+    (200, 128, 4, 32, 1, True, 0.0),
+]
+
+
+@pytest.mark.parametrize("B,S,H,F,L,causal,pad", TINY_CASES,
+                         ids=[f"B{c[0]}_S{c[1]}_H{c[2]}_F{c[3]}_L{c[4]}_{'c' if c[5] else 'nc'}" for c in TINY_CASES])
+def test_tiny_model_single_kernel_vs_oracle(tt, B, S, H, F, L, causal, pad):
+    """d_model = 32 runs as one CUDA-core kernel (fused_tiny.cuh) for the whole model."""
+    cfg = tt.TransformerConfig(B, S, 32, H, F, L, causal)
+    torch.manual_seed(B + H + F + L)
+    model = tt.UserOptimizedTransformer(cfg).to(DEV).eval()
+    x, mask = oracle.generate_random_case(B, S, 32, B * 3 + S, padding_ratio=pad)
+    m = mask if pad > 0 else None
+    with torch.inference_mode():
+        y = model(x.to(DEV), None if m is None else m.to(DEV)).cpu()
+    assert model.last_strategy == "fused_small"
+    assert tt._pkg.runtime.device_error(clear=True) == 0
+    nb = min(B, 16)
+    ref = oracle.model_forward(oracle.params_from_state_dict(model.state_dict()),
+                               oracle.OracleConfig(nb, S, 32, H, F, L, causal), x[:nb].numpy(),
+                               None if m is None else m[:nb].numpy())
+    res = oracle.compare_outputs(ref, y[:nb], rtol=RTOL, atol=ATOL)
+    print(f"tiny B{B} S{S} H{H} F{F} L{L}: max_abs={res.max_abs_error:.3g}")
+    assert res.passed, res

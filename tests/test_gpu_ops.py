@@ -109,3 +109,21 @@ def test_block_megakernel_op_matches_model(ops, pkg):
                                                st["w_out"], st["b_out"], m._lnf[0], m._lnf[1], 4, 1e-5, True, None)
     torch.cuda.synchronize()
     assert torch.equal(y_model, y_op)
+
+
+def test_kv_write_chunks_equal_full_projection(ops):
+    """K|V of three chunks written at their cache rows equal the whole projection;
+    rows outside the written range are untouched."""
+    g = torch.Generator().manual_seed(5)
+    d, S = 128, 700
+    a = _rand(g, S, d, dtype=torch.float16)
+    w = _rand(g, 2 * d, d, scale=1 / math.sqrt(d), dtype=torch.float16)
+    b = _rand(g, 2 * d)
+    cache = torch.full((S + 50, 2 * d), 7.0, dtype=torch.float16, device=DEV)
+    for r0, r1 in ((0, 256), (256, 512), (512, S)):
+        torch.ops.b200.kv_write(a[r0:r1], w, b, cache, r0)
+    torch.library.opcheck(torch.ops.b200.kv_write.default, (a[:64], w, b, cache.clone(), 10))
+    ref = a.float() @ w.float().T + b
+    torch.cuda.synchronize()
+    assert (cache[:S].float() - ref).abs().max().item() < 2e-3
+    assert bool((cache[S:] == 7.0).all())

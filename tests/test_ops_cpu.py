@@ -7,7 +7,7 @@ import torch
 
 
 def test_ops_registered(pkg):
-    for name in ("gemm_out", "linear", "linear_residual", "linear_residual_layernorm", "layernorm",
+    for name in ("gemm_out", "linear", "linear_residual", "linear_residual_layernorm", "kv_write", "layernorm",
                  "flash_causal", "block_megakernel"):
         assert hasattr(torch.ops.b200, name), name
 
@@ -28,6 +28,19 @@ def test_fake_shapes(pkg):
         q = torch.empty(2, 96, 256, dtype=torch.float16, device="cuda")
         o = torch.ops.b200.flash_causal(q, q, q, 4, 0, False, None)
         assert o.shape == (2, 96, 256) and o.dtype == torch.float16
+
+
+def test_kv_write_fake_checks_the_cache_rows(pkg):
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    with FakeTensorMode():
+        a = torch.empty(64, 128, dtype=torch.float16, device="cuda")
+        w = torch.empty(256, 128, dtype=torch.float16, device="cuda")
+        cache = torch.empty(1000, 256, dtype=torch.float16, device="cuda")
+        assert torch.ops.b200.kv_write(a, w, None, cache, 936) is None
+        with pytest.raises(ValueError):
+            torch.ops.b200.kv_write(a, w, None, cache, 937)  # past the end of the cache
+        with pytest.raises(ValueError):
+            torch.ops.b200.kv_write(a, w, None, cache[:, :128], 0)  # columns do not match w_kv
 
 
 def test_residual_epilogue_rejected_by_functional_linear(pkg):
