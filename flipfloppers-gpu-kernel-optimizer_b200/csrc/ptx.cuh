@@ -470,23 +470,24 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-// gelu_as on two values: the same operations, with the squarings, the 0.5*v
-// scaling and the final FMA done as f32x2 pairs (Horner stays scalar so its
-// coefficients remain immediates).
+// gelu_as on two values: the same operations with every multiply-add of the
+// Horner chain, the squarings, the 0.5*v scaling and the final FMA done as
+// f32x2 pairs (each lane of fma.rn.f32x2 rounds exactly like fmaf, so the
+// results are bit-identical to gelu_as); the coefficient pairs are loop
+// invariant in the callers' unrolled loops and stay in registers.
 __device__ __forceinline__ void gelu_as2(float& v0, float& v1) {
-  float q0 = 4.30638e-5f, q1 = 4.30638e-5f;
-  const float u0 = fabsf(v0) * 0.70710678118654752440f, u1 = fabsf(v1) * 0.70710678118654752440f;
-  q0 = fmaf(q0, u0, 2.765672e-4f);  q1 = fmaf(q1, u1, 2.765672e-4f);
-  q0 = fmaf(q0, u0, 1.520143e-4f);  q1 = fmaf(q1, u1, 1.520143e-4f);
-  q0 = fmaf(q0, u0, 9.2705272e-3f); q1 = fmaf(q1, u1, 9.2705272e-3f);
-  q0 = fmaf(q0, u0, 4.22820123e-2f); q1 = fmaf(q1, u1, 4.22820123e-2f);
-  q0 = fmaf(q0, u0, 7.05230784e-2f); q1 = fmaf(q1, u1, 7.05230784e-2f);
-  q0 = fmaf(q0, u0, 1.0f);          q1 = fmaf(q1, u1, 1.0f);
-  uint64_t q = f2pk(q0, q1);
+  const uint64_t u = f2pk(fabsf(v0) * 0.70710678118654752440f, fabsf(v1) * 0.70710678118654752440f);
+  uint64_t q = f2fma(f2pk(4.30638e-5f, 4.30638e-5f), u, f2pk(2.765672e-4f, 2.765672e-4f));
+  q = f2fma(q, u, f2pk(1.520143e-4f, 1.520143e-4f));
+  q = f2fma(q, u, f2pk(9.2705272e-3f, 9.2705272e-3f));
+  q = f2fma(q, u, f2pk(4.22820123e-2f, 4.22820123e-2f));
+  q = f2fma(q, u, f2pk(7.05230784e-2f, 7.05230784e-2f));
+  q = f2fma(q, u, f2pk(1.0f, 1.0f));
   q = f2mul(q, q);
   q = f2mul(q, q);
   q = f2mul(q, q);
   q = f2mul(q, q);  // (1 + a1 u + ... )^16 per lane
+  float q0, q1;
   f2upk(q, q0, q1);
   const float e0 = copysignf(1.0f - fast_rcp(q0), v0), e1 = copysignf(1.0f - fast_rcp(q1), v1);
   const uint64_t hv = f2mul(f2pk(v0, v1), f2pk(0.5f, 0.5f));
