@@ -735,14 +735,19 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
         named_bar(bar_id, 128);
         return buf[ks] + buf[128 + ks] + buf[256 + ks] + buf[384 + ks];
       };
-      auto own_max = [&](float part, float* buf) {
-        part = fmaxf(part, __shfl_xor_sync(0xffffffffu, part, 16));
-        buf[g * 128 + ks] = part;
+      // the head's max (lane j's slot) and the previous head's row sum (lane j+16's
+      // otherwise unused slot) in one reduction
+      auto own_max_sum = [&](float pmax, float psum, float* buf, float& m, float& l) {
+        pmax = fmaxf(pmax, __shfl_xor_sync(0xffffffffu, pmax, 16));
+        psum += __shfl_xor_sync(0xffffffffu, psum, 16);
+        buf[g * 128 + r] = hh ? psum : pmax;
         named_bar(bar_id, 128);
-        return fmaxf(fmaxf(buf[ks], buf[128 + ks]), fmaxf(buf[256 + ks], buf[384 + ks]));
+        m = fmaxf(fmaxf(buf[ks], buf[128 + ks]), fmaxf(buf[256 + ks], buf[384 + ks]));
+        l = buf[ks + 16] + buf[144 + ks] + buf[272 + ks] + buf[400 + ks];
       };
-      // LayerNorm of u (columns cc.. of an own row) in place, two-pass statistics
-      auto layer_norm16 = [&](const float* gamma, const float* beta) {
+      // LayerNorm of u (columns cc.. of an own row) in place, two-pass statistics (the mean
+      // reduced in bm, the variance in bv: consecutive reductions use different buffers)
+      auto layer_norm16 = [&](const float* gamma, const float* beta, float* bm, float* bv) {
         uint64_t a0 = f2pk(0.f, 0.f), a1 = a0;
 #pragma unroll
         for (int i = 0; i < 16; i += 4) {
@@ -752,7 +757,7 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
         float t0, t1, t2, t3;
         f2upk(a0, t0, t1);
         f2upk(a1, t2, t3);
-        const float mean = own_sum((t0 + t2) + (t1 + t3), st0) * (1.f / 128.f);
+        const float mean = own_sum((t0 + t2) + (t1 + t3), bm) * (1.f / 128.f);
         const uint64_t nm = f2pk(-mean, -mean);
         a0 = f2pk(0.f, 0.f);
         a1 = a0;
@@ -766,7 +771,7 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
         }
         f2upk(a0, t0, t1);
         f2upk(a1, t2, t3);
-        const float rstd = rsqrtf(own_sum((t0 + t2) + (t1 + t3), st1) * (1.f / 128.f) + p.eps);
+        const float rstd = rsqrtf(own_sum((t0 + t2) + (t1 + t3), bv) * (1.f / 128.f) + p.eps);
         const uint64_t rs = f2pk(rstd, rstd);
 #pragma unroll
         for (int i = 0; i < 16; i += 4) {
@@ -840,6 +845,7 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
       }
       if (!p.non_causal) kvalid &= (srow >= cc + 15) ? 0xffffu : (srow < cc ? 0u : (0xffffu >> (15 - (srow - cc))));
       float my_l = 1.f;  // softmax denominator of head g
+      float prev_sum = 0.f;  // the previous head's partial row sum, reduced with this head's max
 #pragma unroll 1
       for (int h = 0; h < 4; ++h) {
         wait_w(SB_S_FULL + (h & 1), par(0, 2, h >> 1));
@@ -853,7 +859,10 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
         float mx = -INFINITY;
 #pragma unroll
         for (int i = 0; i < 16; i += 2) mx = fmax3(mx, u[i], u[i + 1]);
-        const float m = own_max(mx, st0) * p.scale_log2;  // reductions alternate st0/st1 strictly
+        float m, lprev;
+        own_max_sum(mx, prev_sum, (h & 1) ? st1 : st0, m, lprev);  // reductions alternate st0/st1 strictly
+        if (h > 0 && h - 1 == g) my_l = lprev;
+        m *= p.scale_log2;
         const uint64_t sc = f2pk(p.scale_log2, p.scale_log2), nm = f2pk(-m, -m);
         uint64_t a0 = f2pk(0.f, 0.f), a1 = a0;
 #pragma unroll
@@ -872,8 +881,11 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
         if (h > 0) wait_w(SB_PV_DONE, par(0, 4, h - 1));  // P of the previous head consumed
         store16_sw128(smem + C::OFF_P);
         publish(SB_P_FULL);
-        const float lh = own_sum(sum, st1);
-        if (h == g) my_l = lh;
+        prev_sum = sum;
+      }
+      {
+        const float l3 = own_sum(prev_sum, st0);  // head 3 (after st1 above)
+        if (g == 3) my_l = l3;
       }
       // ---- W4: context (16 columns of head g) = O / l -> XA
       wait_w(SB_PV_DONE, par(0, 4, 3));
@@ -893,7 +905,7 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
       if (ok) tmem_ld32(trow + 384 + c0, v);
       take_half();
       add16(vec + C::V_BO + cc);
-      layer_norm16(vec + C::V_LN2W, vec + C::V_LN2B);
+      layer_norm16(vec + C::V_LN2W, vec + C::V_LN2B, st1, st0);  // after st0 (the last softmax sum)
       store16_sw128(xa);
       publish(SB_N2);
       // ---- W6: GELU chunks -> H ping-pong
@@ -916,7 +928,7 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
       take_half();
       add16(vec + C::V_BO + cc);
       add16(vec + C::V_BOUT + cc);
-      layer_norm16(vec + C::V_LNFW, vec + C::V_LNFB);
+      layer_norm16(vec + C::V_LNFW, vec + C::V_LNFB, st1, st0);
       {
         const bool zero = srow < p.seq_len && p.row_valid != nullptr && p.row_valid[srow_g] == 0;
         // the warp's own rows are 16 consecutive sequence rows: one 16x32 box, staged SW128

@@ -103,13 +103,14 @@ __device__ __forceinline__ void tiny_layer_norm8(float (&v)[8], const float* gam
 __device__ __forceinline__ int tiny_row(int row, int ld) { return row * ld + (row >> 3) * 4; }
 
 // out[c] = bias[c] + a . W[row0 + c] for c in [0, N): W row-major [.][32] fp32 in shared
-// memory (padded layout).  Four outputs at a time (independent FMA chains).
+// memory (padded layout), a as 16 packed pairs.  Four outputs at a time, each
+// accumulating its even and odd products as one f32x2 pair (independent chains).
 template <int N>
-__device__ __forceinline__ void tiny_matvec32(const float (&a)[32], const float* W, int row0, const float* bias,
+__device__ __forceinline__ void tiny_matvec32(const uint64_t (&a)[16], const float* W, int row0, const float* bias,
                                               float (&out)[N]) {
 #pragma unroll
   for (int c = 0; c < N; c += 4) {
-    float acc0 = bias[c], acc1 = bias[c + 1], acc2 = bias[c + 2], acc3 = bias[c + 3];
+    uint64_t acc0 = 0, acc1 = 0, acc2 = 0, acc3 = 0;  // (0.f, 0.f)
     const float* W0 = W + tiny_row(row0 + c, 32);
     const float* W1 = W + tiny_row(row0 + c + 1, 32);
     const float* W2 = W + tiny_row(row0 + c + 2, 32);
@@ -120,26 +121,31 @@ __device__ __forceinline__ void tiny_matvec32(const float (&a)[32], const float*
       const float4 w1 = *reinterpret_cast<const float4*>(W1 + k);
       const float4 w2 = *reinterpret_cast<const float4*>(W2 + k);
       const float4 w3 = *reinterpret_cast<const float4*>(W3 + k);
-      acc0 = fmaf(a[k], w0.x, fmaf(a[k + 1], w0.y, fmaf(a[k + 2], w0.z, fmaf(a[k + 3], w0.w, acc0))));
-      acc1 = fmaf(a[k], w1.x, fmaf(a[k + 1], w1.y, fmaf(a[k + 2], w1.z, fmaf(a[k + 3], w1.w, acc1))));
-      acc2 = fmaf(a[k], w2.x, fmaf(a[k + 1], w2.y, fmaf(a[k + 2], w2.z, fmaf(a[k + 3], w2.w, acc2))));
-      acc3 = fmaf(a[k], w3.x, fmaf(a[k + 1], w3.y, fmaf(a[k + 2], w3.z, fmaf(a[k + 3], w3.w, acc3))));
+      acc0 = f2fma(a[k / 2 + 1], f2pk(w0.z, w0.w), f2fma(a[k / 2], f2pk(w0.x, w0.y), acc0));
+      acc1 = f2fma(a[k / 2 + 1], f2pk(w1.z, w1.w), f2fma(a[k / 2], f2pk(w1.x, w1.y), acc1));
+      acc2 = f2fma(a[k / 2 + 1], f2pk(w2.z, w2.w), f2fma(a[k / 2], f2pk(w2.x, w2.y), acc2));
+      acc3 = f2fma(a[k / 2 + 1], f2pk(w3.z, w3.w), f2fma(a[k / 2], f2pk(w3.x, w3.y), acc3));
     }
-    out[c] = acc0;
-    out[c + 1] = acc1;
-    out[c + 2] = acc2;
-    out[c + 3] = acc3;
+    float e, o;
+    f2upk(acc0, e, o);
+    out[c] = bias[c] + (e + o);
+    f2upk(acc1, e, o);
+    out[c + 1] = bias[c + 1] + (e + o);
+    f2upk(acc2, e, o);
+    out[c + 2] = bias[c + 2] + (e + o);
+    f2upk(acc3, e, o);
+    out[c + 3] = bias[c + 3] + (e + o);
   }
 }
 
 // acc[o] += sum_k h[k] * W[row0 + o][col0 + k] for o in [0, N): a 32-column slice of a
-// row-major weight with row stride ld (padded layout)
+// row-major weight with row stride ld (padded layout), h as 16 packed pairs
 template <int N>
-__device__ __forceinline__ void tiny_matvec32_acc(const float (&h)[32], const float* W, int row0, int ld, int col0,
+__device__ __forceinline__ void tiny_matvec32_acc(const uint64_t (&h)[16], const float* W, int row0, int ld, int col0,
                                                   float (&acc)[N]) {
 #pragma unroll
   for (int o = 0; o < N; o += 4) {
-    float a0 = acc[o], a1 = acc[o + 1], a2 = acc[o + 2], a3 = acc[o + 3];
+    uint64_t a0 = 0, a1 = 0, a2 = 0, a3 = 0;
     const float* W0 = W + tiny_row(row0 + o, ld) + col0;
     const float* W1 = W + tiny_row(row0 + o + 1, ld) + col0;
     const float* W2 = W + tiny_row(row0 + o + 2, ld) + col0;
@@ -150,15 +156,20 @@ __device__ __forceinline__ void tiny_matvec32_acc(const float (&h)[32], const fl
       const float4 w1 = *reinterpret_cast<const float4*>(W1 + k);
       const float4 w2 = *reinterpret_cast<const float4*>(W2 + k);
       const float4 w3 = *reinterpret_cast<const float4*>(W3 + k);
-      a0 = fmaf(h[k], w0.x, fmaf(h[k + 1], w0.y, fmaf(h[k + 2], w0.z, fmaf(h[k + 3], w0.w, a0))));
-      a1 = fmaf(h[k], w1.x, fmaf(h[k + 1], w1.y, fmaf(h[k + 2], w1.z, fmaf(h[k + 3], w1.w, a1))));
-      a2 = fmaf(h[k], w2.x, fmaf(h[k + 1], w2.y, fmaf(h[k + 2], w2.z, fmaf(h[k + 3], w2.w, a2))));
-      a3 = fmaf(h[k], w3.x, fmaf(h[k + 1], w3.y, fmaf(h[k + 2], w3.z, fmaf(h[k + 3], w3.w, a3))));
+      a0 = f2fma(h[k / 2 + 1], f2pk(w0.z, w0.w), f2fma(h[k / 2], f2pk(w0.x, w0.y), a0));
+      a1 = f2fma(h[k / 2 + 1], f2pk(w1.z, w1.w), f2fma(h[k / 2], f2pk(w1.x, w1.y), a1));
+      a2 = f2fma(h[k / 2 + 1], f2pk(w2.z, w2.w), f2fma(h[k / 2], f2pk(w2.x, w2.y), a2));
+      a3 = f2fma(h[k / 2 + 1], f2pk(w3.z, w3.w), f2fma(h[k / 2], f2pk(w3.x, w3.y), a3));
     }
-    acc[o] = a0;
-    acc[o + 1] = a1;
-    acc[o + 2] = a2;
-    acc[o + 3] = a3;
+    float e, od;
+    f2upk(a0, e, od);
+    acc[o] += e + od;
+    f2upk(a1, e, od);
+    acc[o + 1] += e + od;
+    f2upk(a2, e, od);
+    acc[o + 2] += e + od;
+    f2upk(a3, e, od);
+    acc[o + 3] += e + od;
   }
 }
 
@@ -188,11 +199,13 @@ __device__ __forceinline__ void st8(float* p, const float (&v)[8]) {
   *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
   *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
 }
-__device__ __forceinline__ void ld32(const float* p, float (&v)[32]) {
+// 32 consecutive floats at p (16-byte aligned) as 16 packed pairs
+__device__ __forceinline__ void ld32x2(const float* p, uint64_t (&v)[16]) {
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const float4 a = *reinterpret_cast<const float4*>(p + 4 * j);
-    v[4 * j] = a.x; v[4 * j + 1] = a.y; v[4 * j + 2] = a.z; v[4 * j + 3] = a.w;
+    v[2 * j] = f2pk(a.x, a.y);
+    v[2 * j + 1] = f2pk(a.z, a.w);
   }
 }
 
@@ -253,7 +266,7 @@ __global__ void __launch_bounds__(TinyCfg::THREADS, 1) k_block_tiny(const TinyPa
     __syncthreads();
 
     // LN1 -> the row buffer -> the whole row n; this quarter's K and V columns -> shared memory
-    float n[32];
+    uint64_t n[16];  // the row's LN output as packed pairs
     {
       float t8[8];
 #pragma unroll
@@ -261,7 +274,7 @@ __global__ void __launch_bounds__(TinyCfg::THREADS, 1) k_block_tiny(const TinyPa
       tiny_layer_norm8(t8, vec + C::V_LN1W + 8 * c, vec + C::V_LN1B + 8 * c, p.eps);
       st8(rowbuf + 8 * c, t8);
       __syncwarp();
-      ld32(rowbuf, n);
+      ld32x2(rowbuf, n);
       float kv[8];
       tiny_matvec32<8>(n, sm + C::W_QKV, 32 + 8 * c, vec + C::V_BQKV + 32 + 8 * c, kv);
       st8(sm + C::KS + r * C::LD + 8 * c, kv);
@@ -271,15 +284,20 @@ __global__ void __launch_bounds__(TinyCfg::THREADS, 1) k_block_tiny(const TinyPa
     __syncthreads();  // every row's K and V are in place
 
     // attention for (row r, head): this thread's keys are sub, sub + T, ...
-    float o[HD];
+    // (query and context accumulator as packed pairs: dot products and the P.V update
+    // run as f32x2 FMAs)
+    uint64_t o[HD / 2];
     float m = -INFINITY, lsum = 0.f;
     {
-      float q[HD];
-      tiny_matvec32<HD>(n, sm + C::W_QKV, head * HD, vec + C::V_BQKV + head * HD, q);
+      uint64_t q2[HD / 2];
+      {
+        float q[HD];
+        tiny_matvec32<HD>(n, sm + C::W_QKV, head * HD, vec + C::V_BQKV + head * HD, q);
 #pragma unroll
-      for (int e = 0; e < HD; ++e) {
-        q[e] *= p.scale_log2;  // scores in log2 units
-        o[e] = 0.f;
+        for (int e = 0; e < HD; e += 2) {
+          q2[e / 2] = f2pk(q[e] * p.scale_log2, q[e + 1] * p.scale_log2);  // scores in log2 units
+          o[e / 2] = 0;
+        }
       }
       for (int j0 = sub; j0 < kend; j0 += KB * T) {
         float s[KB];
@@ -294,12 +312,15 @@ __global__ void __launch_bounds__(TinyCfg::THREADS, 1) k_block_tiny(const TinyPa
           const bool valid = T == 1 ? ((kv_word >> jj) & 1u) != 0u : key_ok[j] != 0.f;
           if (j < kend && valid) {
             const float* kr = sm + C::KS + j * C::LD + head * HD;
-            acc = 0.f;
+            uint64_t a2 = 0;
 #pragma unroll
             for (int e = 0; e < HD; e += 4) {
               const float4 kk = *reinterpret_cast<const float4*>(kr + e);
-              acc = fmaf(q[e], kk.x, fmaf(q[e + 1], kk.y, fmaf(q[e + 2], kk.z, fmaf(q[e + 3], kk.w, acc))));
+              a2 = f2fma(q2[e / 2 + 1], f2pk(kk.z, kk.w), f2fma(q2[e / 2], f2pk(kk.x, kk.y), a2));
             }
+            float lo, hi;
+            f2upk(a2, lo, hi);
+            acc = lo + hi;
           }
           s[jj] = acc;
           mb = fmaxf(mb, acc);
@@ -308,22 +329,22 @@ __global__ void __launch_bounds__(TinyCfg::THREADS, 1) k_block_tiny(const TinyPa
         const float mn = fmaxf(m, mb);
         const float corr = fast_exp2(m - mn);  // 0 on the first visible block
         lsum *= corr;
+        const uint64_t corr2 = f2pk(corr, corr);
 #pragma unroll
-        for (int e = 0; e < HD; ++e) o[e] *= corr;
+        for (int e = 0; e < HD / 2; ++e) o[e] = f2mul(o[e], corr2);
         m = mn;
 #pragma unroll
         for (int jj = 0; jj < KB; ++jj) {
           if (s[jj] != -INFINITY) {  // masked keys are skipped, never weighted by zero
             const float pj = fast_exp2(s[jj] - m);
             lsum += pj;
+            const uint64_t p2 = f2pk(pj, pj);
             const float* vr = sm + C::VS + (j0 + jj * T) * C::LD + head * HD;
 #pragma unroll
             for (int e = 0; e < HD; e += 4) {
               const float4 vv = *reinterpret_cast<const float4*>(vr + e);
-              o[e] = fmaf(pj, vv.x, o[e]);
-              o[e + 1] = fmaf(pj, vv.y, o[e + 1]);
-              o[e + 2] = fmaf(pj, vv.z, o[e + 2]);
-              o[e + 3] = fmaf(pj, vv.w, o[e + 3]);
+              o[e / 2] = f2fma(p2, f2pk(vv.x, vv.y), o[e / 2]);
+              o[e / 2 + 1] = f2fma(p2, f2pk(vv.z, vv.w), o[e / 2 + 1]);
             }
           }
         }
@@ -337,23 +358,32 @@ __global__ void __launch_bounds__(TinyCfg::THREADS, 1) k_block_tiny(const TinyPa
       const float a = (m == -INFINITY) ? 0.f : fast_exp2(m - mm);
       const float b2 = (m2 == -INFINITY) ? 0.f : fast_exp2(m2 - mm);
       lsum = lsum * a + l2 * b2;
+      const uint64_t a_2 = f2pk(a, a), b_2 = f2pk(b2, b2);
 #pragma unroll
-      for (int e = 0; e < HD; ++e) o[e] = o[e] * a + __shfl_xor_sync(0xffffffffu, o[e], off) * b2;
+      for (int e = 0; e < HD / 2; ++e) {
+        const uint64_t other = __shfl_xor_sync(0xffffffffu, o[e], off);
+        o[e] = f2fma(o[e], a_2, f2mul(other, b_2));
+      }
       m = mm;
     }
     {
       const float inv = lsum > 0.f ? 1.f / lsum : 0.f;  // a row with no visible key (padding) gets 0
       __syncwarp();  // the quad has read n from the row buffer
       if (sub == 0) {
+        const uint64_t inv2 = f2pk(inv, inv);
 #pragma unroll
-        for (int e = 0; e < HD; ++e) rowbuf[head * HD + e] = o[e] * inv;
+        for (int e = 0; e < HD; e += 2) {
+          float lo, hi;
+          f2upk(f2mul(o[e / 2], inv2), lo, hi);
+          *reinterpret_cast<float2*>(rowbuf + head * HD + e) = make_float2(lo, hi);
+        }
       }
       __syncwarp();
     }
     // out_proj + residual (this quarter's 8 columns); LN2 -> the row buffer -> n
     {
-      float cx[32];
-      ld32(rowbuf, cx);
+      uint64_t cx[16];
+      ld32x2(rowbuf, cx);
       float t8[8];
       tiny_matvec32<8>(cx, sm + C::W_O, 8 * c, vec + C::V_BO + 8 * c, t8);
 #pragma unroll
@@ -365,7 +395,7 @@ __global__ void __launch_bounds__(TinyCfg::THREADS, 1) k_block_tiny(const TinyPa
       __syncwarp();  // the quad has read the context
       st8(rowbuf + 8 * c, t8);
       __syncwarp();
-      ld32(rowbuf, n);
+      ld32x2(rowbuf, n);
     }
     // FFN: this quarter's hidden units -> the row buffer; then its 8 output columns over all units
     __syncwarp();  // the quad has read n
@@ -382,8 +412,8 @@ __global__ void __launch_bounds__(TinyCfg::THREADS, 1) k_block_tiny(const TinyPa
       ld8(vec + C::V_BOUT + 8 * c, acc);
 #pragma unroll 1
       for (int k0 = 0; k0 < F; k0 += 32) {
-        float h32[32];
-        ld32(rowbuf + k0, h32);
+        uint64_t h32[16];
+        ld32x2(rowbuf + k0, h32);
         tiny_matvec32_acc<8>(h32, sm + C::W_OUT, 8 * c, F, k0, acc);
       }
 #pragma unroll
