@@ -661,10 +661,14 @@ int fused_small_impl(const B200FusedSmallArgs* a, cudaStream_t st) {
       !a->b_in || !a->b_out)
     return B200_ERR_ARG;
   if (a->batch <= 0 || a->seq_len <= 0 || a->num_layers <= 0) return B200_ERR_ARG;
+  // every per-layer vector arrives by bulk copy (16-byte aligned source)
+  const float* vecs[] = {a->ln1_w, a->ln1_b, a->ln2_w, a->ln2_b, a->lnf_w, a->lnf_b, a->b_qkv, a->b_o, a->b_in, a->b_out};
   if (a->d_model == 32) {
     if (a->x == a->y) return B200_ERR_ARG;
     if (!al16(a->x) || !al16(a->y) || !al16(a->w_qkv) || !al16(a->w_o) || !al16(a->w_in) || !al16(a->w_out))
       return B200_ERR_ALIGN;
+    for (const float* v : vecs)
+      if (!al16(v)) return B200_ERR_ALIGN;
     if (int rc = check_arch()) return rc;
     return fused_tiny_impl(a, st);
   }
@@ -674,7 +678,6 @@ int fused_small_impl(const B200FusedSmallArgs* a, cudaStream_t st) {
   if (a->x == a->y) return B200_ERR_ARG;
   if (!al16(a->x) || !al16(a->y) || !al16(a->w_qkv) || !al16(a->w_o) || !al16(a->w_in) || !al16(a->w_out))
     return B200_ERR_ALIGN;
-  const float* vecs[] = {a->ln1_w, a->ln1_b, a->ln2_w, a->ln2_b, a->lnf_w, a->lnf_b, a->b_qkv, a->b_o, a->b_in, a->b_out};
   for (const float* v : vecs)
     if (!al16(v)) return B200_ERR_ALIGN;
   if (static_cast<long long>(a->batch) * a->seq_len > 0x7fffffffLL) return B200_ERR_TILE;

@@ -83,8 +83,8 @@ struct SmallCfg {
   static constexpr int OFF_W = 163840;          // WST x 16 KB
   static constexpr int OFF_XIN = OFF_V;         // 64 KB layer input, aliases V and P
   static constexpr int OFF_YST = OFF_Q;         // 64 KB y staging, aliases Q and K
-  static constexpr int OFF_STATS = OFF_W + WST * BOX;   // float [2][4][128]
-  static constexpr int OFF_VEC = OFF_STATS + 2 * 4 * 128 * 4;  // per-layer vectors, fp32
+  static constexpr int OFF_STATS = OFF_W + WST * BOX;   // float [4][4][128]
+  static constexpr int OFF_VEC = OFF_STATS + 4 * 4 * 128 * 4;  // per-layer vectors, fp32
   // float offsets inside the vector block
   static constexpr int V_LN1W = 0, V_LN1B = 128, V_BQKV = 256, V_BO = 640, V_LN2W = 768, V_LN2B = 896,
                        V_BIN = 1024, V_BOUT = 1536, V_LNFW = 1664, V_LNFB = 1792, V_TOTAL = 1920;
@@ -439,6 +439,8 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
     const uint32_t trow = tmem + (static_cast<uint32_t>(q * 32) << 16);
     float* st0 = stats;                  // [4][128]
     float* st1 = stats + 512;
+    float* st2 = stats + 1024;           // second halves of the merged (max, sum) reductions
+    float* st3 = stats + 1536;
     float* vec = reinterpret_cast<float*>(smem + C::OFF_VEC);
     const int wtid = threadIdx.x - 64;   // 0..511 among the workers
     uint8_t* xa = smem + C::OFF_XA;
@@ -455,16 +457,21 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
       named_bar(bar_id, 128);
       return buf[r] + buf[128 + r] + buf[256 + r] + buf[384 + r];
     };
-    auto row_max = [&](float part, float* buf) {
-      buf[g * 128 + r] = part;
+    // a head's row max and the previous head's row sum behind one barrier
+    auto row_max_sum = [&](float pmax, float psum, float* bm, float* bs, float& m, float& l) {
+      bm[g * 128 + r] = pmax;
+      bs[g * 128 + r] = psum;
       named_bar(bar_id, 128);
-      return fmaxf(fmaxf(buf[r], buf[128 + r]), fmaxf(buf[256 + r], buf[384 + r]));
+      m = fmaxf(fmaxf(bm[r], bm[128 + r]), fmaxf(bm[256 + r], bm[384 + r]));
+      l = bs[r] + bs[128 + r] + bs[256 + r] + bs[384 + r];
     };
     // LayerNorm of v (32 columns of this row) in place, two-pass statistics
     // (f32x2 pairs throughout: the statistics use 2 pair accumulators each);
     // vec_parity >= 0: wait for that phase of the vector copies (SB_VFULL)
-    // only before gamma and beta are read
-    auto layer_norm = [&](const float* gamma, const float* beta, int vec_parity = -1) {  // gamma/beta: shared memory
+    // only before gamma and beta are read; bm / bv: the statistics buffers of the
+    // mean and the variance (default st0 / st1)
+    auto layer_norm = [&](const float* gamma, const float* beta, int vec_parity = -1, float* bm = nullptr,
+                          float* bv = nullptr) {  // gamma/beta: shared memory
       uint64_t a0 = f2pk(0.f, 0.f), a1 = a0;
 #pragma unroll
       for (int i = 0; i < 32; i += 4) {
@@ -474,7 +481,7 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
       float t0, t1, t2, t3;
       f2upk(a0, t0, t1);
       f2upk(a1, t2, t3);
-      const float mean = row_sum((t0 + t2) + (t1 + t3), st0) * (1.f / 128.f);
+      const float mean = row_sum((t0 + t2) + (t1 + t3), bm ? bm : st0) * (1.f / 128.f);
       const uint64_t nm = f2pk(-mean, -mean);
       a0 = f2pk(0.f, 0.f);
       a1 = a0;
@@ -488,7 +495,7 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
       }
       f2upk(a0, t0, t1);
       f2upk(a1, t2, t3);
-      const float rstd = rsqrtf(row_sum((t0 + t2) + (t1 + t3), st1) * (1.f / 128.f) + p.eps);
+      const float rstd = rsqrtf(row_sum((t0 + t2) + (t1 + t3), bv ? bv : st1) * (1.f / 128.f) + p.eps);
       const uint64_t rs = f2pk(rstd, rstd);
       if (vec_parity >= 0) wait_w(SB_VFULL, static_cast<uint32_t>(vec_parity));
 #pragma unroll
@@ -595,6 +602,7 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
         }
         if (!p.non_causal) kvalid &= (r >= c0 + 31) ? 0xffffffffu : (r < c0 ? 0u : (0xffffffffu >> (31 - (r - c0))));
         float my_l = 1.f;  // softmax denominator of head g (this thread's head in the context step)
+        float prev_sum = 0.f;  // this thread's partial row sum of the previous head
 #pragma unroll 1
         for (int h = 0; h < 4; ++h) {
           wait_w(SB_S_FULL + (h & 1), par(step, 2, h >> 1));
@@ -607,7 +615,11 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
           float mx = -INFINITY;
 #pragma unroll
           for (int i = 0; i < 32; i += 2) mx = fmax3(mx, v[i], v[i + 1]);
-          const float m = row_max(mx, st0) * p.scale_log2;  // reductions alternate st0/st1 strictly
+          // head h's max with head h-1's sum; the pairs alternate (st0, st2) / (st1, st3)
+          float m, lprev;
+          row_max_sum(mx, prev_sum, (h & 1) ? st1 : st0, (h & 1) ? st3 : st2, m, lprev);
+          if (h > 0 && h - 1 == g) my_l = lprev;
+          m *= p.scale_log2;
           const uint64_t sc = f2pk(p.scale_log2, p.scale_log2), nm = f2pk(-m, -m);
           uint64_t a0 = f2pk(0.f, 0.f), a1 = a0;
 #pragma unroll
@@ -622,13 +634,15 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
           float t0, t1, t2, t3;
           f2upk(a0, t0, t1);
           f2upk(a1, t2, t3);
-          const float sum = (t0 + t2) + (t1 + t3);
+          prev_sum = (t0 + t2) + (t1 + t3);
           // P of the previous head must have been consumed before P is overwritten
           if (h > 0) wait_w(SB_PV_DONE, par(step, 4, h - 1));
           store_sw128(smem + C::OFF_P);
           publish(SB_P_FULL);
-          const float lh = row_sum(sum, st1);
-          if (h == g) my_l = lh;
+        }
+        {
+          const float l3 = row_sum(prev_sum, st0);  // head 3's sum (after (st1, st3) above)
+          if (g == 3) my_l = l3;
         }
         // ---- W4: context = O_g / l_g -> XA (head g's 32 columns)
         wait_w(SB_PV_DONE, par(step, 4, 3));
@@ -646,7 +660,7 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
         if (ok) tmem_ld32(trow + 384 + c0, v);
         f2_add_bias32(v, vec + C::V_BO + c0);
         if (ok) tmem_st32(trow + 384 + c0, v);
-        layer_norm(vec + C::V_LN2W, vec + C::V_LN2B);
+        layer_norm(vec + C::V_LN2W, vec + C::V_LN2B, -1, st1, st0);  // after st0 (head 3's sum)
         store_sw128(xa);
         publish(SB_N2);
         // ---- W6: GELU chunks -> H ping-pong
@@ -668,7 +682,7 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
         if (ok) tmem_ld32(trow + 384 + c0, v);
         f2_add_bias32(v, vec + C::V_BOUT + c0);
         if (l == p.layers - 1) {
-          layer_norm(vec + C::V_LNFW, vec + C::V_LNFB);
+          layer_norm(vec + C::V_LNFW, vec + C::V_LNFB, -1, st1, st0);  // after st0 (LN2's variance)
           // padded rows of the model output are zero (with causal attention and prefix-valid
           // padding the valid rows never see a padded key, so only the output needs masking)
           const bool zero = row_ok && p.row_valid != nullptr && p.row_valid[grow] == 0;

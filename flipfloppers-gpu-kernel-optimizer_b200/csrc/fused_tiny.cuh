@@ -74,7 +74,16 @@ struct TinyCfg {
   static constexpr int VS = KS + S * LD;                // [S][LD]
   static constexpr int ROWS = VS + S * LD;              // [S][RL] exchange buffer (a row's n, context or hidden units)
   static constexpr int KOK = ROWS + S * RL;             // [S] 1: key exists and is not padding
-  static constexpr int TOTAL_FLOATS = KOK + S;
+  // the next layer's fp16 weights and fp32 vectors as they arrive by bulk copy
+  // (row-major, unpadded; the vectors in the VEC layout), converted into the
+  // regions above at the layer boundary
+  static constexpr int STG_QKV = KOK + S;               // [96][32] fp16
+  static constexpr int STG_O = STG_QKV + 3 * D * D / 2; // [32][32] fp16
+  static constexpr int STG_IN = STG_O + D * D / 2;      // [ffn][32] fp16
+  static constexpr int STG_OUT = STG_IN + FMAX * D / 2; // [32][ffn] fp16
+  static constexpr int STG_VEC = STG_OUT + D * FMAX / 2;
+  static constexpr int BAR = STG_VEC + V_TOTAL;         // mbarrier (8 bytes) + abort flag
+  static constexpr int TOTAL_FLOATS = BAR + 4;
   static constexpr int TOTAL = TOTAL_FLOATS * 4;
 };
 
@@ -173,11 +182,11 @@ __device__ __forceinline__ void tiny_matvec32_acc(const uint64_t (&h)[16], const
   }
 }
 
-// fp16 weight [rows][ld] -> fp32 shared memory in the padded layout (ld a multiple of 8),
-// all threads of the CTA
+// fp16 weight [rows][ld] (shared memory, as staged) -> fp32 shared memory in the
+// padded layout (ld a multiple of 8), all threads of the CTA
 __device__ __forceinline__ void tiny_stage_f16(float* dst, const __half* src, int rows, int ld) {
   for (int i = static_cast<int>(threadIdx.x) * 8; i < rows * ld; i += TinyCfg::THREADS * 8) {
-    const uint4 t = __ldg(reinterpret_cast<const uint4*>(src + i));
+    const uint4 t = *reinterpret_cast<const uint4*>(src + i);
     const __half2* h2 = reinterpret_cast<const __half2*>(&t);
     const float2 f0 = __half22float2(h2[0]), f1 = __half22float2(h2[1]), f2 = __half22float2(h2[2]),
                  f3 = __half22float2(h2[3]);
@@ -185,9 +194,6 @@ __device__ __forceinline__ void tiny_stage_f16(float* dst, const __half* src, in
     *reinterpret_cast<float4*>(d) = make_float4(f0.x, f0.y, f1.x, f1.y);
     *reinterpret_cast<float4*>(d + 4) = make_float4(f2.x, f2.y, f3.x, f3.y);
   }
-}
-__device__ __forceinline__ void tiny_stage_f32(float* dst, const float* src, int n) {
-  for (int i = static_cast<int>(threadIdx.x); i < n; i += TinyCfg::THREADS) dst[i] = __ldg(src + i);
 }
 
 // 8 consecutive floats at p (16-byte aligned) -> v / v -> p
@@ -230,6 +236,36 @@ __global__ void __launch_bounds__(TinyCfg::THREADS, 1) k_block_tiny(const TinyPa
   float* vec = sm + C::VEC;
   float* rowbuf = sm + C::ROWS + r * C::RL;
   const float* key_ok = sm + C::KOK;
+  uint64_t* wbar = reinterpret_cast<uint64_t*>(sm + C::BAR);  // a layer's staged weights and vectors
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + C::BAR + 2);
+  // one thread copies layer l's weights and vectors into the staging area (ten bulk
+  // copies, one mbarrier phase): issued a layer ahead, so the HBM / L2 round trip
+  // overlaps the previous layer's arithmetic instead of stalling every boundary
+  auto fetch = [&](int l) {
+    const uint32_t fb = 4u * static_cast<uint32_t>(F);  // bytes of b_in; w_in and w_out are 16 * fb each
+    fence_proxy_async_smem();  // the previous layer's reads of the staging area come first
+    mbar_arrive_expect_tx(wbar, 8192u + 1152u + 33u * fb);
+    bulk_load(sm + C::STG_QKV, p.w_qkv + static_cast<int64_t>(l) * 96 * 32, 6144, wbar);
+    bulk_load(sm + C::STG_O, p.w_o + static_cast<int64_t>(l) * 32 * 32, 2048, wbar);
+    bulk_load(sm + C::STG_IN, p.w_in + static_cast<int64_t>(l) * F * 32, 16u * fb, wbar);
+    bulk_load(sm + C::STG_OUT, p.w_out + static_cast<int64_t>(l) * 32 * F, 16u * fb, wbar);
+    float* sv = sm + C::STG_VEC;
+    bulk_load(sv + C::V_LN1W, p.ln1_w + l * 32, 128, wbar);
+    bulk_load(sv + C::V_LN1B, p.ln1_b + l * 32, 128, wbar);
+    bulk_load(sv + C::V_BQKV, p.b_qkv + l * 96, 384, wbar);
+    bulk_load(sv + C::V_BO, p.b_o + l * 32, 128, wbar);
+    bulk_load(sv + C::V_LN2W, p.ln2_w + l * 32, 128, wbar);
+    bulk_load(sv + C::V_LN2B, p.ln2_b + l * 32, 128, wbar);
+    bulk_load(sv + C::V_BIN, p.b_in + static_cast<int64_t>(l) * F, fb, wbar);
+    bulk_load(sv + C::V_BOUT, p.b_out + l * 32, 128, wbar);
+  };
+  if (threadIdx.x == 0) {
+    mbar_init(wbar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) fetch(0);
   if (c == 0) sm[C::KOK + r] = (row_ok && (p.row_valid == nullptr || p.row_valid[grow] != 0)) ? 1.f : 0.f;
   const int kend = p.non_causal ? p.seq_len : min(r + 1, p.seq_len);  // keys 0..kend-1 may be visible
   // key validity as four 32-bit words in registers (lane i tests key 32w + i)
@@ -251,19 +287,19 @@ __global__ void __launch_bounds__(TinyCfg::THREADS, 1) k_block_tiny(const TinyPa
 
   for (int l = 0; l < p.layers; ++l) {
     __syncthreads();  // the previous layer's weights and K / V are no longer read
-    tiny_stage_f16(sm + C::W_QKV, p.w_qkv + static_cast<int64_t>(l) * 96 * 32, 96, 32);
-    tiny_stage_f16(sm + C::W_O, p.w_o + static_cast<int64_t>(l) * 32 * 32, 32, 32);
-    tiny_stage_f16(sm + C::W_IN, p.w_in + static_cast<int64_t>(l) * F * 32, F, 32);
-    tiny_stage_f16(sm + C::W_OUT, p.w_out + static_cast<int64_t>(l) * 32 * F, 32, F);
-    tiny_stage_f32(vec + C::V_LN1W, p.ln1_w + l * 32, 32);
-    tiny_stage_f32(vec + C::V_LN1B, p.ln1_b + l * 32, 32);
-    tiny_stage_f32(vec + C::V_BQKV, p.b_qkv + l * 96, 96);
-    tiny_stage_f32(vec + C::V_BO, p.b_o + l * 32, 32);
-    tiny_stage_f32(vec + C::V_LN2W, p.ln2_w + l * 32, 32);
-    tiny_stage_f32(vec + C::V_LN2B, p.ln2_b + l * 32, 32);
-    tiny_stage_f32(vec + C::V_BIN, p.b_in + static_cast<int64_t>(l) * F, F);
-    tiny_stage_f32(vec + C::V_BOUT, p.b_out + l * 32, 32);
-    __syncthreads();
+    // layer l's staged copies -> fp32 weights (padded layout) and vectors
+    const bool got = mbar_wait(wbar, static_cast<uint32_t>(l & 1), abort_flag, DERR_WAIT_TMA);
+    if (got) {
+      tiny_stage_f16(sm + C::W_QKV, reinterpret_cast<const __half*>(sm + C::STG_QKV), 96, 32);
+      tiny_stage_f16(sm + C::W_O, reinterpret_cast<const __half*>(sm + C::STG_O), 32, 32);
+      tiny_stage_f16(sm + C::W_IN, reinterpret_cast<const __half*>(sm + C::STG_IN), F, 32);
+      tiny_stage_f16(sm + C::W_OUT, reinterpret_cast<const __half*>(sm + C::STG_OUT), 32, F);
+      if (threadIdx.x < C::V_TOTAL / 4)
+        reinterpret_cast<float4*>(vec)[threadIdx.x] = reinterpret_cast<const float4*>(sm + C::STG_VEC)[threadIdx.x];
+    }
+    // a copy that never landed (bounded wait, error recorded) ends the whole CTA here
+    if (__syncthreads_or(!got)) return;
+    if (threadIdx.x == 0 && l + 1 < p.layers) fetch(l + 1);
 
     // LN1 -> the row buffer -> the whole row n; this quarter's K and V columns -> shared memory
     uint64_t n[16];  // the row's LN output as packed pairs

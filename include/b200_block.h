@@ -218,8 +218,10 @@ int b200_block_forward_chunked(const B200BlockArgs* args, int chunk_rows, b200_s
  * up to 128, seq_len <= 128 (a CUDA-core kernel, one CTA per sequence).  Every
  * intermediate stays on chip (TMEM / shared memory); per layer the weights are stacked
  * along rows: w_qkv [L*3d, d], w_o [L*d, d], w_in [L*ffn, d], w_out [L*d, ffn]
- * (fp16), biases / LayerNorm parameters [L, n] (fp32).  y must not alias x (y
- * carries the residual between layers).  Other shapes return B200_ERR_CONFIG. */
+ * (fp16), biases / LayerNorm parameters [L, n] (fp32).  Every pointer must be
+ * 16-byte aligned (the weights and vectors arrive by bulk copy), else
+ * B200_ERR_ALIGN.  y must not alias x (y carries the residual between
+ * layers).  Other shapes return B200_ERR_CONFIG. */
 typedef struct {
   int batch, seq_len, d_model, num_heads, ffn_dim, num_layers;
   const float* x;
