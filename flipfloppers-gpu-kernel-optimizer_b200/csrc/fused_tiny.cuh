@@ -3,25 +3,29 @@
 //
 // The reference's official matrix has such a shape (d=32 H=4 ffn=32, 4
 // layers; run_eval.sh:44-58).  At d = 32 a 128-row tcgen05 tile would be
-// mostly padding and every stage of the per-layer kernel chain is a few
-// microseconds of launch and prologue around almost no arithmetic, so the
-// whole model runs in one kernel on the CUDA cores:
+// mostly padding in attention (head_dim 8) and every stage of the per-layer
+// kernel chain is a few microseconds of launch and prologue around almost no
+// arithmetic, so the whole model runs in one kernel on the CUDA cores.
 //
-//   one CTA per sequence, four threads per row (512 threads): thread (r, c)
-//   owns columns 8c..8c+7 of row r (x, the LN outputs, the context); the
-//   LayerNorm statistics combine over the quad with two shuffles; a product
-//   that needs a whole row (the projections, the FFN hidden units) reads it
-//   from a per-row shared-memory buffer the quad fills (the quad is one
-//   warp's lanes, so __syncwarp orders it); each thread computes 8 of the
-//   outputs.  The layer's weights are staged in shared memory as fp32 (read
-//   at one address by many lanes: broadcasts); K and V of every row go to
-//   shared memory.  Attention runs per (row, head): with 4 heads one thread
-//   per head walks the visible keys with an online softmax (log2 domain);
-//   with fewer heads the threads of a head take alternate keys and merge
-//   their (max, sum, context) with shuffles.
+// What bounds it is shared memory, not arithmetic: a 128-bit shared load
+// costs four wavefronts even when every lane of a quarter-warp reads the
+// same address, so the design goal is few loaded bytes per multiply-add.
+// One CTA per sequence, 512 threads; an "octet" (8 adjacent lanes) owns the
+// row pair (2i, 2i+1) and thread u of the octet owns columns 4u..4u+3 of both
+// rows (the residual stream lives in registers).  Every projection is a
+// register-blocked product over the pair: each weight loaded from shared
+// memory feeds both rows, each activation load feeds 4 to 12 outputs
+// (QKV: 12 outputs x 2 rows per thread).  LayerNorm statistics combine over
+// the octet with shuffles.  Attention at head_dim 8 gives each thread a
+// (head, key parity) of the pair, so one K / V load serves two query rows;
+// at head_dim 16 / 32 a thread takes one row and 1/2 or 1/4 of its keys.
+// Partial softmaxes merge with shuffles.  Weights are staged as fp32 in shared
+// memory (the next layer's fp16 copies arrive by bulk copy during this one)
+// with 4 floats of padding after every 4 rows, so the 8 rows an octet reads
+// in one instruction fall on distinct bank groups.
 //
 // Matrix products accumulate in fp32 from the fp16 weight copies the other
-// paths use, in chains of 4 independent outputs so the FMA latency overlaps.
+// paths use, as f32x2 pairs (even / odd k) in independent chains.
 #pragma once
 
 #include "ptx.cuh"
@@ -49,35 +53,32 @@ struct TinyParams {
   int non_causal;
 };
 
-// floats of a [rows][ld] weight staged with 4 floats of padding after every 8 rows
-constexpr int tiny_padded(int rows, int ld) { return rows * ld + (rows / 8) * 4; }
+// floats of a [rows][ld] weight staged with 4 floats of padding after every 4 rows
+constexpr int tiny_padded(int rows, int ld) { return rows * ld + (rows / 4) * 4; }
 
 struct TinyCfg {
   static constexpr int D = 32;
   static constexpr int S = 128;          // rows per CTA
-  static constexpr int THREADS = 4 * S;  // a quad per row
+  static constexpr int THREADS = 4 * S;  // an octet (8 threads) per row pair
   static constexpr int FMAX = 128;
-  static constexpr int LD = D + 4;       // padded row stride (floats) of the K / V rows
-  static constexpr int RL = FMAX + 4;    // row stride of the exchange buffer
-  // Weights are row-major with 4 floats of padding after every 8 rows
-  // (tiny_row): the quad's threads read rows 8 apart in the same instruction,
-  // which without the padding would fall on the same banks.
+  static constexpr int LD = D + 4;       // row stride (floats) of the K / V / row buffers
+  static constexpr int HL = FMAX + 4;    // row stride of the hidden-unit buffer
   // shared memory (floats)
-  static constexpr int W_QKV = 0;                                   // [96][32]
-  static constexpr int W_O = W_QKV + tiny_padded(3 * D, D);              // [32][32]
-  static constexpr int W_IN = W_O + tiny_padded(D, D);                   // [FMAX][32]
-  static constexpr int W_OUT = W_IN + tiny_padded(FMAX, D);              // [32][ffn]
-  static constexpr int VEC = W_OUT + tiny_padded(D, FMAX);               // ln1 w,b | b_qkv | b_o | ln2 w,b | b_in | b_out
+  static constexpr int W_QKV = 0;                                  // [96][32]
+  static constexpr int W_O = W_QKV + tiny_padded(3 * D, D);        // [32][32]
+  static constexpr int W_IN = W_O + tiny_padded(D, D);             // [FMAX][32]
+  static constexpr int W_OUT = W_IN + tiny_padded(FMAX, D);        // [32][ffn]
+  static constexpr int VEC = W_OUT + tiny_padded(D, FMAX);         // ln1 w,b | b_qkv | b_o | ln2 w,b | b_in | b_out
   static constexpr int V_LN1W = 0, V_LN1B = 32, V_BQKV = 64, V_BO = 160, V_LN2W = 192, V_LN2B = 224, V_BIN = 256,
                        V_BOUT = 256 + FMAX, V_TOTAL = 288 + FMAX;
-  static constexpr int KS = VEC + V_TOTAL;              // [S][LD]
-  static constexpr int VS = KS + S * LD;                // [S][LD]
-  static constexpr int ROWS = VS + S * LD;              // [S][RL] exchange buffer (a row's n, context or hidden units)
-  static constexpr int KOK = ROWS + S * RL;             // [S] 1: key exists and is not padding
+  static constexpr int KS = VEC + V_TOTAL;              // [S][LD] keys
+  static constexpr int VS = KS + S * LD;                // [S][LD] values
+  static constexpr int NB = VS + S * LD;                // [S][LD] a row's LN output, then Q, then the context
+  static constexpr int HB = NB + S * LD;                // [S][HL] GELU(hidden units)
   // the next layer's fp16 weights and fp32 vectors as they arrive by bulk copy
   // (row-major, unpadded; the vectors in the VEC layout), converted into the
   // regions above at the layer boundary
-  static constexpr int STG_QKV = KOK + S;               // [96][32] fp16
+  static constexpr int STG_QKV = HB + S * HL;           // [96][32] fp16
   static constexpr int STG_O = STG_QKV + 3 * D * D / 2; // [32][32] fp16
   static constexpr int STG_IN = STG_O + D * D / 2;      // [ffn][32] fp16
   static constexpr int STG_OUT = STG_IN + FMAX * D / 2; // [32][ffn] fp16
@@ -85,101 +86,96 @@ struct TinyCfg {
   static constexpr int BAR = STG_VEC + V_TOTAL;         // mbarrier (8 bytes) + abort flag
   static constexpr int TOTAL_FLOATS = BAR + 4;
   static constexpr int TOTAL = TOTAL_FLOATS * 4;
+  static_assert(TOTAL <= 232448, "shared memory");
+  static_assert(KS % 4 == 0 && NB % 4 == 0 && HB % 4 == 0 && STG_QKV % 4 == 0 && STG_VEC % 4 == 0 && BAR % 2 == 0,
+                "16-byte aligned regions");
 };
 
-// sum over the quad (the 4 threads of a row: adjacent lanes)
-__device__ __forceinline__ float quad_sum(float v) {
+// offset (floats) of row `row` of a weight staged with row stride ld (padded layout)
+__device__ __forceinline__ int tiny_row(int row, int ld) { return row * ld + (row >> 2) * 4; }
+
+// sum over the octet (8 adjacent lanes)
+__device__ __forceinline__ float octet_sum(float v) {
   v += __shfl_xor_sync(0xffffffffu, v, 1);
   v += __shfl_xor_sync(0xffffffffu, v, 2);
+  v += __shfl_xor_sync(0xffffffffu, v, 4);
   return v;
 }
 
-// LayerNorm of a 32-wide row held as 8 columns per quad thread (two-pass statistics)
-__device__ __forceinline__ void tiny_layer_norm8(float (&v)[8], const float* gamma8, const float* beta8, float eps) {
-  const float mean = quad_sum(((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]))) * (1.f / 32.f);
+// LayerNorm of a 32-wide row held as 4 columns per octet thread (two-pass statistics);
+// gamma4 / beta4: this thread's 4 parameters
+__device__ __forceinline__ void tiny_layer_norm4(float (&v)[4], const float* gamma4, const float* beta4, float eps) {
+  const float mean = octet_sum((v[0] + v[1]) + (v[2] + v[3])) * (1.f / 32.f);
   float sq = 0.f;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
+  for (int i = 0; i < 4; ++i) {
     v[i] -= mean;
     sq = fmaf(v[i], v[i], sq);
   }
-  const float rstd = rsqrtf(quad_sum(sq) * (1.f / 32.f) + eps);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) v[i] = fmaf(v[i] * rstd, gamma8[i], beta8[i]);
+  const float rstd = rsqrtf(octet_sum(sq) * (1.f / 32.f) + eps);
+  const float4 g = *reinterpret_cast<const float4*>(gamma4), b = *reinterpret_cast<const float4*>(beta4);
+  v[0] = fmaf(v[0] * rstd, g.x, b.x);
+  v[1] = fmaf(v[1] * rstd, g.y, b.y);
+  v[2] = fmaf(v[2] * rstd, g.z, b.z);
+  v[3] = fmaf(v[3] * rstd, g.w, b.w);
 }
 
-// offset (floats) of row `row` of a weight staged with row stride ld (TinyCfg::padded layout)
-__device__ __forceinline__ int tiny_row(int row, int ld) { return row * ld + (row >> 3) * 4; }
+__device__ __forceinline__ void ld4(const float* p, float (&v)[4]) {
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+}
+__device__ __forceinline__ void st4(float* p, const float (&v)[4]) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+}
 
-// out[c] = bias[c] + a . W[row0 + c] for c in [0, N): W row-major [.][32] fp32 in shared
-// memory (padded layout), a as 16 packed pairs.  Four outputs at a time, each
-// accumulating its even and odd products as one f32x2 pair (independent chains).
-template <int N>
-__device__ __forceinline__ void tiny_matvec32(const uint64_t (&a)[16], const float* W, int row0, const float* bias,
-                                              float (&out)[N]) {
+// acc[r][4g + i] += sum_k a_r[k] * W[32g + 4u + i][k0 + k] for k in [0, 32), rows r = 0, 1
+// (a0 / a1: the two rows' 32 activations in shared memory, W: padded row-major
+// weight with row stride ld).  Per 4-k step: two activation loads and 4*NG
+// weight loads feed 16*NG multiply-adds.  Accumulators are f32x2 pairs of the
+// even / odd k partial sums.
+template <int NG>
+__device__ __forceinline__ void tiny_mm32(const float* a0, const float* a1, const float* W, int ld, int u, int k0,
+                                          uint64_t (&acc)[2][4 * NG]) {
+  const float* wb = W + tiny_row(4 * u, ld) + k0;
 #pragma unroll
-  for (int c = 0; c < N; c += 4) {
-    uint64_t acc0 = 0, acc1 = 0, acc2 = 0, acc3 = 0;  // (0.f, 0.f)
-    const float* W0 = W + tiny_row(row0 + c, 32);
-    const float* W1 = W + tiny_row(row0 + c + 1, 32);
-    const float* W2 = W + tiny_row(row0 + c + 2, 32);
-    const float* W3 = W + tiny_row(row0 + c + 3, 32);
+  for (int k = 0; k < 32; k += 4) {
+    const float4 x0 = *reinterpret_cast<const float4*>(a0 + k);
+    const float4 x1 = *reinterpret_cast<const float4*>(a1 + k);
+    const uint64_t x0a = f2pk(x0.x, x0.y), x0b = f2pk(x0.z, x0.w);
+    const uint64_t x1a = f2pk(x1.x, x1.y), x1b = f2pk(x1.z, x1.w);
 #pragma unroll
-    for (int k = 0; k < 32; k += 4) {
-      const float4 w0 = *reinterpret_cast<const float4*>(W0 + k);
-      const float4 w1 = *reinterpret_cast<const float4*>(W1 + k);
-      const float4 w2 = *reinterpret_cast<const float4*>(W2 + k);
-      const float4 w3 = *reinterpret_cast<const float4*>(W3 + k);
-      acc0 = f2fma(a[k / 2 + 1], f2pk(w0.z, w0.w), f2fma(a[k / 2], f2pk(w0.x, w0.y), acc0));
-      acc1 = f2fma(a[k / 2 + 1], f2pk(w1.z, w1.w), f2fma(a[k / 2], f2pk(w1.x, w1.y), acc1));
-      acc2 = f2fma(a[k / 2 + 1], f2pk(w2.z, w2.w), f2fma(a[k / 2], f2pk(w2.x, w2.y), acc2));
-      acc3 = f2fma(a[k / 2 + 1], f2pk(w3.z, w3.w), f2fma(a[k / 2], f2pk(w3.x, w3.y), acc3));
+    for (int g = 0; g < NG; ++g) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        // row 32g + 4u + i: (32g + 4u + i) * ld + (8g + u) * 4
+        const float4 w = *reinterpret_cast<const float4*>(wb + g * (32 * ld + 32) + i * ld + k);
+        const uint64_t wa = f2pk(w.x, w.y), wc = f2pk(w.z, w.w);
+        acc[0][4 * g + i] = f2fma(x0b, wc, f2fma(x0a, wa, acc[0][4 * g + i]));
+        acc[1][4 * g + i] = f2fma(x1b, wc, f2fma(x1a, wa, acc[1][4 * g + i]));
+      }
     }
-    float e, o;
-    f2upk(acc0, e, o);
-    out[c] = bias[c] + (e + o);
-    f2upk(acc1, e, o);
-    out[c + 1] = bias[c + 1] + (e + o);
-    f2upk(acc2, e, o);
-    out[c + 2] = bias[c + 2] + (e + o);
-    f2upk(acc3, e, o);
-    out[c + 3] = bias[c + 3] + (e + o);
   }
 }
 
-// acc[o] += sum_k h[k] * W[row0 + o][col0 + k] for o in [0, N): a 32-column slice of a
-// row-major weight with row stride ld (padded layout), h as 16 packed pairs
 template <int N>
-__device__ __forceinline__ void tiny_matvec32_acc(const uint64_t (&h)[16], const float* W, int row0, int ld, int col0,
-                                                  float (&acc)[N]) {
+__device__ __forceinline__ void tiny_zero(uint64_t (&acc)[2][N]) {
 #pragma unroll
-  for (int o = 0; o < N; o += 4) {
-    uint64_t a0 = 0, a1 = 0, a2 = 0, a3 = 0;
-    const float* W0 = W + tiny_row(row0 + o, ld) + col0;
-    const float* W1 = W + tiny_row(row0 + o + 1, ld) + col0;
-    const float* W2 = W + tiny_row(row0 + o + 2, ld) + col0;
-    const float* W3 = W + tiny_row(row0 + o + 3, ld) + col0;
-#pragma unroll
-    for (int k = 0; k < 32; k += 4) {
-      const float4 w0 = *reinterpret_cast<const float4*>(W0 + k);
-      const float4 w1 = *reinterpret_cast<const float4*>(W1 + k);
-      const float4 w2 = *reinterpret_cast<const float4*>(W2 + k);
-      const float4 w3 = *reinterpret_cast<const float4*>(W3 + k);
-      a0 = f2fma(h[k / 2 + 1], f2pk(w0.z, w0.w), f2fma(h[k / 2], f2pk(w0.x, w0.y), a0));
-      a1 = f2fma(h[k / 2 + 1], f2pk(w1.z, w1.w), f2fma(h[k / 2], f2pk(w1.x, w1.y), a1));
-      a2 = f2fma(h[k / 2 + 1], f2pk(w2.z, w2.w), f2fma(h[k / 2], f2pk(w2.x, w2.y), a2));
-      a3 = f2fma(h[k / 2 + 1], f2pk(w3.z, w3.w), f2fma(h[k / 2], f2pk(w3.x, w3.y), a3));
-    }
-    float e, od;
-    f2upk(a0, e, od);
-    acc[o] += e + od;
-    f2upk(a1, e, od);
-    acc[o + 1] += e + od;
-    f2upk(a2, e, od);
-    acc[o + 2] += e + od;
-    f2upk(a3, e, od);
-    acc[o + 3] += e + od;
-  }
+  for (int i = 0; i < N; ++i) acc[0][i] = acc[1][i] = 0ull;
+}
+
+// the 4 outputs 4g..4g+3 of row r of an accumulator, plus bias b4
+template <int N>
+__device__ __forceinline__ void tiny_out4(const uint64_t (&acc)[2][N], int r, int g, const float* b4, float (&o)[4]) {
+  const float4 b = *reinterpret_cast<const float4*>(b4);
+  float e, d;
+  f2upk(acc[r][4 * g], e, d);
+  o[0] = b.x + (e + d);
+  f2upk(acc[r][4 * g + 1], e, d);
+  o[1] = b.y + (e + d);
+  f2upk(acc[r][4 * g + 2], e, d);
+  o[2] = b.z + (e + d);
+  f2upk(acc[r][4 * g + 3], e, d);
+  o[3] = b.w + (e + d);
 }
 
 // fp16 weight [rows][ld] (shared memory, as staged) -> fp32 shared memory in the
@@ -196,49 +192,192 @@ __device__ __forceinline__ void tiny_stage_f16(float* dst, const __half* src, in
   }
 }
 
-// 8 consecutive floats at p (16-byte aligned) -> v / v -> p
-__device__ __forceinline__ void ld8(const float* p, float (&v)[8]) {
-  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
-  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-}
-__device__ __forceinline__ void st8(float* p, const float (&v)[8]) {
-  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
-  *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
-}
-// 32 consecutive floats at p (16-byte aligned) as 16 packed pairs
-__device__ __forceinline__ void ld32x2(const float* p, uint64_t (&v)[16]) {
+// Attention of an octet's rows for head_dim HD; thread u of the octet whose row pair
+// starts at r0.  Q of the rows is in NB (its columns head*HD..); the context of
+// each (row, head) goes back to the same place.  Head_dim 8: a thread takes both
+// rows of the pair, one head and alternate keys (one K / V load serves two rows);
+// head_dim 16 / 32: one row, one head and every 2nd / 4th key.  Online softmax in
+// the log2 domain per row; the T threads of a (rows, head) merge their partial
+// (max, sum, context) with shuffles.  Keys are walked in blocks of 32 (kw: key
+// validity words, bit i of word w = key 32w + i exists and is not padding);
+// masked keys are skipped, never weighted by zero.
+template <int HD>
+__device__ __forceinline__ void tiny_attention(float* sm, int u, int r0, const uint32_t (&kw)[4],
+                                               const TinyParams& p) {
+  using C = TinyCfg;
+  constexpr int H = C::D / HD;
+  constexpr int R = HD == 8 ? 2 : 1;   // query rows per thread
+  constexpr int TPR = R == 2 ? 8 : 4;  // threads sharing a row set
+  constexpr int T = TPR / H;           // threads per (row set, head)
+  constexpr int KB = 32 / T;           // keys per thread per 32-key block
+  const int idx = R == 2 ? u : (u & 3);
+  const int rbase = R == 2 ? r0 : r0 + (u >> 2);
+  const int head = idx / T, sub = idx % T;
+  const int kend = p.non_causal ? p.seq_len : min(rbase + R, p.seq_len);  // keys 0..kend-1 may be visible
+
+  uint64_t q2[R][HD / 2], o[R][HD / 2];
+  float m[R], l[R];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const float4 a = *reinterpret_cast<const float4*>(p + 4 * j);
-    v[2 * j] = f2pk(a.x, a.y);
-    v[2 * j + 1] = f2pk(a.z, a.w);
+  for (int rr = 0; rr < R; ++rr) {
+    const float* qr = sm + C::NB + (rbase + rr) * C::LD + head * HD;
+#pragma unroll
+    for (int e = 0; e < HD; e += 4) {
+      const float4 a = *reinterpret_cast<const float4*>(qr + e);
+      q2[rr][e / 2] = f2pk(a.x * p.scale_log2, a.y * p.scale_log2);  // scores come out in log2 units
+      q2[rr][e / 2 + 1] = f2pk(a.z * p.scale_log2, a.w * p.scale_log2);
+      o[rr][e / 2] = o[rr][e / 2 + 1] = 0ull;
+    }
+    m[rr] = -INFINITY;
+    l[rr] = 0.f;
   }
+  for (int kb = 0; kb < kend; kb += 32) {
+    const uint32_t word = (kb < 32 ? kw[0] : kb < 64 ? kw[1] : kb < 96 ? kw[2] : kw[3]) >> sub;
+    float s[R][KB];
+    float mb[R];
+#pragma unroll
+    for (int rr = 0; rr < R; ++rr) mb[rr] = -INFINITY;
+#pragma unroll
+    for (int jj = 0; jj < KB; ++jj) {
+      const int j = kb + sub + jj * T;
+      float acc[R];
+#pragma unroll
+      for (int rr = 0; rr < R; ++rr) acc[rr] = -INFINITY;
+      if (j < kend && ((word >> (jj * T)) & 1u)) {
+        const float* kr = sm + C::KS + j * C::LD + head * HD;
+        uint64_t a2[R];
+#pragma unroll
+        for (int rr = 0; rr < R; ++rr) a2[rr] = 0ull;
+#pragma unroll
+        for (int e = 0; e < HD; e += 4) {
+          const float4 kk = *reinterpret_cast<const float4*>(kr + e);
+          const uint64_t ka = f2pk(kk.x, kk.y), kc = f2pk(kk.z, kk.w);
+#pragma unroll
+          for (int rr = 0; rr < R; ++rr) a2[rr] = f2fma(q2[rr][e / 2 + 1], kc, f2fma(q2[rr][e / 2], ka, a2[rr]));
+        }
+#pragma unroll
+        for (int rr = 0; rr < R; ++rr) {
+          if (p.non_causal || j <= rbase + rr) {
+            float lo, hi;
+            f2upk(a2[rr], lo, hi);
+            acc[rr] = lo + hi;
+          }
+        }
+      }
+#pragma unroll
+      for (int rr = 0; rr < R; ++rr) {
+        s[rr][jj] = acc[rr];
+        mb[rr] = fmaxf(mb[rr], acc[rr]);
+      }
+    }
+#pragma unroll
+    for (int rr = 0; rr < R; ++rr) {
+      if (mb[rr] != -INFINITY) {  // rows with no visible key in this block keep their state
+        const float mn = fmaxf(m[rr], mb[rr]);
+        const float corr = fast_exp2(m[rr] - mn);  // 0 on the row's first visible block
+        l[rr] *= corr;
+        const uint64_t c2 = f2pk(corr, corr);
+#pragma unroll
+        for (int e = 0; e < HD / 2; ++e) o[rr][e] = f2mul(o[rr][e], c2);
+        m[rr] = mn;
+      }
+    }
+#pragma unroll
+    for (int jj = 0; jj < KB; ++jj) {
+      bool any = false;
+#pragma unroll
+      for (int rr = 0; rr < R; ++rr) any |= s[rr][jj] != -INFINITY;
+      if (any) {
+        const float* vr = sm + C::VS + (kb + sub + jj * T) * C::LD + head * HD;
+#pragma unroll
+        for (int rr = 0; rr < R; ++rr) {
+          // a masked score gives 0 here (exp2(-inf)) without touching l or o below
+          const float pj = s[rr][jj] != -INFINITY ? fast_exp2(s[rr][jj] - m[rr]) : 0.f;
+          s[rr][jj] = pj;
+          l[rr] += pj;
+        }
+#pragma unroll
+        for (int e = 0; e < HD; e += 4) {
+          const float4 vv = *reinterpret_cast<const float4*>(vr + e);
+          const uint64_t va = f2pk(vv.x, vv.y), vc = f2pk(vv.z, vv.w);
+#pragma unroll
+          for (int rr = 0; rr < R; ++rr) {
+            if (R == 1 || s[rr][jj] != 0.f) {
+              const uint64_t p2 = f2pk(s[rr][jj], s[rr][jj]);
+              o[rr][e / 2] = f2fma(p2, va, o[rr][e / 2]);
+              o[rr][e / 2 + 1] = f2fma(p2, vc, o[rr][e / 2 + 1]);
+            }
+          }
+        }
+      }
+    }
+  }
+  // merge the partial softmaxes of the T threads of a (rows, head) (alternate keys)
+#pragma unroll
+  for (int off = 1; off < T; off <<= 1) {
+#pragma unroll
+    for (int rr = 0; rr < R; ++rr) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m[rr], off), l2 = __shfl_xor_sync(0xffffffffu, l[rr], off);
+      const float mm = fmaxf(m[rr], m2);
+      const float a = (m[rr] == -INFINITY) ? 0.f : fast_exp2(m[rr] - mm);
+      const float b2 = (m2 == -INFINITY) ? 0.f : fast_exp2(m2 - mm);
+      l[rr] = l[rr] * a + l2 * b2;
+      const uint64_t a_2 = f2pk(a, a), b_2 = f2pk(b2, b2);
+#pragma unroll
+      for (int e = 0; e < HD / 2; ++e) {
+        const uint64_t other = __shfl_xor_sync(0xffffffffu, o[rr][e], off);
+        o[rr][e] = f2fma(o[rr][e], a_2, f2mul(other, b_2));
+      }
+      m[rr] = mm;
+    }
+  }
+  // each of the T threads writes 8 of the R*HD results: row sub % R, dims 8*(sub / R)..
+  const int rw = sub % R, dc = sub / R;
+  uint64_t w[4];
+  float inv = 0.f;
+#pragma unroll
+  for (int rr = 0; rr < R; ++rr) {
+    if (rr == rw) {
+      inv = l[rr] > 0.f ? 1.f / l[rr] : 0.f;  // a row with no visible key (padding) gets 0
+#pragma unroll
+      for (int c = 0; c < HD / 8; ++c)
+        if (c == dc) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) w[e] = o[rr][4 * c + e];
+        }
+    }
+  }
+  __syncwarp();  // every thread of the octet has read its Q
+  const uint64_t inv2 = f2pk(inv, inv);
+  float* dst = sm + C::NB + (rbase + rw) * C::LD + head * HD + 8 * dc;
+  float v[8];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) f2upk(f2mul(w[e], inv2), v[2 * e], v[2 * e + 1]);
+  *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+  *reinterpret_cast<float4*>(dst + 4) = make_float4(v[4], v[5], v[6], v[7]);
 }
 
 template <int HD>
 __global__ void __launch_bounds__(TinyCfg::THREADS, 1) k_block_tiny(const TinyParams p) {
   using C = TinyCfg;
   static_assert(HD == 8 || HD == 16 || HD == 32, "head_dim 8, 16 or 32");
-  constexpr int H = C::D / HD;  // heads
-  constexpr int T = 4 / H;      // threads of a quad per head; they take alternate keys
-  constexpr int KB = HD == 32 ? 16 : 32;  // keys per softmax block (fewer live scores at head_dim 32)
   extern __shared__ float4 smem_f4[];
   float* sm = reinterpret_cast<float*>(smem_f4);
 
   griddep_sync();
-  const int r = threadIdx.x >> 2;  // row
-  const int c = threadIdx.x & 3;   // column quarter: columns 8c..8c+7
-  const int head = c / T, sub = c % T;
+  const int u = threadIdx.x & 7;                   // columns 4u..4u+3 of the octet's rows
+  const int r0 = static_cast<int>(threadIdx.x >> 3) * 2;  // the octet's row pair r0, r0 + 1
   const int seq = blockIdx.x;
   const int F = p.ffn;
-  const bool row_ok = r < p.seq_len;
-  const int64_t grow = static_cast<int64_t>(seq) * p.seq_len + r;
+  const bool ok0 = r0 < p.seq_len, ok1 = r0 + 1 < p.seq_len;
+  const int64_t g0 = static_cast<int64_t>(seq) * p.seq_len + r0;  // global row of r0
   float* vec = sm + C::VEC;
-  float* rowbuf = sm + C::ROWS + r * C::RL;
-  const float* key_ok = sm + C::KOK;
+  float* nb0 = sm + C::NB + r0 * C::LD;
+  float* nb1 = nb0 + C::LD;
+  float* hb0 = sm + C::HB + r0 * C::HL;
+  float* hb1 = hb0 + C::HL;
   uint64_t* wbar = reinterpret_cast<uint64_t*>(sm + C::BAR);  // a layer's staged weights and vectors
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + C::BAR + 2);
-  // one thread copies layer l's weights and vectors into the staging area (ten bulk
+  // one thread copies layer l's weights and vectors into the staging area (twelve bulk
   // copies, one mbarrier phase): issued a layer ahead, so the HBM / L2 round trip
   // overlaps the previous layer's arithmetic instead of stalling every boundary
   auto fetch = [&](int l) {
@@ -266,8 +405,6 @@ __global__ void __launch_bounds__(TinyCfg::THREADS, 1) k_block_tiny(const TinyPa
   }
   __syncthreads();
   if (threadIdx.x == 0) fetch(0);
-  if (c == 0) sm[C::KOK + r] = (row_ok && (p.row_valid == nullptr || p.row_valid[grow] != 0)) ? 1.f : 0.f;
-  const int kend = p.non_causal ? p.seq_len : min(r + 1, p.seq_len);  // keys 0..kend-1 may be visible
   // key validity as four 32-bit words in registers (lane i tests key 32w + i)
   uint32_t kw[4];
 #pragma unroll
@@ -277,16 +414,12 @@ __global__ void __launch_bounds__(TinyCfg::THREADS, 1) k_block_tiny(const TinyPa
                                                           p.row_valid[static_cast<int64_t>(seq) * p.seq_len + j] != 0));
   }
 
-  float x[8];
-  if (row_ok) {
-    ld8(p.x + grow * 32 + 8 * c, x);
-  } else {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) x[i] = 0.f;
-  }
+  float x0[4] = {0.f, 0.f, 0.f, 0.f}, x1[4] = {0.f, 0.f, 0.f, 0.f};  // the residual stream
+  if (ok0) ld4(p.x + g0 * 32 + 4 * u, x0);
+  if (ok1) ld4(p.x + (g0 + 1) * 32 + 4 * u, x1);
 
   for (int l = 0; l < p.layers; ++l) {
-    __syncthreads();  // the previous layer's weights and K / V are no longer read
+    __syncthreads();  // the previous layer's weights, K / V and row buffers are no longer read
     // layer l's staged copies -> fp32 weights (padded layout) and vectors
     const bool got = mbar_wait(wbar, static_cast<uint32_t>(l & 1), abort_flag, DERR_WAIT_TMA);
     if (got) {
@@ -301,171 +434,103 @@ __global__ void __launch_bounds__(TinyCfg::THREADS, 1) k_block_tiny(const TinyPa
     if (__syncthreads_or(!got)) return;
     if (threadIdx.x == 0 && l + 1 < p.layers) fetch(l + 1);
 
-    // LN1 -> the row buffer -> the whole row n; this quarter's K and V columns -> shared memory
-    uint64_t n[16];  // the row's LN output as packed pairs
+    // ---- LN1 -> NB
     {
-      float t8[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) t8[i] = x[i];
-      tiny_layer_norm8(t8, vec + C::V_LN1W + 8 * c, vec + C::V_LN1B + 8 * c, p.eps);
-      st8(rowbuf + 8 * c, t8);
-      __syncwarp();
-      ld32x2(rowbuf, n);
-      float kv[8];
-      tiny_matvec32<8>(n, sm + C::W_QKV, 32 + 8 * c, vec + C::V_BQKV + 32 + 8 * c, kv);
-      st8(sm + C::KS + r * C::LD + 8 * c, kv);
-      tiny_matvec32<8>(n, sm + C::W_QKV, 64 + 8 * c, vec + C::V_BQKV + 64 + 8 * c, kv);
-      st8(sm + C::VS + r * C::LD + 8 * c, kv);
-    }
-    __syncthreads();  // every row's K and V are in place
-
-    // attention for (row r, head): this thread's keys are sub, sub + T, ...
-    // (query and context accumulator as packed pairs: dot products and the P.V update
-    // run as f32x2 FMAs)
-    uint64_t o[HD / 2];
-    float m = -INFINITY, lsum = 0.f;
-    {
-      uint64_t q2[HD / 2];
-      {
-        float q[HD];
-        tiny_matvec32<HD>(n, sm + C::W_QKV, head * HD, vec + C::V_BQKV + head * HD, q);
-#pragma unroll
-        for (int e = 0; e < HD; e += 2) {
-          q2[e / 2] = f2pk(q[e] * p.scale_log2, q[e + 1] * p.scale_log2);  // scores in log2 units
-          o[e / 2] = 0;
-        }
-      }
-      for (int j0 = sub; j0 < kend; j0 += KB * T) {
-        float s[KB];
-        float mb = -INFINITY;
-        // one head per thread (T == 1): the block's keys j0.. share one validity word
-        const uint32_t kv_word = T == 1 ? (j0 < 32 ? kw[0] : j0 < 64 ? kw[1] : j0 < 96 ? kw[2] : kw[3]) >> (j0 & 31)
-                                        : 0u;
-#pragma unroll
-        for (int jj = 0; jj < KB; ++jj) {
-          const int j = j0 + jj * T;
-          float acc = -INFINITY;
-          const bool valid = T == 1 ? ((kv_word >> jj) & 1u) != 0u : key_ok[j] != 0.f;
-          if (j < kend && valid) {
-            const float* kr = sm + C::KS + j * C::LD + head * HD;
-            uint64_t a2 = 0;
-#pragma unroll
-            for (int e = 0; e < HD; e += 4) {
-              const float4 kk = *reinterpret_cast<const float4*>(kr + e);
-              a2 = f2fma(q2[e / 2 + 1], f2pk(kk.z, kk.w), f2fma(q2[e / 2], f2pk(kk.x, kk.y), a2));
-            }
-            float lo, hi;
-            f2upk(a2, lo, hi);
-            acc = lo + hi;
-          }
-          s[jj] = acc;
-          mb = fmaxf(mb, acc);
-        }
-        if (mb == -INFINITY) continue;  // no visible key in this block
-        const float mn = fmaxf(m, mb);
-        const float corr = fast_exp2(m - mn);  // 0 on the first visible block
-        lsum *= corr;
-        const uint64_t corr2 = f2pk(corr, corr);
-#pragma unroll
-        for (int e = 0; e < HD / 2; ++e) o[e] = f2mul(o[e], corr2);
-        m = mn;
-#pragma unroll
-        for (int jj = 0; jj < KB; ++jj) {
-          if (s[jj] != -INFINITY) {  // masked keys are skipped, never weighted by zero
-            const float pj = fast_exp2(s[jj] - m);
-            lsum += pj;
-            const uint64_t p2 = f2pk(pj, pj);
-            const float* vr = sm + C::VS + (j0 + jj * T) * C::LD + head * HD;
-#pragma unroll
-            for (int e = 0; e < HD; e += 4) {
-              const float4 vv = *reinterpret_cast<const float4*>(vr + e);
-              o[e / 2] = f2fma(p2, f2pk(vv.x, vv.y), o[e / 2]);
-              o[e / 2 + 1] = f2fma(p2, f2pk(vv.z, vv.w), o[e / 2 + 1]);
-            }
-          }
-        }
-      }
-    }
-    // merge the partial softmaxes of a head's T threads (alternate keys)
-#pragma unroll
-    for (int off = 1; off < T; off <<= 1) {
-      const float m2 = __shfl_xor_sync(0xffffffffu, m, off), l2 = __shfl_xor_sync(0xffffffffu, lsum, off);
-      const float mm = fmaxf(m, m2);
-      const float a = (m == -INFINITY) ? 0.f : fast_exp2(m - mm);
-      const float b2 = (m2 == -INFINITY) ? 0.f : fast_exp2(m2 - mm);
-      lsum = lsum * a + l2 * b2;
-      const uint64_t a_2 = f2pk(a, a), b_2 = f2pk(b2, b2);
-#pragma unroll
-      for (int e = 0; e < HD / 2; ++e) {
-        const uint64_t other = __shfl_xor_sync(0xffffffffu, o[e], off);
-        o[e] = f2fma(o[e], a_2, f2mul(other, b_2));
-      }
-      m = mm;
-    }
-    {
-      const float inv = lsum > 0.f ? 1.f / lsum : 0.f;  // a row with no visible key (padding) gets 0
-      __syncwarp();  // the quad has read n from the row buffer
-      if (sub == 0) {
-        const uint64_t inv2 = f2pk(inv, inv);
-#pragma unroll
-        for (int e = 0; e < HD; e += 2) {
-          float lo, hi;
-          f2upk(f2mul(o[e / 2], inv2), lo, hi);
-          *reinterpret_cast<float2*>(rowbuf + head * HD + e) = make_float2(lo, hi);
-        }
-      }
-      __syncwarp();
-    }
-    // out_proj + residual (this quarter's 8 columns); LN2 -> the row buffer -> n
-    {
-      uint64_t cx[16];
-      ld32x2(rowbuf, cx);
-      float t8[8];
-      tiny_matvec32<8>(cx, sm + C::W_O, 8 * c, vec + C::V_BO + 8 * c, t8);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        x[i] += t8[i];
-        t8[i] = x[i];
-      }
-      tiny_layer_norm8(t8, vec + C::V_LN2W + 8 * c, vec + C::V_LN2B + 8 * c, p.eps);
-      __syncwarp();  // the quad has read the context
-      st8(rowbuf + 8 * c, t8);
-      __syncwarp();
-      ld32x2(rowbuf, n);
-    }
-    // FFN: this quarter's hidden units -> the row buffer; then its 8 output columns over all units
-    __syncwarp();  // the quad has read n
-    for (int u0 = c * (F / 4); u0 < (c + 1) * (F / 4); u0 += 8) {
-      float h8[8];
-      tiny_matvec32<8>(n, sm + C::W_IN, u0, vec + C::V_BIN + u0, h8);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) h8[i] = gelu_as(h8[i]);
-      st8(rowbuf + u0, h8);
+      float t0[4] = {x0[0], x0[1], x0[2], x0[3]}, t1[4] = {x1[0], x1[1], x1[2], x1[3]};
+      tiny_layer_norm4(t0, vec + C::V_LN1W + 4 * u, vec + C::V_LN1B + 4 * u, p.eps);
+      tiny_layer_norm4(t1, vec + C::V_LN1W + 4 * u, vec + C::V_LN1B + 4 * u, p.eps);
+      st4(nb0 + 4 * u, t0);
+      st4(nb1 + 4 * u, t1);
     }
     __syncwarp();
+    // ---- QKV: columns 4u..4u+3 of Q, K and V for both rows; Q -> NB, K / V -> KS / VS
     {
-      float acc[8];
-      ld8(vec + C::V_BOUT + 8 * c, acc);
-#pragma unroll 1
-      for (int k0 = 0; k0 < F; k0 += 32) {
-        uint64_t h32[16];
-        ld32x2(rowbuf + k0, h32);
-        tiny_matvec32_acc<8>(h32, sm + C::W_OUT, 8 * c, F, k0, acc);
-      }
-#pragma unroll
-      for (int i = 0; i < 8; ++i) x[i] += acc[i];
+      uint64_t acc[2][12];
+      tiny_zero(acc);
+      tiny_mm32<3>(nb0, nb1, sm + C::W_QKV, 32, u, 0, acc);
+      float o[4];
+      __syncwarp();  // the octet has read its LN rows (Q overwrites them)
+      tiny_out4(acc, 0, 0, vec + C::V_BQKV + 4 * u, o);
+      st4(nb0 + 4 * u, o);
+      tiny_out4(acc, 1, 0, vec + C::V_BQKV + 4 * u, o);
+      st4(nb1 + 4 * u, o);
+      tiny_out4(acc, 0, 1, vec + C::V_BQKV + 32 + 4 * u, o);
+      st4(sm + C::KS + r0 * C::LD + 4 * u, o);
+      tiny_out4(acc, 1, 1, vec + C::V_BQKV + 32 + 4 * u, o);
+      st4(sm + C::KS + (r0 + 1) * C::LD + 4 * u, o);
+      tiny_out4(acc, 0, 2, vec + C::V_BQKV + 64 + 4 * u, o);
+      st4(sm + C::VS + r0 * C::LD + 4 * u, o);
+      tiny_out4(acc, 1, 2, vec + C::V_BQKV + 64 + 4 * u, o);
+      st4(sm + C::VS + (r0 + 1) * C::LD + 4 * u, o);
     }
-    __syncwarp();  // the row buffer is free for the next layer
+    __syncthreads();  // every row's K and V are in place
+    // ---- attention -> the context in NB
+    tiny_attention<HD>(sm, u, r0, kw, p);
+    __syncwarp();
+    // ---- out_proj + residual; LN2 -> NB
+    {
+      uint64_t acc[2][4];
+      tiny_zero(acc);
+      tiny_mm32<1>(nb0, nb1, sm + C::W_O, 32, u, 0, acc);
+      float o[4];
+      tiny_out4(acc, 0, 0, vec + C::V_BO + 4 * u, o);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) x0[i] += o[i];
+      tiny_out4(acc, 1, 0, vec + C::V_BO + 4 * u, o);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) x1[i] += o[i];
+      float t0[4] = {x0[0], x0[1], x0[2], x0[3]}, t1[4] = {x1[0], x1[1], x1[2], x1[3]};
+      tiny_layer_norm4(t0, vec + C::V_LN2W + 4 * u, vec + C::V_LN2B + 4 * u, p.eps);
+      tiny_layer_norm4(t1, vec + C::V_LN2W + 4 * u, vec + C::V_LN2B + 4 * u, p.eps);
+      __syncwarp();  // the octet has read the context
+      st4(nb0 + 4 * u, t0);
+      st4(nb1 + 4 * u, t1);
+    }
+    __syncwarp();
+    // ---- FFN in: hidden units 32m + 4u .. 32m + 4u + 3 of both rows, GELU -> HB
+#pragma unroll 1
+    for (int m = 0; m < F / 32; ++m) {
+      uint64_t acc[2][4];
+      tiny_zero(acc);
+      tiny_mm32<1>(nb0, nb1, sm + C::W_IN + tiny_row(32 * m, 32), 32, u, 0, acc);
+      float o[4];
+      tiny_out4(acc, 0, 0, vec + C::V_BIN + 32 * m + 4 * u, o);
+      gelu_as2(o[0], o[1]);
+      gelu_as2(o[2], o[3]);
+      st4(hb0 + 32 * m + 4 * u, o);
+      tiny_out4(acc, 1, 0, vec + C::V_BIN + 32 * m + 4 * u, o);
+      gelu_as2(o[0], o[1]);
+      gelu_as2(o[2], o[3]);
+      st4(hb1 + 32 * m + 4 * u, o);
+    }
+    __syncwarp();
+    // ---- FFN out + residual: columns 4u..4u+3 over all hidden units
+    {
+      uint64_t acc[2][4];
+      tiny_zero(acc);
+#pragma unroll 1
+      for (int k0 = 0; k0 < F; k0 += 32) tiny_mm32<1>(hb0 + k0, hb1 + k0, sm + C::W_OUT, F, u, k0, acc);
+      float o[4];
+      tiny_out4(acc, 0, 0, vec + C::V_BOUT + 4 * u, o);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) x0[i] += o[i];
+      tiny_out4(acc, 1, 0, vec + C::V_BOUT + 4 * u, o);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) x1[i] += o[i];
+    }
   }
 
   // final LayerNorm -> y (padded rows are zero)
-  tiny_layer_norm8(x, p.lnf_w + 8 * c, p.lnf_b + 8 * c, p.eps);
-  if (!row_ok) return;
-  if (p.row_valid != nullptr && p.row_valid[grow] == 0) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) x[i] = 0.f;
+  tiny_layer_norm4(x0, p.lnf_w + 4 * u, p.lnf_b + 4 * u, p.eps);
+  tiny_layer_norm4(x1, p.lnf_w + 4 * u, p.lnf_b + 4 * u, p.eps);
+  if (ok0) {
+    if (p.row_valid != nullptr && p.row_valid[g0] == 0) x0[0] = x0[1] = x0[2] = x0[3] = 0.f;
+    st4(p.y + g0 * 32 + 4 * u, x0);
   }
-  st8(p.y + grow * 32 + 8 * c, x);
+  if (ok1) {
+    if (p.row_valid != nullptr && p.row_valid[g0 + 1] == 0) x1[0] = x1[1] = x1[2] = x1[3] = 0.f;
+    st4(p.y + (g0 + 1) * 32 + 4 * u, x1);
+  }
 }
 
 }  // namespace b200
