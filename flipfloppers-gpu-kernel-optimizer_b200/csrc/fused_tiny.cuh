@@ -364,8 +364,13 @@ __global__ void __launch_bounds__(TinyCfg::THREADS, 1) k_block_tiny(const TinyPa
   float* sm = reinterpret_cast<float*>(smem_f4);
 
   griddep_sync();
-  const int u = threadIdx.x & 7;                   // columns 4u..4u+3 of the octet's rows
-  const int r0 = static_cast<int>(threadIdx.x >> 3) * 2;  // the octet's row pair r0, r0 + 1
+  const int u = threadIdx.x & 7;  // columns 4u..4u+3 of the octet's rows
+  // warp w holds the 8-row block b(w), the octet rows b(w)*8 + 2k, + 1.  Warps
+  // w, w+4, w+8, w+12 share a scheduler; giving them blocks s, 7-s, 8+s, 15-s
+  // (s = w % 4) balances the causal attention work across the four schedulers
+  const int wid = static_cast<int>(threadIdx.x >> 5), ws = wid & 3, wt = wid >> 2;
+  const int rblk = wt == 0 ? ws : wt == 1 ? 7 - ws : wt == 2 ? 8 + ws : 15 - ws;
+  const int r0 = rblk * 8 + static_cast<int>((threadIdx.x >> 3) & 3) * 2;  // the octet's row pair r0, r0 + 1
   const int seq = blockIdx.x;
   const int F = p.ffn;
   const bool ok0 = r0 < p.seq_len, ok1 = r0 + 1 < p.seq_len;
