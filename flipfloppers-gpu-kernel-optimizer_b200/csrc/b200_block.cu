@@ -118,20 +118,37 @@ bool pdl_enabled() {
   return on;
 }
 
-// (errors are left for the caller's launch_status(), like a <<<>>> launch)
+// (errors are left for the caller's launch_status(), like a <<<>>> launch);
+// cluster_x > 1: thread-block clusters of cluster_x CTAs along x
 template <typename... Params, typename... Args>
-void launch_kernel(void (*kern)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+void launch_kernel_cluster(void (*kern)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                           unsigned cluster_x, Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = n;
   cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+template <typename... Params, typename... Args>
+void launch_kernel(void (*kern)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  launch_kernel_cluster(kern, grid, block, smem, st, 1u, std::forward<Args>(args)...);
 }
 
 // Refuse a launch the kernel's compiled resources cannot satisfy, with the reason recorded.
@@ -611,6 +628,16 @@ int small_rows_mode() {
   return mode;
 }
 
+// B200_TINY_SPLIT=0|1 forces one CTA per sequence / a two-CTA cluster per sequence
+// for d_model = 32 (default: the cluster when the sequences leave SMs idle)
+int tiny_split_mode() {
+  static const int mode = [] {
+    const char* e = std::getenv("B200_TINY_SPLIT");
+    return e ? std::atoi(e) : -1;
+  }();
+  return mode;
+}
+
 // d_model = 32: the CUDA-core kernel of fused_tiny.cuh (head_dim 8 / 16 / 32)
 int fused_tiny_impl(const B200FusedSmallArgs* a, cudaStream_t st) {
   const int H = a->num_heads;
@@ -644,15 +671,24 @@ int fused_tiny_impl(const B200FusedSmallArgs* a, cudaStream_t st) {
   p.scale_log2 = static_cast<float>(1.4426950408889634 / __builtin_sqrt(static_cast<double>(32 / H)));
   p.row_valid = static_cast<const unsigned char*>(a->row_valid);
   p.non_causal = a->non_causal;
-  const int smem = TinyCfg::TOTAL;
-  auto launch = [&](auto kern) {
-    if (int rc = set_smem(reinterpret_cast<const void*>(kern), smem)) return rc;
-    launch_kernel(kern, dim3(a->batch), dim3(TinyCfg::THREADS), smem, st, p);
+  const int split_mode = tiny_split_mode();
+  const bool split = split_mode != 0 && (split_mode == 1 || 2LL * a->batch <= num_sms()) && a->batch <= 0x3fffffff;
+  auto launch = [&](auto kern, auto cfg) {
+    using Cfg = decltype(cfg);
+    if (int rc = set_smem(reinterpret_cast<const void*>(kern), Cfg::TOTAL)) return rc;
+    if (int rc = check_block_fits(reinterpret_cast<const void*>(kern), Cfg::THREADS)) return rc;
+    const unsigned cl = Cfg::RL < Cfg::S ? 2u : 1u;
+    launch_kernel_cluster(kern, dim3(a->batch * cl), dim3(Cfg::THREADS), Cfg::TOTAL, st, cl, p);
     return launch_status();
   };
-  if (H == 4) return launch(k_block_tiny<8>);
-  if (H == 2) return launch(k_block_tiny<16>);
-  return launch(k_block_tiny<32>);
+  if (split) {
+    if (H == 4) return launch(k_block_tiny<8, true>, TinyCfgT<true>{});
+    if (H == 2) return launch(k_block_tiny<16, true>, TinyCfgT<true>{});
+    return launch(k_block_tiny<32, true>, TinyCfgT<true>{});
+  }
+  if (H == 4) return launch(k_block_tiny<8, false>, TinyCfg{});
+  if (H == 2) return launch(k_block_tiny<16, false>, TinyCfg{});
+  return launch(k_block_tiny<32, false>, TinyCfg{});
 }
 
 int fused_small_impl(const B200FusedSmallArgs* a, cudaStream_t st) {

@@ -56,10 +56,15 @@ struct TinyParams {
 // floats of a [rows][ld] weight staged with 4 floats of padding after every 4 rows
 constexpr int tiny_padded(int rows, int ld) { return rows * ld + (rows / 4) * 4; }
 
-struct TinyCfg {
+// SPLIT: a cluster of two CTAs per sequence, each owning 64 of its rows (the
+// K / V rows the other CTA needs cross over distributed shared memory)
+template <bool SPLIT>
+struct TinyCfgT {
   static constexpr int D = 32;
-  static constexpr int S = 128;          // rows per CTA
-  static constexpr int THREADS = 4 * S;  // an octet (8 threads) per row pair
+  static constexpr int S = 128;                 // rows per sequence
+  static constexpr int RL = SPLIT ? 64 : 128;   // rows owned by a CTA
+  static constexpr int THREADS = 4 * RL;        // an octet (8 threads) per row pair
+  static constexpr int KVB = SPLIT ? 2 : 1;     // K / V buffers (by layer parity when split)
   static constexpr int FMAX = 128;
   static constexpr int LD = D + 4;       // row stride (floats) of the K / V / row buffers
   static constexpr int HL = FMAX + 4;    // row stride of the hidden-unit buffer
@@ -71,25 +76,26 @@ struct TinyCfg {
   static constexpr int VEC = W_OUT + tiny_padded(D, FMAX);         // ln1 w,b | b_qkv | b_o | ln2 w,b | b_in | b_out
   static constexpr int V_LN1W = 0, V_LN1B = 32, V_BQKV = 64, V_BO = 160, V_LN2W = 192, V_LN2B = 224, V_BIN = 256,
                        V_BOUT = 256 + FMAX, V_TOTAL = 288 + FMAX;
-  static constexpr int KS = VEC + V_TOTAL;              // [S][LD] keys
-  static constexpr int VS = KS + S * LD;                // [S][LD] values
-  static constexpr int NB = VS + S * LD;                // [S][LD] a row's LN output, then Q, then the context
-  static constexpr int HB = NB + S * LD;                // [S][HL] GELU(hidden units)
+  static constexpr int KS = VEC + V_TOTAL;              // [KVB][S][LD] keys
+  static constexpr int VS = KS + KVB * S * LD;          // [KVB][S][LD] values
+  static constexpr int NB = VS + KVB * S * LD;          // [RL][LD] a row's LN output, then Q, then the context
+  static constexpr int HB = NB + RL * LD;               // [RL][HL] GELU(hidden units)
   // the next layer's fp16 weights and fp32 vectors as they arrive by bulk copy
   // (row-major, unpadded; the vectors in the VEC layout), converted into the
   // regions above at the layer boundary
-  static constexpr int STG_QKV = HB + S * HL;           // [96][32] fp16
+  static constexpr int STG_QKV = HB + RL * HL;          // [96][32] fp16
   static constexpr int STG_O = STG_QKV + 3 * D * D / 2; // [32][32] fp16
   static constexpr int STG_IN = STG_O + D * D / 2;      // [ffn][32] fp16
   static constexpr int STG_OUT = STG_IN + FMAX * D / 2; // [32][ffn] fp16
   static constexpr int STG_VEC = STG_OUT + D * FMAX / 2;
-  static constexpr int BAR = STG_VEC + V_TOTAL;         // mbarrier (8 bytes) + abort flag
-  static constexpr int TOTAL_FLOATS = BAR + 4;
+  static constexpr int BAR = STG_VEC + V_TOTAL;         // weight mbarrier, abort flag, 2 exchange mbarriers
+  static constexpr int TOTAL_FLOATS = BAR + 8;
   static constexpr int TOTAL = TOTAL_FLOATS * 4;
   static_assert(TOTAL <= 232448, "shared memory");
   static_assert(KS % 4 == 0 && NB % 4 == 0 && HB % 4 == 0 && STG_QKV % 4 == 0 && STG_VEC % 4 == 0 && BAR % 2 == 0,
                 "16-byte aligned regions");
 };
+using TinyCfg = TinyCfgT<false>;
 
 // offset (floats) of row `row` of a weight staged with row stride ld (padded layout)
 __device__ __forceinline__ int tiny_row(int row, int ld) { return row * ld + (row >> 2) * 4; }
@@ -181,7 +187,7 @@ __device__ __forceinline__ void tiny_out4(const uint64_t (&acc)[2][N], int r, in
 // fp16 weight [rows][ld] (shared memory, as staged) -> fp32 shared memory in the
 // padded layout (ld a multiple of 8), all threads of the CTA
 __device__ __forceinline__ void tiny_stage_f16(float* dst, const __half* src, int rows, int ld) {
-  for (int i = static_cast<int>(threadIdx.x) * 8; i < rows * ld; i += TinyCfg::THREADS * 8) {
+  for (int i = static_cast<int>(threadIdx.x) * 8; i < rows * ld; i += static_cast<int>(blockDim.x) * 8) {
     const uint4 t = *reinterpret_cast<const uint4*>(src + i);
     const __half2* h2 = reinterpret_cast<const __half2*>(&t);
     const float2 f0 = __half22float2(h2[0]), f1 = __half22float2(h2[1]), f2 = __half22float2(h2[2]),
@@ -193,7 +199,8 @@ __device__ __forceinline__ void tiny_stage_f16(float* dst, const __half* src, in
 }
 
 // Attention of an octet's rows for head_dim HD; thread u of the octet whose row pair
-// starts at r0.  Q of the rows is in NB (its columns head*HD..); the context of
+// starts at r0 (nbp: the pair's two rows of NB; ks / vs: the key and value rows of
+// the sequence).  Q of the rows is in NB (its columns head*HD..); the context of
 // each (row, head) goes back to the same place.  Head_dim 8: a thread takes both
 // rows of the pair, one head and alternate keys (one K / V load serves two rows);
 // head_dim 16 / 32: one row, one head and every 2nd / 4th key.  Online softmax in
@@ -202,7 +209,8 @@ __device__ __forceinline__ void tiny_stage_f16(float* dst, const __half* src, in
 // validity words, bit i of word w = key 32w + i exists and is not padding);
 // masked keys are skipped, never weighted by zero.
 template <int HD>
-__device__ __forceinline__ void tiny_attention(float* sm, int u, int r0, const uint32_t (&kw)[4],
+__device__ __forceinline__ void tiny_attention(const float* ks, const float* vs, float* nbp, int u, int r0,
+                                               const uint32_t (&kw)[4],
                                                const TinyParams& p) {
   using C = TinyCfg;
   constexpr int H = C::D / HD;
@@ -219,7 +227,7 @@ __device__ __forceinline__ void tiny_attention(float* sm, int u, int r0, const u
   float m[R], l[R];
 #pragma unroll
   for (int rr = 0; rr < R; ++rr) {
-    const float* qr = sm + C::NB + (rbase + rr) * C::LD + head * HD;
+    const float* qr = nbp + (rbase - r0 + rr) * C::LD + head * HD;
 #pragma unroll
     for (int e = 0; e < HD; e += 4) {
       const float4 a = *reinterpret_cast<const float4*>(qr + e);
@@ -243,7 +251,7 @@ __device__ __forceinline__ void tiny_attention(float* sm, int u, int r0, const u
 #pragma unroll
       for (int rr = 0; rr < R; ++rr) acc[rr] = -INFINITY;
       if (j < kend && ((word >> (jj * T)) & 1u)) {
-        const float* kr = sm + C::KS + j * C::LD + head * HD;
+        const float* kr = ks + j * C::LD + head * HD;
         uint64_t a2[R];
 #pragma unroll
         for (int rr = 0; rr < R; ++rr) a2[rr] = 0ull;
@@ -287,7 +295,7 @@ __device__ __forceinline__ void tiny_attention(float* sm, int u, int r0, const u
 #pragma unroll
       for (int rr = 0; rr < R; ++rr) any |= s[rr][jj] != -INFINITY;
       if (any) {
-        const float* vr = sm + C::VS + (kb + sub + jj * T) * C::LD + head * HD;
+        const float* vr = vs + (kb + sub + jj * T) * C::LD + head * HD;
 #pragma unroll
         for (int rr = 0; rr < R; ++rr) {
           // a masked score gives 0 here (exp2(-inf)) without touching l or o below
@@ -348,7 +356,7 @@ __device__ __forceinline__ void tiny_attention(float* sm, int u, int r0, const u
   }
   __syncwarp();  // every thread of the octet has read its Q
   const uint64_t inv2 = f2pk(inv, inv);
-  float* dst = sm + C::NB + (rbase + rw) * C::LD + head * HD + 8 * dc;
+  float* dst = nbp + (rbase - r0 + rw) * C::LD + head * HD + 8 * dc;
   float v[8];
 #pragma unroll
   for (int e = 0; e < 4; ++e) f2upk(f2mul(w[e], inv2), v[2 * e], v[2 * e + 1]);
@@ -356,9 +364,19 @@ __device__ __forceinline__ void tiny_attention(float* sm, int u, int r0, const u
   *reinterpret_cast<float4*>(dst + 4) = make_float4(v[4], v[5], v[6], v[7]);
 }
 
-template <int HD>
-__global__ void __launch_bounds__(TinyCfg::THREADS, 1) k_block_tiny(const TinyParams p) {
-  using C = TinyCfg;
+// SPLIT = false: one CTA per sequence (grid = sequences).  SPLIT = true: a cluster
+// of two CTAs per sequence (grid = 2 x sequences, cluster dims 2): half 0 owns
+// rows 0-31 and 96-127, half 1 rows 32-95 (equal causal work).  Each half
+// computes K and V of its own rows and also stores the ones the other half
+// attends to (half 1 needs keys 0-31, or all when non-causal; half 0 keys 32-95) into that CTA's
+// shared memory, then arrives on the other CTA's exchange mbarrier (release at
+// cluster scope) and waits, bounded, on its own.  The K / V buffers alternate by
+// layer parity, so a half can write layer l+1's rows while the other still
+// reads layer l's: it gets there only after the other half's layer-l arrival,
+// which follows that half's layer-(l-1) attention.
+template <int HD, bool SPLIT>
+__global__ void __launch_bounds__(TinyCfgT<SPLIT>::THREADS, 1) k_block_tiny(const TinyParams p) {
+  using C = TinyCfgT<SPLIT>;
   static_assert(HD == 8 || HD == 16 || HD == 32, "head_dim 8, 16 or 32");
   extern __shared__ float4 smem_f4[];
   float* sm = reinterpret_cast<float*>(smem_f4);
@@ -368,20 +386,30 @@ __global__ void __launch_bounds__(TinyCfg::THREADS, 1) k_block_tiny(const TinyPa
   // warp w holds the 8-row block b(w), the octet rows b(w)*8 + 2k, + 1.  Warps
   // w, w+4, w+8, w+12 share a scheduler; giving them blocks s, 7-s, 8+s, 15-s
   // (s = w % 4) balances the causal attention work across the four schedulers
+  // (split: blocks s, 15-s for half 0 and 4+s, 11-s for half 1)
   const int wid = static_cast<int>(threadIdx.x >> 5), ws = wid & 3, wt = wid >> 2;
-  const int rblk = wt == 0 ? ws : wt == 1 ? 7 - ws : wt == 2 ? 8 + ws : 15 - ws;
+  uint32_t half = 0;
+  int rblk;
+  if constexpr (SPLIT) {
+    half = cluster_ctarank();
+    rblk = half == 0 ? (wt == 0 ? ws : 15 - ws) : (wt == 0 ? 4 + ws : 11 - ws);
+  } else {
+    rblk = wt == 0 ? ws : wt == 1 ? 7 - ws : wt == 2 ? 8 + ws : 15 - ws;
+  }
   const int r0 = rblk * 8 + static_cast<int>((threadIdx.x >> 3) & 3) * 2;  // the octet's row pair r0, r0 + 1
-  const int seq = blockIdx.x;
+  const int lr0 = static_cast<int>(threadIdx.x >> 3) * 2;  // its rows in NB / HB (private to the octet)
+  const int seq = SPLIT ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
   const int F = p.ffn;
   const bool ok0 = r0 < p.seq_len, ok1 = r0 + 1 < p.seq_len;
   const int64_t g0 = static_cast<int64_t>(seq) * p.seq_len + r0;  // global row of r0
   float* vec = sm + C::VEC;
-  float* nb0 = sm + C::NB + r0 * C::LD;
+  float* nb0 = sm + C::NB + lr0 * C::LD;
   float* nb1 = nb0 + C::LD;
-  float* hb0 = sm + C::HB + r0 * C::HL;
+  float* hb0 = sm + C::HB + lr0 * C::HL;
   float* hb1 = hb0 + C::HL;
   uint64_t* wbar = reinterpret_cast<uint64_t*>(sm + C::BAR);  // a layer's staged weights and vectors
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + C::BAR + 2);
+  uint64_t* xbar = reinterpret_cast<uint64_t*>(sm + C::BAR + 4);  // [2] the other half's K / V rows, by layer parity
   // one thread copies layer l's weights and vectors into the staging area (twelve bulk
   // copies, one mbarrier phase): issued a layer ahead, so the HBM / L2 round trip
   // overlaps the previous layer's arithmetic instead of stalling every boundary
@@ -405,11 +433,23 @@ __global__ void __launch_bounds__(TinyCfg::THREADS, 1) k_block_tiny(const TinyPa
   };
   if (threadIdx.x == 0) {
     mbar_init(wbar, 1);
+    if (SPLIT) {
+      mbar_init(&xbar[0], C::THREADS);  // every thread of the other half arrives once per layer
+      mbar_init(&xbar[1], C::THREADS);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
   __syncthreads();
   if (threadIdx.x == 0) fetch(0);
+  // shared::cluster addresses of the other half's K / V buffers and exchange barriers
+  uint32_t peer_ks = 0, peer_vs = 0, peer_xbar = 0;
+  if constexpr (SPLIT) {
+    cluster_sync_all();  // both halves' barriers are initialised before any remote arrival
+    peer_ks = mapa_shared(smem_u32(sm + C::KS), half ^ 1u);
+    peer_vs = mapa_shared(smem_u32(sm + C::VS), half ^ 1u);
+    peer_xbar = mapa_shared(smem_u32(xbar), half ^ 1u);
+  }
   // key validity as four 32-bit words in registers (lane i tests key 32w + i)
   uint32_t kw[4];
 #pragma unroll
@@ -449,6 +489,9 @@ __global__ void __launch_bounds__(TinyCfg::THREADS, 1) k_block_tiny(const TinyPa
     }
     __syncwarp();
     // ---- QKV: columns 4u..4u+3 of Q, K and V for both rows; Q -> NB, K / V -> KS / VS
+    const int kvo = SPLIT ? (l & 1) * C::S * C::LD : 0;  // this layer's K / V buffer
+    float* ksl = sm + C::KS + kvo;
+    float* vsl = sm + C::VS + kvo;
     {
       uint64_t acc[2][12];
       tiny_zero(acc);
@@ -459,18 +502,27 @@ __global__ void __launch_bounds__(TinyCfg::THREADS, 1) k_block_tiny(const TinyPa
       st4(nb0 + 4 * u, o);
       tiny_out4(acc, 1, 0, vec + C::V_BQKV + 4 * u, o);
       st4(nb1 + 4 * u, o);
-      tiny_out4(acc, 0, 1, vec + C::V_BQKV + 32 + 4 * u, o);
-      st4(sm + C::KS + r0 * C::LD + 4 * u, o);
-      tiny_out4(acc, 1, 1, vec + C::V_BQKV + 32 + 4 * u, o);
-      st4(sm + C::KS + (r0 + 1) * C::LD + 4 * u, o);
-      tiny_out4(acc, 0, 2, vec + C::V_BQKV + 64 + 4 * u, o);
-      st4(sm + C::VS + r0 * C::LD + 4 * u, o);
-      tiny_out4(acc, 1, 2, vec + C::V_BQKV + 64 + 4 * u, o);
-      st4(sm + C::VS + (r0 + 1) * C::LD + 4 * u, o);
+      // the other half attends to these rows: half 1 needs keys 0-31 (all keys when
+      // non-causal), half 0 keys 32-95
+      const bool send = SPLIT && (half == 1 || r0 < 32 || p.non_causal);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {  // K row r0, K row r0+1, V row r0, V row r0+1
+        tiny_out4(acc, t & 1, 1 + (t >> 1), vec + C::V_BQKV + 32 * (1 + (t >> 1)) + 4 * u, o);
+        const int off = kvo + (r0 + (t & 1)) * C::LD + 4 * u;
+        st4(sm + ((t >> 1) ? C::VS : C::KS) + off, o);
+        if (send)
+          st_cluster_f4(((t >> 1) ? peer_vs : peer_ks) + 4u * static_cast<uint32_t>(off), make_float4(o[0], o[1], o[2], o[3]));
+      }
     }
-    __syncthreads();  // every row's K and V are in place
+    bool have_kv = true;
+    if constexpr (SPLIT) {
+      mbar_arrive_cluster(peer_xbar + 8u * static_cast<uint32_t>(l & 1));
+      have_kv = mbar_wait_cluster(&xbar[l & 1], static_cast<uint32_t>((l >> 1) & 1), abort_flag, DERR_WAIT_GRID);
+    }
+    // every row's K and V are in place (a bounded exchange wait that gave up ends the CTA)
+    if (__syncthreads_or(!have_kv)) return;
     // ---- attention -> the context in NB
-    tiny_attention<HD>(sm, u, r0, kw, p);
+    tiny_attention<HD>(ksl, vsl, nb0, u, r0, kw, p);
     __syncwarp();
     // ---- out_proj + residual; LN2 -> NB
     {

@@ -168,3 +168,46 @@ def test_tiny_model_single_kernel_vs_oracle(tt, B, S, H, F, L, causal, pad):
     res = oracle.compare_outputs(ref, y[:nb], rtol=RTOL, atol=ATOL)
     print(f"tiny B{B} S{S} H{H} F{F} L{L}: max_abs={res.max_abs_error:.3g}")
     assert res.passed, res
+
+
+@pytest.mark.parametrize("mode", ["0", "1"])
+def test_tiny_single_cta_and_cluster_split_in_subprocess(mode):
+    """d_model = 32 with one CTA per sequence and with a two-CTA cluster per
+    sequence (each half finishing 64 query rows, K / V rows exchanged through
+    distributed shared memory; B200_TINY_SPLIT forces the choice and is read once
+    per process, hence the child process) against the oracle: 1, 2 and 4 heads,
+    several layers (the exchange buffers alternate by layer), ragged S, key
+    padding, non-causal, and more clusters than fit on the GPU at once."""
+    import os
+    import subprocess
+    import sys
+    code = r'''
+import torch
+import oracle
+import torch_transformer_benchmark as tt
+rt = tt._pkg.runtime
+DEV = "cuda"
+for (B, S, H, F, L, causal, pad) in ((64, 128, 4, 32, 4, True, 0.0), (3, 100, 2, 64, 3, True, 0.0),
+                                     (5, 128, 1, 128, 2, True, 0.25), (4, 77, 4, 96, 3, False, 0.3),
+                                     (2, 33, 4, 32, 5, True, 0.0), (160, 128, 4, 64, 2, True, 0.1)):
+    cfg = tt.TransformerConfig(B, S, 32, H, F, L, causal)
+    torch.manual_seed(B * 5 + H + F + L)
+    model = tt.UserOptimizedTransformer(cfg).to(DEV).eval()
+    x, mask = oracle.generate_random_case(B, S, 32, B + S + F + L, padding_ratio=pad)
+    m = mask if pad > 0 else None
+    with torch.inference_mode():
+        y = model(x.to(DEV), None if m is None else m.to(DEV)).cpu()
+    assert model.last_strategy == "fused_small"
+    assert rt.device_error(clear=True) == 0
+    params = oracle.params_from_state_dict(model.state_dict())
+    for lo, hi in ((0, min(B, 8)), (max(B - 4, 0), B)):
+        ref = oracle.model_forward(params, oracle.OracleConfig(hi - lo, S, 32, H, F, L, causal), x[lo:hi].numpy(),
+                                   None if m is None else m[lo:hi].numpy())
+        res = oracle.compare_outputs(ref, y[lo:hi], rtol=0.02, atol=0.002)
+        assert res.passed, (B, S, H, F, L, causal, pad, res)
+print("OK")
+'''
+    env = dict(os.environ, B200_TINY_SPLIT=mode)
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and "OK" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
