@@ -48,6 +48,10 @@ CONFIGS = {
     "C4a": (64, 1024, 128, 4, 512, 1),
     "C4b": (64, 128, 1024, 4, 4096, 1),
     "C5": (32, 100000, 1024, 16, 4096, 1),
+    # rows 7 and 11 of the reference's official matrix (run_eval.sh:44-58: 4 layers,
+    # ffn = d): optional workloads for the d=32 kernel and head_dim-8 attention
+    "M7": (64, 128, 32, 4, 32, 4),
+    "M11": (64, 128, 128, 16, 128, 4),
 }
 # C5 keeps the global batch (B=32) fixed and splits it across the ranks (strong scaling)
 STRONG = {"C5"}
