@@ -708,8 +708,8 @@ int fused_small_impl(const B200FusedSmallArgs* a, cudaStream_t st) {
     if (int rc = check_arch()) return rc;
     return fused_tiny_impl(a, st);
   }
-  if (a->d_model != 128 || a->num_heads != 4 || a->ffn_dim <= 0 || a->ffn_dim % 128 || a->ffn_dim > 512 ||
-      a->seq_len > 128)
+  if (a->d_model != 128 || (a->num_heads != 1 && a->num_heads != 2 && a->num_heads != 4) || a->ffn_dim <= 0 ||
+      a->ffn_dim % 128 || a->ffn_dim > 512 || a->seq_len > 128)
     return B200_ERR_CONFIG;
   if (a->x == a->y) return B200_ERR_ARG;
   if (!al16(a->x) || !al16(a->y) || !al16(a->w_qkv) || !al16(a->w_o) || !al16(a->w_in) || !al16(a->w_out))
@@ -745,7 +745,8 @@ int fused_small_impl(const B200FusedSmallArgs* a, cudaStream_t st) {
   p.lnf_w = a->lnf_w;
   p.lnf_b = a->lnf_b;
   p.eps = a->eps;
-  p.scale_log2 = static_cast<float>(1.4426950408889634 / __builtin_sqrt(32.0));
+  p.heads = a->num_heads;
+  p.scale_log2 = static_cast<float>(1.4426950408889634 / __builtin_sqrt(128.0 / a->num_heads));
   p.row_valid = static_cast<const unsigned char*>(a->row_valid);
   p.non_causal = a->non_causal;
   const int smem = SmallCfg::TOTAL;

@@ -54,6 +54,7 @@ struct SmallParams {
   int seq_len;        // rows per sequence (<= 128)
   int layers;
   int ffn;            // multiple of 128, <= 512
+  int heads;          // 1, 2 or 4 (head_dim 128, 64 or 32)
   const float* x;     // [num_seq*seq_len, 128]
   float* y;           // [num_seq*seq_len, 128]
   const float* ln1_w; const float* ln1_b;   // [layers, 128]
@@ -64,7 +65,7 @@ struct SmallParams {
   const float* b_out;                       // [layers, 128]
   const float* lnf_w; const float* lnf_b;   // [128]
   float eps;
-  float scale_log2;   // 32^-0.5 * log2(e)
+  float scale_log2;   // head_dim^-0.5 * log2(e)
   const unsigned char* row_valid;  // [num_seq*seq_len] key-padding mask (0 = padded row), may be null
   int non_causal;                  // 1: every query sees every valid key
 };
@@ -351,11 +352,15 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
           release(src);
         }
       };
+      // head h spans the 32-column Q / K / V tiles gpb*h .. gpb*h + gpb - 1 (SW64, one
+      // per column group): S = Q.K^T takes two K=16 steps per tile
+      const int H = p.heads, gpb = 4 / H;
       auto issue_s = [&](int h) {
-#pragma unroll
-        for (int kk = 0; kk < 2; ++kk)
-          umma_f16_ss(tmem + (h & 1) * 128, make_sdesc(qs + h * 8192 + kk * 32, 16, 512, UMMA_SW64),
-                      make_sdesc(ks + h * 8192 + kk * 32, 16, 512, UMMA_SW64), ID_N128, kk ? 1u : 0u);
+        for (int kk = 0; kk < 2 * gpb; ++kk) {
+          const uint32_t off = static_cast<uint32_t>((gpb * h + (kk >> 1)) * 8192 + (kk & 1) * 32);
+          umma_f16_ss(tmem + (h & 1) * 128, make_sdesc(qs + off, 16, 512, UMMA_SW64),
+                      make_sdesc(ks + off, 16, 512, UMMA_SW64), ID_N128, kk ? 1u : 0u);
+        }
         tc_commit(&bar[SB_S_FULL + (h & 1)]);
       };
       for (int step = 0; ok && step < nsteps; ++step) {
@@ -375,20 +380,22 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
         if (!mbar_wait(&bar[SB_QKV_SMEM], par(step, 1, 0), abort_flag, DERR_WAIT_SOFTMAX)) break;
         tc_fence_after();
         issue_s(0);
-        issue_s(1);
-        for (int h = 0; h < 4 && ok; ++h) {
-          if (!mbar_wait(&bar[SB_P_FULL], par(step, 4, h), abort_flag, DERR_WAIT_SOFTMAX)) {
+        if (H > 1) issue_s(1);
+        for (int h = 0; h < H && ok; ++h) {
+          if (!mbar_wait(&bar[SB_P_FULL], par(step, H, h), abort_flag, DERR_WAIT_SOFTMAX)) {
             ok = false;
             break;
           }
           tc_fence_after();
+          for (int t = gpb * h; t < gpb * (h + 1); ++t) {  // O columns 32t.. from V tile t
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            umma_f16_ss(tmem + 256 + 32 * h,
-                        make_sdesc(ps + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024, UMMA_SW128),
-                        make_sdesc(vs + h * 8192 + kk * 16 * 64, 128 * 64, 512, UMMA_SW64), ID_PV, kk ? 1u : 0u);
+            for (int kk = 0; kk < 8; ++kk)
+              umma_f16_ss(tmem + 256 + 32 * t,
+                          make_sdesc(ps + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024, UMMA_SW128),
+                          make_sdesc(vs + t * 8192 + kk * 16 * 64, 128 * 64, 512, UMMA_SW64), ID_PV, kk ? 1u : 0u);
+          }
           tc_commit(&bar[SB_PV_DONE]);
-          if (h + 2 < 4) issue_s(h + 2);
+          if (h + 2 < H) issue_s(h + 2);
         }
         if (!ok) break;
         // out_proj
@@ -441,6 +448,12 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
     float* st1 = stats + 512;
     float* st2 = stats + 1024;           // second halves of the merged (max, sum) reductions
     float* st3 = stats + 1536;
+    // heads: H of head_dim 128 / H; column group g (32 columns) belongs to head hg.
+    // The last head's row sum goes to st_f, the buffer its max did not use, and the
+    // LayerNorms after it take (st_o, st_f), so consecutive reductions still alternate.
+    const int H = p.heads, hg = g / (4 / H);
+    float* st_f = ((H - 1) & 1) ? st0 : st1;
+    float* st_o = ((H - 1) & 1) ? st1 : st0;
     float* vec = reinterpret_cast<float*>(smem + C::OFF_VEC);
     const int wtid = threadIdx.x - 64;   // 0..511 among the workers
     uint8_t* xa = smem + C::OFF_XA;
@@ -601,11 +614,11 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
           kvalid = __ballot_sync(0xffffffffu, v_ok);
         }
         if (!p.non_causal) kvalid &= (r >= c0 + 31) ? 0xffffffffu : (r < c0 ? 0u : (0xffffffffu >> (31 - (r - c0))));
-        float my_l = 1.f;  // softmax denominator of head g (this thread's head in the context step)
+        float my_l = 1.f;  // softmax denominator of head hg (this thread's head in the context step)
         float prev_sum = 0.f;  // this thread's partial row sum of the previous head
 #pragma unroll 1
-        for (int h = 0; h < 4; ++h) {
-          wait_w(SB_S_FULL + (h & 1), par(step, 2, h >> 1));
+        for (int h = 0; h < H; ++h) {
+          wait_w(SB_S_FULL + (h & 1), par(step, (h & 1) ? H / 2 : (H + 1) / 2, h >> 1));
           if (ok) tmem_ld32(trow + (h & 1) * 128 + c0, v);
           if (kvalid != 0xffffffffu) {  // raw scores; the positive scale is applied in the exponent
 #pragma unroll
@@ -618,7 +631,7 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
           // head h's max with head h-1's sum; the pairs alternate (st0, st2) / (st1, st3)
           float m, lprev;
           row_max_sum(mx, prev_sum, (h & 1) ? st1 : st0, (h & 1) ? st3 : st2, m, lprev);
-          if (h > 0 && h - 1 == g) my_l = lprev;
+          if (h > 0 && h - 1 == hg) my_l = lprev;
           m *= p.scale_log2;
           const uint64_t sc = f2pk(p.scale_log2, p.scale_log2), nm = f2pk(-m, -m);
           uint64_t a0 = f2pk(0.f, 0.f), a1 = a0;
@@ -636,16 +649,16 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
           f2upk(a1, t2, t3);
           prev_sum = (t0 + t2) + (t1 + t3);
           // P of the previous head must have been consumed before P is overwritten
-          if (h > 0) wait_w(SB_PV_DONE, par(step, 4, h - 1));
+          if (h > 0) wait_w(SB_PV_DONE, par(step, H, h - 1));
           store_sw128(smem + C::OFF_P);
           publish(SB_P_FULL);
         }
         {
-          const float l3 = row_sum(prev_sum, st0);  // head 3's sum (after (st1, st3) above)
-          if (g == 3) my_l = l3;
+          const float lf = row_sum(prev_sum, st_f);  // the last head's sum
+          if (hg == H - 1) my_l = lf;
         }
-        // ---- W4: context = O_g / l_g -> XA (head g's 32 columns)
-        wait_w(SB_PV_DONE, par(step, 4, 3));
+        // ---- W4: context = O / l of head hg -> XA (this thread's 32 columns)
+        wait_w(SB_PV_DONE, par(step, H, H - 1));
         if (ok) tmem_ld32(trow + 256 + c0, v);
         {
           const float inv = 1.f / my_l;
@@ -660,7 +673,7 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
         if (ok) tmem_ld32(trow + 384 + c0, v);
         f2_add_bias32(v, vec + C::V_BO + c0);
         if (ok) tmem_st32(trow + 384 + c0, v);
-        layer_norm(vec + C::V_LN2W, vec + C::V_LN2B, -1, st1, st0);  // after st0 (head 3's sum)
+        layer_norm(vec + C::V_LN2W, vec + C::V_LN2B, -1, st_o, st_f);  // after st_f (the last head's sum)
         store_sw128(xa);
         publish(SB_N2);
         // ---- W6: GELU chunks -> H ping-pong
@@ -682,7 +695,7 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
         if (ok) tmem_ld32(trow + 384 + c0, v);
         f2_add_bias32(v, vec + C::V_BOUT + c0);
         if (l == p.layers - 1) {
-          layer_norm(vec + C::V_LNFW, vec + C::V_LNFB, -1, st1, st0);  // after st0 (LN2's variance)
+          layer_norm(vec + C::V_LNFW, vec + C::V_LNFB, -1, st_o, st_f);  // after st_f (LN2's variance)
           // padded rows of the model output are zero (with causal attention and prefix-valid
           // padding the valid rows never see a padded key, so only the output needs masking)
           const bool zero = row_ok && p.row_valid != nullptr && p.row_valid[grow] == 0;
@@ -858,11 +871,11 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
         kvalid = (__ballot_sync(0xffffffffu, v_ok) >> (16 * hh)) & 0xffffu;
       }
       if (!p.non_causal) kvalid &= (srow >= cc + 15) ? 0xffffu : (srow < cc ? 0u : (0xffffu >> (15 - (srow - cc))));
-      float my_l = 1.f;  // softmax denominator of head g
+      float my_l = 1.f;  // softmax denominator of head hg
       float prev_sum = 0.f;  // the previous head's partial row sum, reduced with this head's max
 #pragma unroll 1
-      for (int h = 0; h < 4; ++h) {
-        wait_w(SB_S_FULL + (h & 1), par(0, 2, h >> 1));
+      for (int h = 0; h < H; ++h) {
+        wait_w(SB_S_FULL + (h & 1), par(0, (h & 1) ? H / 2 : (H + 1) / 2, h >> 1));
         if (ok) tmem_ld32(trow + (h & 1) * 128 + c0, v);
         take_half();
         if (kvalid != 0xffffu) {
@@ -875,7 +888,7 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
         for (int i = 0; i < 16; i += 2) mx = fmax3(mx, u[i], u[i + 1]);
         float m, lprev;
         own_max_sum(mx, prev_sum, (h & 1) ? st1 : st0, m, lprev);  // reductions alternate st0/st1 strictly
-        if (h > 0 && h - 1 == g) my_l = lprev;
+        if (h > 0 && h - 1 == hg) my_l = lprev;
         m *= p.scale_log2;
         const uint64_t sc = f2pk(p.scale_log2, p.scale_log2), nm = f2pk(-m, -m);
         uint64_t a0 = f2pk(0.f, 0.f), a1 = a0;
@@ -892,17 +905,17 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
         f2upk(a0, t0, t1);
         f2upk(a1, t2, t3);
         const float sum = (t0 + t2) + (t1 + t3);
-        if (h > 0) wait_w(SB_PV_DONE, par(0, 4, h - 1));  // P of the previous head consumed
+        if (h > 0) wait_w(SB_PV_DONE, par(0, H, h - 1));  // P of the previous head consumed
         store16_sw128(smem + C::OFF_P);
         publish(SB_P_FULL);
         prev_sum = sum;
       }
       {
-        const float l3 = own_sum(prev_sum, st0);  // head 3 (after st1 above)
-        if (g == 3) my_l = l3;
+        const float lf = own_sum(prev_sum, st_f);  // the last head's sum
+        if (hg == H - 1) my_l = lf;
       }
-      // ---- W4: context (16 columns of head g) = O / l -> XA
-      wait_w(SB_PV_DONE, par(0, 4, 3));
+      // ---- W4: context (16 columns of head hg) = O / l -> XA
+      wait_w(SB_PV_DONE, par(0, H, H - 1));
       if (ok) tmem_ld32(trow + 256 + c0, v);
       take_half();
       {
@@ -919,7 +932,7 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
       if (ok) tmem_ld32(trow + 384 + c0, v);
       take_half();
       add16(vec + C::V_BO + cc);
-      layer_norm16(vec + C::V_LN2W, vec + C::V_LN2B, st1, st0);  // after st0 (the last softmax sum)
+      layer_norm16(vec + C::V_LN2W, vec + C::V_LN2B, st_o, st_f);  // after st_f (the last softmax sum)
       store16_sw128(xa);
       publish(SB_N2);
       // ---- W6: GELU chunks -> H ping-pong
@@ -942,7 +955,7 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
       take_half();
       add16(vec + C::V_BO + cc);
       add16(vec + C::V_BOUT + cc);
-      layer_norm16(vec + C::V_LNFW, vec + C::V_LNFB, st1, st0);
+      layer_norm16(vec + C::V_LNFW, vec + C::V_LNFB, st_o, st_f);
       {
         const bool zero = srow < p.seq_len && p.row_valid != nullptr && p.row_valid[srow_g] == 0;
         // the warp's own rows are 16 consecutive sequence rows: one 16x32 box, staged SW128

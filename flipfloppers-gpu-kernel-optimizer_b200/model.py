@@ -273,10 +273,10 @@ class UserOptimizedTransformer(nn.Module):
 
     def _fused_small_eligible(self) -> bool:
         """Shapes the single-kernel whole-model path takes: the tensor-core kernels
-        (d_model 128, 4 heads, ffn <= 512) and the CUDA-core one (d_model 32, 1, 2 or
-        4 heads, ffn <= 128)."""
+        (d_model 128, 1, 2 or 4 heads, ffn <= 512) and the CUDA-core one (d_model 32,
+        1, 2 or 4 heads, ffn <= 128)."""
         c = self.config
-        big = c.d_model == 128 and c.num_heads == 4 and c.ffn_dim % 128 == 0 and c.ffn_dim <= 512
+        big = c.d_model == 128 and c.num_heads in (1, 2, 4) and c.ffn_dim % 128 == 0 and c.ffn_dim <= 512
         tiny = c.d_model == 32 and c.num_heads in (1, 2, 4) and c.ffn_dim % 32 == 0 and c.ffn_dim <= 128
         return (big or tiny) and _FUSED_SMALL_ON
 
@@ -284,7 +284,7 @@ class UserOptimizedTransformer(nn.Module):
         """Pick the execution strategy for a shape, once (keyed by shape only).
 
         * ``fused_small`` -- the whole model in one persistent kernel
-          (d_model=128, 4 heads, ffn<=512, seq_len<=128: every intermediate
+          (d_model=128, 1/2/4 heads, ffn<=512, seq_len<=128: every intermediate
           fits on chip);
         * ``chain`` -- per layer: LN, QKV GEMM, flash attention, out_proj GEMM
           (+residual), LN, ffn_in GEMM (+GELU), ffn_out GEMM (+residual), final
@@ -295,7 +295,7 @@ class UserOptimizedTransformer(nn.Module):
           ``B200_CHUNK_MEM_FRAC`` of the free device memory."""
         if self.force_strategy is not None:
             if self.force_strategy == "fused_small" and not (self._fused_small_eligible() and S <= 128):
-                raise ValueError("fused_small needs d_model=128, 4 heads, ffn_dim<=512 (multiple of 128) or d_model=32, "
+                raise ValueError("fused_small needs d_model=128, 1/2/4 heads, ffn_dim<=512 (multiple of 128) or d_model=32, "
                                  "1/2/4 heads, ffn_dim<=128 (multiple of 32); seq_len<=128")
             if self.force_strategy == "chunked":
                 if not self.config.causal:

@@ -211,7 +211,7 @@ size_t b200_block_chunked_workspace_bytes(long long tokens, int chunk_rows, int 
 int b200_block_forward_chunked(const B200BlockArgs* args, int chunk_rows, b200_stream_t stream);
 
 /* Whole causal model (num_layers pre-LN blocks + final LayerNorm) in ONE
- * kernel, for small models: d_model == 128, num_heads == 4, ffn_dim a
+ * kernel, for small models: d_model == 128, num_heads 1, 2 or 4, ffn_dim a
  * multiple of 128 up to 512, seq_len <= 128 (tensor-core kernels: one
  * persistent CTA per sequence, or two CTAs per sequence for one layer and few
  * sequences), or d_model == 32, num_heads 1, 2 or 4, ffn_dim a multiple of 32

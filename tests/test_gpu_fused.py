@@ -139,6 +139,48 @@ print("OK")
     assert r.returncode == 0 and "OK" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
 
 
+@pytest.mark.parametrize("mode", ["0", "1"])
+def test_fused_one_and_two_heads_in_subprocess(mode):
+    """d_model = 128 with 1 or 2 heads (head_dim 128 / 64: S = Q.K^T over 8 / 4
+    K-steps, P.V into 4 / 2 32-column blocks per head) in the one-CTA and the
+    row-split kernel against the oracle: the reference matrix's shapes (4 layers,
+    ffn = d), ragged S with key padding, non-causal, ffn 512."""
+    import os
+    import subprocess
+    import sys
+    code = r'''
+import torch
+import oracle
+import torch_transformer_benchmark as tt
+rt = tt._pkg.runtime
+DEV = "cuda"
+for (B, S, H, F, L, causal, pad) in ((64, 128, 1, 128, 4, True, 0.0), (64, 128, 2, 128, 4, True, 0.0),
+                                     (5, 100, 1, 512, 1, True, 0.25), (6, 128, 2, 256, 1, True, 0.0),
+                                     (3, 77, 2, 384, 1, False, 0.3), (4, 128, 1, 128, 1, False, 0.0),
+                                     (200, 128, 2, 512, 1, True, 0.0), (3, 64, 1, 256, 2, True, 0.0)):
+    cfg = tt.TransformerConfig(B, S, 128, H, F, L, causal)
+    torch.manual_seed(B * 11 + H + F + L)
+    model = tt.UserOptimizedTransformer(cfg).to(DEV).eval()
+    x, mask = oracle.generate_random_case(B, S, 128, B + S + F + H, padding_ratio=pad)
+    m = mask if pad > 0 else None
+    with torch.inference_mode():
+        y = model(x.to(DEV), None if m is None else m.to(DEV)).cpu()
+    assert model.last_strategy == "fused_small"
+    assert rt.device_error(clear=True) == 0
+    params = oracle.params_from_state_dict(model.state_dict())
+    for lo, hi in ((0, min(B, 8)), (max(B - 4, 0), B)):
+        ref = oracle.model_forward(params, oracle.OracleConfig(hi - lo, S, 128, H, F, L, causal), x[lo:hi].numpy(),
+                                   None if m is None else m[lo:hi].numpy())
+        res = oracle.compare_outputs(ref, y[lo:hi], rtol=0.02, atol=0.002)
+        assert res.passed, (B, S, H, F, L, causal, pad, res)
+print("OK")
+'''
+    env = dict(os.environ, B200_SMALL_ROWS=mode)
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and "OK" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+
+
 TINY_CASES = [  # B, S, H, ffn, L, causal, padding ratio
     (64, 128, 4, 32, 4, True, 0.0),   # the reference's official matrix row 7
     (3, 100, 2, 64, 2, True, 0.0),
