@@ -754,20 +754,28 @@ int fused_small_impl(const B200FusedSmallArgs* a, cudaStream_t st) {
   // latency-bound per-row phases while the batch leaves SMs idle (measured
   // at C2: see DESIGN); one layer only, as each CTA rebuilds K/V from x.
   const int rows_mode = small_rows_mode();
-  if (L == 1 && rows_mode != 0 && (rows_mode == 1 || 2LL * a->batch <= num_sms()) && a->batch <= 0x3fffffff) {
-    CUtensorMap ty16;  // 16-row y boxes: a worker warp's own rows
+  const bool rows = L == 1 && rows_mode != 0 && (rows_mode == 1 || 2LL * a->batch <= num_sms()) &&
+                    a->batch <= 0x3fffffff;
+  CUtensorMap ty16;  // row-split mode: 16-row y boxes (a worker warp's own rows)
+  if (rows) {
     if (int rc = make_map_f32_seq(&ty16, a->y, a->batch, a->seq_len, 128, 16)) return rc;
-    if (int rc = set_smem(reinterpret_cast<const void*>(k_block_rows), smem)) return rc;
-    if (int rc = check_block_fits(reinterpret_cast<const void*>(k_block_rows), SmallCfg::THREADS)) return rc;
-    launch_kernel(k_block_rows, dim3(2 * a->batch), dim3(SmallCfg::THREADS), smem, st, tq, to, ti, tout, tx, ty16,
-                  p);
-    return launch_status();
   }
-  if (int rc = set_smem(reinterpret_cast<const void*>(k_block_small), smem)) return rc;
-  if (int rc = check_block_fits(reinterpret_cast<const void*>(k_block_small), SmallCfg::THREADS)) return rc;
-  const int grid = a->batch < num_sms() ? a->batch : num_sms();
-  launch_kernel(k_block_small, dim3(grid), dim3(SmallCfg::THREADS), smem, st, tq, to, ti, tout, tx, ty, p);
-  return launch_status();
+  auto launch = [&](auto k_small, auto k_rows) {
+    if (rows) {
+      if (int rc = set_smem(reinterpret_cast<const void*>(k_rows), smem)) return rc;
+      if (int rc = check_block_fits(reinterpret_cast<const void*>(k_rows), SmallCfg::THREADS)) return rc;
+      launch_kernel(k_rows, dim3(2 * a->batch), dim3(SmallCfg::THREADS), smem, st, tq, to, ti, tout, tx, ty16, p);
+      return launch_status();
+    }
+    if (int rc = set_smem(reinterpret_cast<const void*>(k_small), smem)) return rc;
+    if (int rc = check_block_fits(reinterpret_cast<const void*>(k_small), SmallCfg::THREADS)) return rc;
+    const int grid = a->batch < num_sms() ? a->batch : num_sms();
+    launch_kernel(k_small, dim3(grid), dim3(SmallCfg::THREADS), smem, st, tq, to, ti, tout, tx, ty, p);
+    return launch_status();
+  };
+  if (a->num_heads == 4) return launch(k_block_small<4>, k_block_rows<4>);
+  if (a->num_heads == 2) return launch(k_block_small<2>, k_block_rows<2>);
+  return launch(k_block_small<1>, k_block_rows<1>);
 }
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }

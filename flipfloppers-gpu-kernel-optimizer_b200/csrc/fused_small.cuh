@@ -133,8 +133,9 @@ __device__ __forceinline__ uint32_t par(int step, int per, int idx) {
 // The kernel body.  ROWS = false: one CTA per sequence (persistent over
 // sequences and layers).  ROWS = true: two CTAs per sequence, one layer (the
 // row-split mode, see k_block_rows); the producer and MMA roles are the same
-// in both modes, only the workers' phases differ.
-template <bool ROWS>
+// in both modes, only the workers' phases differ.  NH: heads (1, 2 or 4; a
+// compile-time constant so the per-head loops unroll as for a fixed shape).
+template <bool ROWS, int NH>
 __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, const CUtensorMap* tm_o,
                                                  const CUtensorMap* tm_in, const CUtensorMap* tm_out,
                                                  const CUtensorMap* tm_x, const CUtensorMap* tm_y,
@@ -354,8 +355,9 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
       };
       // head h spans the 32-column Q / K / V tiles gpb*h .. gpb*h + gpb - 1 (SW64, one
       // per column group): S = Q.K^T takes two K=16 steps per tile
-      const int H = p.heads, gpb = 4 / H;
+      constexpr int H = NH, gpb = 4 / NH;
       auto issue_s = [&](int h) {
+#pragma unroll
         for (int kk = 0; kk < 2 * gpb; ++kk) {
           const uint32_t off = static_cast<uint32_t>((gpb * h + (kk >> 1)) * 8192 + (kk & 1) * 32);
           umma_f16_ss(tmem + (h & 1) * 128, make_sdesc(qs + off, 16, 512, UMMA_SW64),
@@ -387,7 +389,9 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
             break;
           }
           tc_fence_after();
-          for (int t = gpb * h; t < gpb * (h + 1); ++t) {  // O columns 32t.. from V tile t
+#pragma unroll
+          for (int tt = 0; tt < gpb; ++tt) {  // O columns 32t.. from V tile t
+            const int t = gpb * h + tt;
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk)
               umma_f16_ss(tmem + 256 + 32 * t,
@@ -451,7 +455,8 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
     // heads: H of head_dim 128 / H; column group g (32 columns) belongs to head hg.
     // The last head's row sum goes to st_f, the buffer its max did not use, and the
     // LayerNorms after it take (st_o, st_f), so consecutive reductions still alternate.
-    const int H = p.heads, hg = g / (4 / H);
+    constexpr int H = NH;
+    const int hg = g / (4 / NH);
     float* st_f = ((H - 1) & 1) ? st0 : st1;
     float* st_o = ((H - 1) & 1) ? st1 : st0;
     float* vec = reinterpret_cast<float*>(smem + C::OFF_VEC);
@@ -985,24 +990,26 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
   }
 }
 
+template <int NH>
 __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
     k_block_small(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_o,
                   const __grid_constant__ CUtensorMap tm_in, const __grid_constant__ CUtensorMap tm_out,
                   const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_y,
                   const SmallParams p) {
-  block_small_body<false>(&tm_qkv, &tm_o, &tm_in, &tm_out, &tm_x, &tm_y, p);
+  block_small_body<false, NH>(&tm_qkv, &tm_o, &tm_in, &tm_out, &tm_x, &tm_y, p);
 }
 
 // Row-split mode for one layer and at most one sequence per two SMs: CTAs 2s
 // and 2s+1 both run sequence s, each finishing 64 of its query rows (tm_y has
 // 16-row boxes).  No data moves between the two CTAs: each computes LN1, K and
 // V for all 128 rows itself, which costs less than exchanging them.
+template <int NH>
 __global__ void __launch_bounds__(SmallCfg::THREADS, 1)
     k_block_rows(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_o,
                  const __grid_constant__ CUtensorMap tm_in, const __grid_constant__ CUtensorMap tm_out,
                  const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_y,
                  const SmallParams p) {
-  block_small_body<true>(&tm_qkv, &tm_o, &tm_in, &tm_out, &tm_x, &tm_y, p);
+  block_small_body<true, NH>(&tm_qkv, &tm_o, &tm_in, &tm_out, &tm_x, &tm_y, p);
 }
 
 }  // namespace b200
