@@ -10,9 +10,12 @@
 // What bounds it is shared memory, not arithmetic: a 128-bit shared load
 // costs four wavefronts even when every lane of a quarter-warp reads the
 // same address, so the design goal is few loaded bytes per multiply-add.
-// One CTA per sequence, 512 threads; an "octet" (8 adjacent lanes) owns the
-// row pair (2i, 2i+1) and thread u of the octet owns columns 4u..4u+3 of both
-// rows (the residual stream lives in registers).  Every projection is a
+// One CTA per sequence (512 threads), or, when the sequences leave SMs idle,
+// a cluster of two CTAs per sequence (256 threads each, 64 causally balanced
+// rows each, K/V rows exchanged through distributed shared memory; see the
+// kernel).  An "octet" (8 adjacent lanes) owns the row pair (2i, 2i+1) and
+// thread u of the octet owns columns 4u..4u+3 of both rows (the residual
+// stream lives in registers).  Every projection is a
 // register-blocked product over the pair: each weight loaded from shared
 // memory feeds both rows, each activation load feeds 4 to 12 outputs
 // (QKV: 12 outputs x 2 rows per thread).  LayerNorm statistics combine over
