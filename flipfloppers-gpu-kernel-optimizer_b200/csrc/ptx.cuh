@@ -139,6 +139,9 @@ __device__ __forceinline__ void st_cluster_f4(uint32_t addr, float4 v) {
                "f"(v.w)
                : "memory");
 }
+__device__ __forceinline__ void st_cluster_f2(uint32_t addr, float2 v) {
+  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(v.x), "f"(v.y) : "memory");
+}
 // arrive on an mbarrier of another CTA of the cluster; release at cluster scope orders
 // this thread's earlier shared::cluster stores before the arrival
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
