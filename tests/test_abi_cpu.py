@@ -66,6 +66,35 @@ def test_arg_checks_do_not_touch_device(pkg):
     assert lib.b200_flash_causal_launch(a, None) == -9
 
 
+def test_fused_small_arg_checks_do_not_touch_device(pkg):
+    """The whole-model launcher rejects unsupported shapes, aliasing and
+    misalignment before any CUDA call: d_model 128 takes 1, 2 or 4 heads (3 and
+    16 are refused), ffn a multiple of 128 up to 512, seq_len <= 128."""
+    rt = pkg.runtime
+    lib = rt.lib()
+
+    def args(**kw):
+        a = rt.FusedSmallArgs()
+        a.batch, a.seq_len, a.d_model, a.num_heads, a.ffn_dim, a.num_layers = 2, 128, 128, 4, 512, 1
+        for name in ("ln1_w", "ln1_b", "w_qkv", "b_qkv", "w_o", "b_o", "ln2_w", "ln2_b", "w_in", "b_in", "w_out",
+                     "b_out", "lnf_w", "lnf_b"):
+            setattr(a, name, 4096)
+        a.x, a.y, a.eps = 256, 512, 1e-5
+        for k, v in kw.items():
+            setattr(a, k, v)
+        return a
+
+    for heads in (3, 16):
+        assert lib.b200_block_fused_small_launch(args(num_heads=heads), None) == -1
+    assert lib.b200_block_fused_small_launch(args(ffn_dim=96), None) == -1
+    assert lib.b200_block_fused_small_launch(args(ffn_dim=640), None) == -1
+    assert lib.b200_block_fused_small_launch(args(seq_len=129), None) == -1
+    assert lib.b200_block_fused_small_launch(args(y=256), None) == -9      # y aliases x
+    assert lib.b200_block_fused_small_launch(args(w_in=4100), None) == -5  # weights 16-byte aligned
+    assert lib.b200_block_fused_small_launch(args(b_o=4100), None) == -5   # vectors arrive by bulk copy
+    assert lib.b200_block_fused_small_launch(args(lnf_w=None), None) == -9
+
+
 def test_model_state_dict_matches_reference_layout(tt):
     import oracle
     cfg = tt.TransformerConfig(2, 16, 64, 2, 256, 2, True)
