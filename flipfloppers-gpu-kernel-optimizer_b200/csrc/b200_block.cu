@@ -1083,6 +1083,23 @@ int b200_zero_masked_rows(float* y, const unsigned char* row_valid, long long ro
   return launch_status();
 }
 
+int b200_mask_prepare(const unsigned char* mask, int batch, int seq_len, int* kv_lens, b200_stream_t stream) {
+  if (!mask || !kv_lens || batch <= 0 || seq_len <= 0) return B200_ERR_ARG;
+  if (int rc = check_arch()) return rc;
+  launch_kernel(k_mask_prepare, dim3(static_cast<unsigned>(batch)), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                mask, seq_len, kv_lens);
+  return launch_status();
+}
+
+int b200_mask_finish(float* y, const unsigned char* mask, int batch, int seq_len, int d, b200_stream_t stream) {
+  if (!y || !mask || batch <= 0 || seq_len <= 0 || d <= 0) return B200_ERR_ARG;
+  if (int rc = check_arch()) return rc;
+  const int vec4 = (d % 4 == 0 && al16(y)) ? 1 : 0;
+  launch_kernel(k_mask_finish, dim3(static_cast<unsigned>(batch)), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                y, mask, seq_len, d, vec4);
+  return launch_status();
+}
+
 int b200_gemm_launch(int epilogue, const void* A, long long lda, const void* W, long long ldw, const float* bias,
                      const float* resid, long long ld_resid, void* out, long long ld_out, int M, int N, int K,
                      b200_stream_t stream) {
@@ -1127,20 +1144,45 @@ int b200_block_fused_small_launch(const B200FusedSmallArgs* args, b200_stream_t 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[B200_NOALLOC_SCRATCH_BYTES];
 
 namespace {
+// Per device: the context the address was resolved in, and the address.  A call
+// from another context on the same device (a new primary context after
+// cudaDeviceReset, or a context the caller created) resolves it again.
+CUcontext g_noalloc_ctx[128] = {nullptr};
 void* g_noalloc_addr[128] = {nullptr};
+PFN_cuCtxGetCurrent_v4000 g_ctx_get = nullptr;
+std::once_flag g_ctx_once;
+
+CUcontext current_context() {
+  std::call_once(g_ctx_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_ctx_get = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(fn);
+    else
+      cudaGetLastError();
+  });
+  CUcontext c = nullptr;
+  if (g_ctx_get == nullptr || g_ctx_get(&c) != CUDA_SUCCESS) return nullptr;
+  return c;
+}
 
 int noalloc_scratch_addr(void** out) {
   const int dev = current_device();
   if (dev < 0 || dev >= 128) return B200_ERR_SCRATCH_SETUP;
+  const CUcontext ctx = current_context();
+  if (ctx == nullptr) return B200_ERR_SCRATCH_SETUP;
   std::lock_guard<std::mutex> lk(g_mu);
-  if (g_noalloc_addr[dev] == nullptr) {
+  if (g_noalloc_addr[dev] == nullptr || g_noalloc_ctx[dev] != ctx) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || p == nullptr) {
       cudaGetLastError();
+      set_detail("cudaGetSymbolAddress(g_noalloc_scratch)", e);
       return B200_ERR_SCRATCH_SETUP;
     }
     g_noalloc_addr[dev] = p;
+    g_noalloc_ctx[dev] = ctx;
   }
   *out = g_noalloc_addr[dev];
   return B200_OK;

@@ -637,7 +637,9 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
           float m, lprev;
           row_max_sum(mx, prev_sum, (h & 1) ? st1 : st0, (h & 1) ? st3 : st2, m, lprev);
           if (h > 0 && h - 1 == hg) my_l = lprev;
-          m *= p.scale_log2;
+          // a row that sees no key (its mask excludes every visible key) keeps P = 0 and a zero
+          // context, as the reference's masked-out rows end up after their block (TTB:163-164)
+          m = (m == -INFINITY) ? 0.f : m * p.scale_log2;
           const uint64_t sc = f2pk(p.scale_log2, p.scale_log2), nm = f2pk(-m, -m);
           uint64_t a0 = f2pk(0.f, 0.f), a1 = a0;
 #pragma unroll
@@ -666,7 +668,7 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
         wait_w(SB_PV_DONE, par(step, H, H - 1));
         if (ok) tmem_ld32(trow + 256 + c0, v);
         {
-          const float inv = 1.f / my_l;
+          const float inv = my_l > 0.f ? 1.f / my_l : 0.f;
           const uint64_t iv = f2pk(inv, inv);
 #pragma unroll
           for (int i = 0; i < 32; i += 2) f2upk(f2mul(f2pk(v[i], v[i + 1]), iv), v[i], v[i + 1]);
@@ -894,7 +896,9 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
         float m, lprev;
         own_max_sum(mx, prev_sum, (h & 1) ? st1 : st0, m, lprev);  // reductions alternate st0/st1 strictly
         if (h > 0 && h - 1 == hg) my_l = lprev;
-        m *= p.scale_log2;
+        // a row that sees no key (its mask excludes every visible key) keeps P = 0 and a zero
+        // context, as the reference's masked-out rows end up after their block (TTB:163-164)
+        m = (m == -INFINITY) ? 0.f : m * p.scale_log2;
         const uint64_t sc = f2pk(p.scale_log2, p.scale_log2), nm = f2pk(-m, -m);
         uint64_t a0 = f2pk(0.f, 0.f), a1 = a0;
 #pragma unroll
@@ -924,7 +928,7 @@ __device__ __forceinline__ void block_small_body(const CUtensorMap* tm_qkv, cons
       if (ok) tmem_ld32(trow + 256 + c0, v);
       take_half();
       {
-        const float inv = 1.f / my_l;
+        const float inv = my_l > 0.f ? 1.f / my_l : 0.f;
         const uint64_t iv = f2pk(inv, inv);
 #pragma unroll
         for (int i = 0; i < 16; i += 2) f2upk(f2mul(f2pk(u[i], u[i + 1]), iv), u[i], u[i + 1]);

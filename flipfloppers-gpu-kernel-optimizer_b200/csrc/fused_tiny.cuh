@@ -482,6 +482,10 @@ __global__ void __launch_bounds__(TinyCfgT<SPLIT>::THREADS, 1) k_block_tiny(cons
   }
   __syncthreads();
   if (threadIdx.x == 0) fetch(0);
+  // layer whose weight copy is in flight and not yet waited for (-1: none); the same
+  // value in every thread (the fetch schedule does not depend on data)
+  int pending = 0;
+  bool aborted = false;
   // shared::cluster addresses of the other half's K / V buffers and exchange barriers
   uint32_t peer_ks = 0, peer_vs = 0, peer_xbar = 0;
   if constexpr (SPLIT) {
@@ -517,9 +521,16 @@ __global__ void __launch_bounds__(TinyCfgT<SPLIT>::THREADS, 1) k_block_tiny(cons
       if (threadIdx.x < C::V_TOTAL / 4)
         reinterpret_cast<float4*>(vec)[threadIdx.x] = reinterpret_cast<const float4*>(sm + C::STG_VEC)[threadIdx.x];
     }
-    // a copy that never landed (bounded wait, error recorded) ends the whole CTA here
-    if (__syncthreads_or(!got)) return;
-    if (threadIdx.x == 0 && l + 1 < p.layers) fetch(l + 1);
+    // a copy that never landed (bounded wait, error recorded) ends the layer loop here
+    if (__syncthreads_or(!got)) {
+      aborted = true;
+      break;
+    }
+    pending = -1;
+    if (l + 1 < p.layers) {
+      if (threadIdx.x == 0) fetch(l + 1);
+      pending = l + 1;
+    }
 
     // ---- LN1 -> NB
     {
@@ -566,8 +577,11 @@ __global__ void __launch_bounds__(TinyCfgT<SPLIT>::THREADS, 1) k_block_tiny(cons
       mbar_arrive_cluster(peer_xbar + 8u * static_cast<uint32_t>(l & 1));
       have_kv = mbar_wait_cluster(&xbar[l & 1], static_cast<uint32_t>((l >> 1) & 1), abort_flag, DERR_WAIT_GRID);
     }
-    // every row's K and V are in place (a bounded exchange wait that gave up ends the CTA)
-    if (__syncthreads_or(!have_kv)) return;
+    // every row's K and V are in place (a bounded exchange wait that gave up ends the loop)
+    if (__syncthreads_or(!have_kv)) {
+      aborted = true;
+      break;
+    }
     // ---- attention -> the context in NB
     tiny_attention<HD, G>(ksl, vsl, nb0, u, r0, kw, p);
     __syncwarp();
@@ -625,22 +639,36 @@ __global__ void __launch_bounds__(TinyCfgT<SPLIT>::THREADS, 1) k_block_tiny(cons
     }
   }
 
-  // final LayerNorm -> y (padded rows are zero)
-  tiny_layer_norm<G, CC>(x0, p.lnf_w + CC * u, p.lnf_b + CC * u, p.eps);
-  tiny_layer_norm<G, CC>(x1, p.lnf_w + CC * u, p.lnf_b + CC * u, p.eps);
-  if (ok0) {
-    if (p.row_valid != nullptr && p.row_valid[g0] == 0) {
+  if (aborted) {
+    // shared memory is released at exit: let the weight copy still in flight land first
+    // (bounded; a copy that never lands records DERR_WAIT_DRAIN)
+    if (threadIdx.x == 0 && pending >= 0) mbar_wait_drain(wbar, static_cast<uint32_t>(pending & 1));
+  } else {
+    // final LayerNorm -> y (padded rows are zero)
+    tiny_layer_norm<G, CC>(x0, p.lnf_w + CC * u, p.lnf_b + CC * u, p.eps);
+    tiny_layer_norm<G, CC>(x1, p.lnf_w + CC * u, p.lnf_b + CC * u, p.eps);
+    if (ok0) {
+      if (p.row_valid != nullptr && p.row_valid[g0] == 0) {
 #pragma unroll
-      for (int i = 0; i < CC; ++i) x0[i] = 0.f;
+        for (int i = 0; i < CC; ++i) x0[i] = 0.f;
+      }
+      stc<CC>(p.y + g0 * 32 + CC * u, x0);
     }
-    stc<CC>(p.y + g0 * 32 + CC * u, x0);
+    if (ok1) {
+      if (p.row_valid != nullptr && p.row_valid[g0 + 1] == 0) {
+#pragma unroll
+        for (int i = 0; i < CC; ++i) x1[i] = 0.f;
+      }
+      stc<CC>(p.y + (g0 + 1) * 32 + CC * u, x1);
+    }
   }
-  if (ok1) {
-    if (p.row_valid != nullptr && p.row_valid[g0 + 1] == 0) {
-#pragma unroll
-      for (int i = 0; i < CC; ++i) x1[i] = 0.f;
-    }
-    stc<CC>(p.y + (g0 + 1) * 32 + CC * u, x1);
+  if constexpr (SPLIT) {
+    // Neither half exits while the other may still store K / V rows or arrive on a
+    // barrier in its shared memory.  Every wait above is bounded and no path returns
+    // early, so both halves reach this cluster barrier: a half that gave up waits here
+    // while the other runs into its own (bounded) exchange wait, gives up too and joins.
+    __syncwarp();
+    cluster_sync_all();
   }
 }
 

@@ -151,4 +151,71 @@ __global__ void __launch_bounds__(256)
   for (int c = lane; c < d; c += 32) yr[c] = 0.f;
 }
 
+// ------------------------------------------------------------------ key-padding mask, checked on the device
+// The reference's valid_token_mask [B, S] (TTB:125-128, 140-141, 163-164,
+// 190-191): padded keys are excluded from attention and padded rows of every
+// block output are zero.  The kernel chain handles prefix-valid masks (valid
+// tokens first, padding last, what the harness's generate_random_case makes,
+// TTB:1793-1803) through per-sequence key counts, so the mask is read on the
+// device on every call -- nothing about its contents is cached on the host,
+// where an in-place edit or a new mask at a reused address would go unseen.
+
+// One CTA per sequence: the number of valid tokens and whether a valid token
+// follows a padded one (a hole: not prefix-valid).  Called by every thread.
+__device__ __forceinline__ void mask_scan(const unsigned char* __restrict__ m, int S, int& count, bool& holes) {
+  int c = 0;
+  bool h = false;
+#pragma unroll 4
+  for (int i = threadIdx.x; i < S; i += blockDim.x) {
+    const bool v = m[i] != 0;
+    c += v;
+    if (v && i > 0 && m[i - 1] == 0) h = true;
+  }
+  // block reductions: a sum (per-warp shuffles, then shared memory) and an OR
+  __shared__ int part[32];
+  for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = c;
+  holes = __syncthreads_or(h) != 0;
+  int t = 0;
+  for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += part[w];
+  count = t;
+}
+
+// kv_lens[b] = valid tokens of sequence b (the key count attention uses);
+// a mask with a hole records DERR_MASK_HOLES.  grid = batch, block = 256.
+__global__ void __launch_bounds__(256)
+    k_mask_prepare(const unsigned char* __restrict__ mask, int S, int* __restrict__ kv_lens) {
+  griddep_sync();
+  int count;
+  bool holes;
+  mask_scan(mask + static_cast<int64_t>(blockIdx.x) * S, S, count, holes);
+  if (threadIdx.x == 0) {
+    kv_lens[blockIdx.x] = count;
+    if (holes) record_error(DERR_MASK_HOLES);
+  }
+}
+
+// After the chain: the padded rows [count, S) of sequence b are set to 0.  A
+// sequence whose mask has a hole was computed with the wrong key set, so all of
+// its rows are set to NaN and DERR_MASK_HOLES is recorded: a wrong result never
+// passes as a plausible one.  grid = batch, block = 256; y fp32 [B*S, d].
+__global__ void __launch_bounds__(256)
+    k_mask_finish(float* __restrict__ y, const unsigned char* __restrict__ mask, int S, int d, int vec4) {
+  griddep_sync();
+  int count;
+  bool holes;
+  mask_scan(mask + static_cast<int64_t>(blockIdx.x) * S, S, count, holes);
+  if (holes && threadIdx.x == 0) record_error(DERR_MASK_HOLES);
+  const int r0 = holes ? 0 : count;
+  const float fill = holes ? __int_as_float(0x7fc00000) : 0.f;
+  float* ys = y + (static_cast<int64_t>(blockIdx.x) * S + r0) * d;
+  const int64_t n = static_cast<int64_t>(S - r0) * d;
+  if (vec4) {  // d % 4 == 0 and y 16-byte aligned (checked by the launcher)
+    float4* y4 = reinterpret_cast<float4*>(ys);
+    for (int64_t i = threadIdx.x; i < n / 4; i += blockDim.x) y4[i] = make_float4(fill, fill, fill, fill);
+  } else {
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) ys[i] = fill;
+  }
+}
+
 }  // namespace b200

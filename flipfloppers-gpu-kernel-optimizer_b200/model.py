@@ -160,7 +160,7 @@ class UserOptimizedTransformer(nn.Module):
         self.chunk_rows: Optional[int] = None      # query rows per chunk of the chunked strategy (None: gate decides)
         self._chunk_plan: Dict[Tuple, int] = {}
         self._ws: Dict[Tuple, torch.Tensor] = {}
-        self._mask_cache: dict = {}
+        self._kv_lens: Dict[Tuple, torch.Tensor] = {}
         self._plan: Dict[Tuple, str] = {}
         self._graphs: "OrderedDict[Tuple, torch.cuda.CUDAGraph]" = OrderedDict()
         self._warm: set = set()
@@ -224,52 +224,46 @@ class UserOptimizedTransformer(nn.Module):
 
     # ------------------------------------------------------------------ arbiter
     def _mask_is_all_ones(self, m: Optional[torch.Tensor]) -> bool:
-        """Cached ``mask.all()``, keyed by (data_ptr, shape) as in TTB:1011-1025."""
-        return self._padding_rows(m, None) is None
+        """``mask.all()``, the property the reference caches by ``data_ptr`` (TTB:1011-1025).
 
-    def _padding_rows(self, m: Optional[torch.Tensor], device) -> Optional[torch.Tensor]:
-        """Per-row valid flags (uint8 [B*S] on ``device``) of a key-padding mask, or None if
-        there is no padding.  A property of the mask, cached by (data_ptr, shape) like the
-        reference's ``_mask_is_all_ones`` (TTB:1011-1025).
+        Deliberately NOT cached here and not used by ``forward``: the caching
+        allocator hands freed blocks back at the same address and an in-place
+        edit keeps it, so a pointer-keyed verdict can go stale; the kernels read
+        the mask itself on every call instead (``_mask_bytes``).  This helper
+        synchronises the device."""
+        return m is None or bool(m.all())
 
-        The reference masks padded keys in attention and zeroes padded rows after each
-        block and after the final norm (TTB:125-128, 140-141, 163-164, 190-191).  With
-        a prefix-valid mask (``True`` then ``False`` along each sequence, what
-        ``generate_random_case`` produces, TTB:1793-1803) that is: attention limited to
-        each sequence's first ``len`` keys (automatic for valid rows under causal
-        attention; the kernels apply it for non-causal attention from the per-sequence
-        lengths) and the output's padded rows set to zero.  Padded rows never influence
-        valid rows, so their intermediate values need no masking.  Masks with interior
-        holes are rejected."""
+    @staticmethod
+    def _mask_bytes(m: Optional[torch.Tensor], B: int, S: int, device: torch.device) -> Optional[torch.Tensor]:
+        """The key-padding mask as one byte per token on ``device`` ([B, S] uint8, nonzero =
+        valid), or None without a mask.  A contiguous bool mask on the device is used as it
+        is (no copy, no host synchronisation); anything else is converted on the stream.
+
+        The kernels read these bytes on every call, so a mask edited in place or a new
+        mask at a reused address is always seen.  Semantics (TTB:125-128, 140-141,
+        163-164, 190-191): padded keys are excluded from attention and padded rows of
+        the output are 0.  The single-kernel path masks keys one by one and takes any
+        mask; the kernel chain supports prefix-valid masks (valid tokens first, what
+        ``generate_random_case`` produces, TTB:1793-1803) and checks that on the device:
+        a sequence whose mask has a hole comes back as NaN rows with device error
+        ``runtime.DERR_MASK_HOLES`` recorded."""
         if m is None:
             return None
-        key = (m.data_ptr(), tuple(m.shape), str(m.device))
-        hit = self._mask_cache.get(key)
-        if hit is None:
-            mb = m.to(torch.bool)
-            if bool(mb.all()):
-                hit = ("ones", None, None)
-            else:
-                if mb.dim() != 2:
-                    raise ValueError("valid_token_mask must be [batch, seq_len]")
-                mi = mb.to(torch.int8)
-                if mi.shape[1] > 1 and bool((mi[:, 1:] > mi[:, :-1]).any()):
-                    raise NotImplementedError(
-                        "valid_token_mask must be prefix-valid per sequence (valid tokens first, padding last); "
-                        "masks with interior holes are not supported")
-                hit = ("pad", mb.to(torch.uint8).contiguous().reshape(-1), mb.sum(1).to(torch.int32).contiguous())
-            self._mask_cache[key] = hit
-        if hit[1] is not None and device is not None and hit[1].device != device:
-            hit = ("pad", hit[1].to(device), hit[2].to(device))
-            self._mask_cache[key] = hit
-        return hit[1]
+        if m.dim() != 2 or tuple(m.shape) != (B, S):
+            raise ValueError(f"valid_token_mask must be [{B}, {S}], got {tuple(m.shape)}")
+        if m.dtype == torch.bool and m.device == device and m.is_contiguous():
+            return m.view(torch.uint8)
+        return m.to(device=device, dtype=torch.bool).contiguous().view(torch.uint8)
 
-    def _padding_lens(self, m: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
-        """Valid tokens per sequence (int32 [B]) of a cached padding mask, or None."""
-        if m is None:
-            return None
-        hit = self._mask_cache.get((m.data_ptr(), tuple(m.shape), str(m.device)))
-        return None if hit is None else hit[2] if len(hit) > 2 else None
+    def _kv_lens_buffer(self, B: int, device: torch.device) -> torch.Tensor:
+        """Per-sequence valid-key counts (int32 [B]) that ``b200_mask_prepare`` fills on the device."""
+        key = (B, device.index)
+        buf = self._kv_lens.get(key)
+        if buf is None:
+            self._graphs.clear()  # captured graphs point at the old buffer
+            buf = torch.zeros(B, dtype=torch.int32, device=device)
+            self._kv_lens[key] = buf
+        return buf
 
     def _fused_small_eligible(self) -> bool:
         """Shapes the single-kernel whole-model path takes: the tensor-core kernels
@@ -360,44 +354,41 @@ class UserOptimizedTransformer(nn.Module):
         if x.dim() != 3 or x.shape[-1] != cfg.d_model:
             raise ValueError(f"expected x of shape [B, S, {cfg.d_model}], got {tuple(x.shape)}")
         B, S, d = x.shape
-        if valid_token_mask is not None and tuple(valid_token_mask.shape) != (B, S):
-            raise ValueError(f"valid_token_mask must be [{B}, {S}], got {tuple(valid_token_mask.shape)}")
-        rows_valid = self._padding_rows(valid_token_mask, x.device)
-        kv_lens = self._padding_lens(valid_token_mask) if rows_valid is not None else None
+        mask = self._mask_bytes(valid_token_mask, B, S, x.device)
         out_dtype = x.dtype
         xin = x if (x.dtype == torch.float32 and x.is_contiguous()) else x.to(torch.float32).contiguous()
         dev = xin.device
         y = torch.empty_like(xin)
         if dev.index == torch.cuda.current_device():
-            self._forward_into(xin, y, rows_valid, kv_lens)
+            self._forward_into(xin, y, mask)
         else:
             with torch.cuda.device(dev):
-                self._forward_into(xin, y, rows_valid, kv_lens)
+                self._forward_into(xin, y, mask)
         return y if out_dtype == torch.float32 else y.to(out_dtype)
 
     def _run_graphed(self, x: torch.Tensor, y: torch.Tensor, ws: torch.Tensor, strat: str,
-                     rows_valid: Optional[torch.Tensor] = None, kv_lens: Optional[torch.Tensor] = None) -> None:
+                     mask: Optional[torch.Tensor] = None) -> None:
         """Replay (or capture) the forward as one CUDA graph keyed by shape and pointers.
 
         The graph reads x (and the padding flags) and writes y at the addresses it was
         captured with; keying on every pointer keeps that correct for any caller, and
         the caching allocator hands the same output block back to a loop that drops its
-        previous result, so steady-state calls replay without copies."""
-        rv = 0 if rows_valid is None else rows_valid.data_ptr()
-        kl = 0 if kv_lens is None else kv_lens.data_ptr()
-        key = (tuple(x.shape), x.data_ptr(), y.data_ptr(), ws.data_ptr(), strat, rv, kl)
+        previous result, so steady-state calls replay without copies.  The mask's bytes
+        are read by the replayed kernels, so its contents are never part of the key."""
+        mp = 0 if mask is None else mask.data_ptr()
+        key = (tuple(x.shape), x.data_ptr(), y.data_ptr(), ws.data_ptr(), strat, mp)
         g = self._graphs.get(key)
         if g is None:
             shape_key = (tuple(x.shape), strat)
             if shape_key not in self._warm:
                 # first call at this shape: launch eagerly (sets kernel attributes, validates arguments)
-                self._launch(x, y, ws, strat, rows_valid, kv_lens)
+                self._launch(x, y, ws, strat, mask)
                 torch.cuda.current_stream().synchronize()
                 self._warm.add(shape_key)
                 return
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
-                self._launch(x, y, ws, strat, rows_valid, kv_lens)
+                self._launch(x, y, ws, strat, mask)
             self._graphs[key] = g
             while len(self._graphs) > _GRAPH_CACHE:
                 self._graphs.popitem(last=False)
@@ -406,20 +397,28 @@ class UserOptimizedTransformer(nn.Module):
         g.replay()
 
     def _launch(self, x: torch.Tensor, y: torch.Tensor, ws: torch.Tensor, strat: str,
-                rows_valid: Optional[torch.Tensor] = None, kv_lens: Optional[torch.Tensor] = None) -> None:
+                mask: Optional[torch.Tensor] = None) -> None:
+        """Launch the forward on the current stream.  With a mask: the single kernel masks
+        keys and rows itself; the chain gets per-sequence key counts from the device
+        (non-causal attention; causal attention of a valid row under a prefix-valid mask
+        never reaches a padded key) and a last kernel that zeroes padded rows and turns
+        a mask with holes into NaN rows plus a device error."""
+        B, S, _ = x.shape
         if strat == "fused_small":
-            self._forward_fused_small(x, y, rows_valid)
+            self._forward_fused_small(x, y, mask)
             return
+        kv_lens = None
+        if mask is not None and not self.config.causal:
+            kv_lens = rt.mask_prepare(mask, self._kv_lens_buffer(B, x.device))
         if strat == "chunked":
-            B, S, _ = x.shape
             self._forward_chain(x, y, ws, chunk_rows=self._chunk_plan[(B, S, x.device.index)])
         else:
             self._forward_chain(x, y, ws, kv_lens=kv_lens)
-        if rows_valid is not None:
-            rt.zero_masked_rows(y, rows_valid)
+        if mask is not None:
+            rt.mask_finish(y, mask)
 
     def _forward_fused_small(self, x: torch.Tensor, y: torch.Tensor,
-                             rows_valid: Optional[torch.Tensor] = None) -> None:
+                             mask: Optional[torch.Tensor] = None) -> None:
         cfg = self.config
         B, S, d = x.shape
         st = self._stack
@@ -432,7 +431,7 @@ class UserOptimizedTransformer(nn.Module):
             setattr(a, name, st[name].data_ptr())
         a.lnf_w, a.lnf_b = self._lnf[0].data_ptr(), self._lnf[1].data_ptr()
         a.eps = float(self.layers[0].norm1.eps)
-        a.row_valid = None if rows_valid is None else rows_valid.data_ptr()
+        a.row_valid = None if mask is None else mask.data_ptr()
         a.non_causal = 0 if cfg.causal else 1
         rt.fused_small(a)
 
@@ -554,10 +553,9 @@ class UserOptimizedTransformer(nn.Module):
             pipes[key] = pipe
         return pipe
 
-    def _forward_into(self, xin: torch.Tensor, y: torch.Tensor, rows_valid: Optional[torch.Tensor] = None,
-                      kv_lens: Optional[torch.Tensor] = None) -> None:
+    def _forward_into(self, xin: torch.Tensor, y: torch.Tensor, mask: Optional[torch.Tensor] = None) -> None:
         """Forward of a contiguous fp32 CUDA tensor into a preallocated ``y`` (current stream);
-        ``rows_valid`` (uint8 [B*S], optional) zeroes padded output rows."""
+        ``mask`` (uint8 [B, S] on the device, optional) is the key-padding mask."""
         B, S, d = xin.shape
         dev = xin.device
         self._ensure_packs(dev)
@@ -571,9 +569,9 @@ class UserOptimizedTransformer(nn.Module):
         else:
             ws = self._workspace(256, dev)
         if _GRAPHS_ON and xin.numel() <= _GRAPH_MAX_ELEMS:
-            self._run_graphed(xin, y, ws, strat, rows_valid, kv_lens)
+            self._run_graphed(xin, y, ws, strat, mask)
         else:
-            self._launch(xin, y, ws, strat, rows_valid, kv_lens)
+            self._launch(xin, y, ws, strat, mask)
 
     # ------------------------------------------------------------------ profiling helper
     @torch.no_grad()

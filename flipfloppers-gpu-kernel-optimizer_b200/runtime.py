@@ -110,6 +110,8 @@ EXPORTS = [
     ("b200_add_layernorm_launch", ctypes.c_int,
      [_vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, _vp]),
     ("b200_zero_masked_rows", ctypes.c_int, [_vp, _vp, _c_ll, ctypes.c_int, _vp]),
+    ("b200_mask_prepare", ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp, _vp]),
+    ("b200_mask_finish", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
     ("b200_gemm_launch", ctypes.c_int,
      [ctypes.c_int, _vp, _c_ll, _vp, _c_ll, _vp, _vp, _c_ll, _vp, _c_ll, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
     ("b200_gemm_residual_layernorm_launch", ctypes.c_int,
@@ -223,6 +225,31 @@ def zero_masked_rows(y: torch.Tensor, row_valid: torch.Tensor, stream=None) -> t
     d = y.shape[-1]
     rc = lib().b200_zero_masked_rows(_p(y), _p(row_valid), y.numel() // d, d, _stream(stream))
     check(rc, "b200_zero_masked_rows")
+    return y
+
+
+# device error word value recorded when a key-padding mask with a hole reaches the kernel chain
+DERR_MASK_HOLES = 7
+
+
+def mask_prepare(mask: torch.Tensor, kv_lens: torch.Tensor, stream=None) -> torch.Tensor:
+    """kv_lens[b] = valid tokens of sequence b of ``mask`` ([B, S] bool/uint8 on the device,
+    contiguous), computed on the device; a mask with a hole records DERR_MASK_HOLES."""
+    _require_cuda(mask, kv_lens)
+    B, S = mask.shape
+    if kv_lens.dtype != torch.int32 or kv_lens.numel() < B:
+        raise TypeError("mask_prepare: kv_lens must be int32 with one entry per sequence")
+    check(lib().b200_mask_prepare(_p(mask), B, S, _p(kv_lens), _stream(stream)), "b200_mask_prepare")
+    return kv_lens
+
+
+def mask_finish(y: torch.Tensor, mask: torch.Tensor, stream=None) -> torch.Tensor:
+    """Padded rows of y (fp32 [B, S, d] / [B*S, d]) set to 0 from ``mask`` ([B, S], on the
+    device); every row of a sequence whose mask has a hole is set to NaN (DERR_MASK_HOLES)."""
+    _require_cuda(y, mask)
+    B, S = mask.shape
+    d = y.shape[-1]
+    check(lib().b200_mask_finish(_p(y), _p(mask), B, S, d, _stream(stream)), "b200_mask_finish")
     return y
 
 

@@ -112,6 +112,27 @@ int b200_add_layernorm_launch(const float* a, const float* b, const float* bias,
  * semantics.  y fp32 [rows, d], row_valid uint8 [rows]. */
 int b200_zero_masked_rows(float* y, const unsigned char* row_valid, long long rows, int d, b200_stream_t stream);
 
+/* The key-padding mask of the kernel chain (b200_block_forward and the chunked
+ * forward), checked on the device on every call so that nothing about a mask's
+ * contents has to be cached on the host.  Replaces the reference's
+ * `_mask_is_all_ones` property cache (torch_transformer_benchmark.py:1011-1025)
+ * and its masking of padded keys and rows (TTB:125-128, 140-141, 163-164,
+ * 190-191).  mask: [batch, seq_len] bytes, nonzero = valid token (a torch bool
+ * tensor as is).  The chain supports prefix-valid masks (valid tokens first,
+ * padding last, what the reference harness generates, TTB:1793-1803).
+ *
+ * b200_mask_prepare: kv_lens[b] = number of valid tokens of sequence b (the
+ * per-sequence key count of non-causal attention, B200BlockArgs.kv_lens).
+ * b200_mask_finish: after the forward, rows of y past each sequence's valid
+ * prefix are set to 0.
+ * A mask with a hole (a valid token after a padded one) records device error
+ * 7 (see b200_device_error), and b200_mask_finish sets every row of such a
+ * sequence to NaN, so a result computed with the wrong key set is never
+ * returned as a plausible one.  (The single-kernel path,
+ * b200_block_fused_small_launch, masks keys one by one and takes any mask.) */
+int b200_mask_prepare(const unsigned char* mask, int batch, int seq_len, int* kv_lens, b200_stream_t stream);
+int b200_mask_finish(float* y, const unsigned char* mask, int batch, int seq_len, int d, b200_stream_t stream);
+
 /* out[M,N] = epilogue(A[M,K] . W[N,K]^T + bias[N]).  A, W fp16 row-major with
  * leading dimensions lda, ldw (elements); bias fp32 (may be null); resid fp32
  * [M, ld_resid] for B200_EPI_BIAS_RESID_F32.  The residual epilogue adds onto
@@ -265,6 +286,9 @@ int b200_block_fused_small_launch(const B200FusedSmallArgs* args, b200_stream_t 
  * is launched.
  * Set-up: the first call on a device (with that device current) looks up the
  * buffer's device address; make that first call before any stream capture.
+ * The address is kept per device and CUDA context: after cudaDeviceReset (or
+ * from another context on the same device) the next call looks it up again,
+ * and that call, too, must come before any stream capture.
  * Sharing: every call on a device uses the same buffer, which keeps the last
  * call's contents (nothing in it needs to start at zero: every region is
  * written before it is read).  Calls whose work overlaps on the GPU (other

@@ -233,12 +233,3 @@ def test_noncausal_against_oracle(tt, B, S, d, H, F, L):
                                oracle.OracleConfig(B, S, d, H, F, L, False), x.numpy())
     res = oracle.compare_outputs(ref, y, rtol=RTOL, atol=ATOL)
     assert res.passed, res
-
-
-def test_mask_with_holes_is_rejected(tt):
-    model, _ = _model(tt, 2, 64, 128, 4, 512, 1)
-    x, _ = oracle.generate_random_case(2, 64, 128, 1)
-    mask = torch.ones(2, 64, dtype=torch.bool)
-    mask[0, 10] = False
-    with pytest.raises(NotImplementedError, match="prefix-valid"):
-        model(x.to(DEV), mask.to(DEV))

@@ -21,7 +21,8 @@ PKG = os.path.join(REPO, "flipfloppers-gpu-kernel-optimizer_b200")
 sys.path.insert(0, PKG)
 import harness_tools as ht  # noqa: E402
 
-REFERENCE_HARNESS = "/root/reference/torch_transformer_benchmark.py"
+# a checkout of the reference, named like tests/golden/make_golden.py does (REFERENCE_DIR)
+REFERENCE_HARNESS = os.path.join(os.environ.get("REFERENCE_DIR", ""), "torch_transformer_benchmark.py")
 
 # a miniature harness with every frozen symbol, a stub user class and the tolerance flags
 CANON = textwrap.dedent('''
@@ -121,7 +122,8 @@ def test_splice_cli_check(tmp_path):
                           capture_output=True).returncode == 1
 
 
-@pytest.mark.skipif(not os.path.exists(REFERENCE_HARNESS), reason="reference harness not present")
+@pytest.mark.skipif(not os.environ.get("REFERENCE_DIR") or not os.path.exists(REFERENCE_HARNESS),
+                    reason="reference harness not present (set REFERENCE_DIR to a checkout)")
 def test_splice_of_the_reference_harness_builds_the_library_model(tmp_path):
     """The reference's own harness, spliced: frozen symbols unchanged, and its
     UserOptimizedTransformer is this library's, loading the baseline's weights strictly."""

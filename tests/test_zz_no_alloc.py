@@ -6,10 +6,11 @@ foreign-language caller with no CUDA allocator, a loop that cannot pay for
 cudaMalloc's implicit synchronisation -- so the library offers the block
 forward with its intermediates in a static 32 MiB device buffer instead of a
 caller-provided workspace.  This file checks, through the C ABI, that two
-calls in a row agree with b200_block_forward (which takes a workspace) under
-the harness's tolerance, and that a problem larger than the buffer is refused
-before anything is launched.  It must pass alone in a fresh process and after
-the rest of the suite.
+calls in a row agree with b200_block_forward (which takes a workspace): both
+run the same kernels on the same inputs, so the outputs must be bit-identical
+(stricter than the harness's atol 0.002 / rtol 0.02, which is checked too), and
+that a problem larger than the buffer is refused before anything is launched.
+It must pass alone in a fresh process and after the rest of the suite.
 """
 
 import ctypes
@@ -71,6 +72,7 @@ def test_noalloc_matches_workspace_entry_point(tt):
         assert torch.isfinite(y_na).all()
         res = oracle.compare_outputs(y_ws.cpu(), y_na.cpu(), rtol=RTOL, atol=ATOL)
         assert res.passed, (call, res)
+        assert torch.equal(y_ws, y_na), (call, (y_ws - y_na).abs().max().item())
     assert rt.device_error(clear=True) == 0
 
 
