@@ -4,12 +4,15 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config C2]
     torchrun --nproc-per-node N bench.py --gpus N ...     (N > 1: one process per GPU)
 
-Workload (N=1): BASELINE configuration 2 (``configs[1]``) -- causal pre-LN
-block, B=64, S=128, d=128, H=4, ffn=512, L=1, fp32 in/out, seeded default
-init, x ~ N(0,1) from the CPU generator (seed 1234+100000, as the reference
-harness's benchmark input, TTB:2061-2068).  N>1: every rank runs its own
-B=64 batch on its own GPU (batch sharding, no collective on the data path;
-weak scaling); timing is the max over ranks.
+Workload (default): BASELINE configuration 5 (``configs[4]``), the largest
+configuration that fits one B200 -- causal pre-LN block, B=32, S=100000,
+d=1024, H=16 (head_dim 64), ffn=4096, L=1, fp32 in/out, seeded default init,
+x ~ N(0,1) drawn on the device (13 GB).  N>1: the 32 sequences are split
+across the ranks (batch sharding, no collective on the data path; strong
+scaling, the global batch stays 32); timing is the max over ranks.
+``--config C2|C3|C4a|C4b`` measure the other BASELINE configurations (B per
+rank fixed: weak scaling), ``--config M7|M11`` two rows of the reference's
+official matrix.
 
 ``value``: tokens/s of the whole job with x resident in HBM (CUDA events on
 the launching stream around each step, L2 flushed between steps by a 256 MiB
@@ -61,12 +64,17 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=None, help="timed steps (default 10 for C5, else 200)")
+    ap.add_argument("--warmup", type=int, default=None, help="warm-up steps (default 3 for C5, else 20)")
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    ap.add_argument("--config", choices=sorted(CONFIGS), default="C2")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="C5")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    return ap.parse_args()
+    a = ap.parse_args()
+    if a.steps is None:
+        a.steps = 10 if a.config in STRONG else 200
+    if a.warmup is None:
+        a.warmup = 3 if a.config in STRONG else 20
+    return a
 
 
 def rank_batch(cfg_name, rank, world):
@@ -77,10 +85,10 @@ def rank_batch(cfg_name, rank, world):
     return B
 
 
-# exact sampled-row check of the multi-GB configuration: rows of sequence 0 (causal,
-# one layer: row t depends only on rows 0..t)
-SAMPLED_PREFIX = 16384
-SAMPLED_ROWS = sorted(SAMPLED_PREFIX - 1 - 2047 * i for i in range(8))  # ascending, as the oracle returns them
+# bounded CPU sample of the multi-GB configuration (one sequence): the K/V prefix of
+# C5_PREFIXES[-1] rows and one query chunk of C5_CHUNK rows ending at each prefix
+C5_CHUNK = 512
+C5_PREFIXES = (4096, 16384)
 
 # ~20 ms of device-side spinning queued ahead of the timed steps
 QUEUE_PREFILL_CYCLES = 40_000_000
@@ -195,36 +203,67 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- CPU baseline (oracle port)
-def cpu_sampled_rows_estimate(cfg_name, x_seq=None):
-    """C5 cannot run on the CPU unchunked (its score tensor alone is ~20 TB): time the exact
-    sampled-row restatement (oracle.sampled_rows_forward) on one sequence and extrapolate a
-    full forward as B x (K/V-prefix projection + sum over rows of the per-row cost, which
-    grows linearly with the row's prefix length)."""
-    import numpy as np
-    import oracle
+def _host_cores():
     try:
         from threadpoolctl import threadpool_info
-        cores = max([i.get("num_threads", 1) for i in threadpool_info()] or [os.cpu_count() or 1])
+        return int(max([i.get("num_threads", 1) for i in threadpool_info()] or [os.cpu_count() or 1]))
     except Exception:  # noqa: BLE001
-        cores = os.cpu_count() or 1
+        return os.cpu_count() or 1
+
+
+def cpu_chunked_step(cfg_name, params, x_seq):
+    """One bounded CPU sample of the multi-GB configuration, extrapolated to a full forward.
+
+    A full CPU forward of C5 is infeasible (hours), so one step times the NumPy
+    restatement of the reference's chunked forward (oracle.prefix_kv and
+    oracle.chunk_rows_forward, TTB:1378-1609) on one sequence: the K/V prefix of
+    P2 rows, and one C5_CHUNK-row query chunk ending at P1 and at P2.  A chunk's
+    cost is a + b * prefix (projections and FFN of its rows, attention over its
+    prefix), so the two chunks fix a and b; a sequence is S / R chunks at
+    prefixes R, 2R, .. S plus the K/V projection of S rows, and the forward is B
+    sequences.  Returns (estimated seconds per forward, wall seconds of the
+    sample, output rows [P2 - R, P2) of the sequence)."""
+    import oracle
     B, S, d, H, F, L = CONFIGS[cfg_name]
-    T = SAMPLED_PREFIX  # prefix sampled
+    P1, P2 = C5_PREFIXES
+    R = C5_CHUNK
+    w0 = time.perf_counter()
+    kv = oracle.prefix_kv(params, x_seq, P2)
+    t_kv = time.perf_counter() - w0
+    t0 = time.perf_counter()
+    oracle.chunk_rows_forward(params, H, x_seq, P1 - R, P1, kv=kv)
+    t1 = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    y2 = oracle.chunk_rows_forward(params, H, x_seq, P2 - R, P2, kv=kv)
+    t2 = time.perf_counter() - t0
+    wall = time.perf_counter() - w0
+    b = max((t2 - t1) / (P2 - P1), 0.0)
+    a = max(t1 - b * P1, 0.0)
+    n = -(-S // R)
+    per_seq = t_kv * S / P2 + n * a + b * R * n * (n + 1) / 2
+    return B * per_seq, wall, y2
+
+
+def cpu_chunked_estimate(cfg_name, x_seq=None, steps=1):
+    """cpu_baseline of the multi-GB configuration: the median of ``steps`` samples."""
+    import oracle
+    B, S, d, H, F, L = CONFIGS[cfg_name]
     params = oracle.params_from_state_dict(oracle.init_state_dict(1, d, F, 1234))
-    x = oracle.generate_chunked_input(1, S, d, seed=1234, rows=T)[0].numpy() if x_seq is None else x_seq[:T]
-    t0 = time.perf_counter()
-    oracle.sampled_rows_forward(params, H, x, [T - 1], key_block=8192)
-    t_one = time.perf_counter() - t0             # K/V prefix of T rows + one row at position T-1
-    t0 = time.perf_counter()
-    y_rows = oracle.sampled_rows_forward(params, H, x, SAMPLED_ROWS, key_block=8192)
-    t_nine = time.perf_counter() - t0
-    per_row_at_T = max((t_nine - t_one) / 7, 1e-6)  # marginal cost of a row with a T-key prefix
-    kv = max(t_one - per_row_at_T, 1e-6) * S / T     # K/V projections scale with the prefix length
-    rows = per_row_at_T * (S / 2) / T * S          # per-row cost ~ linear in its prefix; mean prefix S/2
-    est = B * (kv + rows)
-    return {"value": B * S / est, "unit": "tokens/s", "cores": int(cores), "kind": "port",
-            "sample": f"ESTIMATE: oracle.sampled_rows_forward on one sequence prefix of {T} rows "
-                      f"(K/V prefix {t_one:.1f} s, marginal row {per_row_at_T * 1e3:.1f} ms at {T} keys), "
-                      f"extrapolated to B={B} x S={S}: {est / 60:.1f} min per forward"}, est, 1, y_rows
+    if x_seq is None:
+        x_seq = oracle.generate_chunked_input(1, S, d, seed=1234, rows=C5_PREFIXES[-1])[0].numpy()
+    ests, walls, y = [], [], None
+    for _ in range(steps):
+        est, wall, y = cpu_chunked_step(cfg_name, params, x_seq)
+        ests.append(est)
+        walls.append(wall)
+    est = statistics.median(ests)
+    P1, P2 = C5_PREFIXES
+    base = {"value": B * S / est, "unit": "tokens/s", "cores": _host_cores(), "kind": "port",
+            "sample": f"ESTIMATE: NumPy fp32 restatement of the reference's chunked forward (oracle.chunk_rows_forward) "
+                      f"on one sequence -- K/V of a {P2}-row prefix and {C5_CHUNK}-row query chunks ending at {P1} and "
+                      f"{P2} ({statistics.median(walls):.2f} s per sample), chunk cost linear in its prefix, "
+                      f"extrapolated to B={B} x S={S}: {est / 60:.1f} min per forward"}
+    return base, est, statistics.median(walls), y
 
 
 def cpu_sample_batch(cfg_name):
@@ -237,13 +276,7 @@ def cpu_forward_rate(cfg_name, budget_s=12.0, min_reps=1):
     """tokens/s of the NumPy restatement of the reference module on this host (all BLAS threads)."""
     import numpy as np
     import oracle
-    if cfg_name in STRONG:
-        return cpu_sampled_rows_estimate(cfg_name)
-    try:
-        from threadpoolctl import threadpool_info
-        cores = max([i.get("num_threads", 1) for i in threadpool_info()] or [os.cpu_count() or 1])
-    except Exception:  # noqa: BLE001
-        cores = os.cpu_count() or 1
+    cores = _host_cores()
     B, S, d, H, F, L = CONFIGS[cfg_name]
     Bs = cpu_sample_batch(cfg_name)
     params = oracle.params_from_state_dict(oracle.init_state_dict(L, d, F, 1234))
@@ -273,13 +306,32 @@ def run_reference(args, rank, world):
     import numpy as np
     import oracle
     if args.config in STRONG:
-        base, est, _, _ = cpu_sampled_rows_estimate(args.config)
-        line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": "tokens/s",
-                "n_gpus": args.gpus, "steps": 1, "warmup": 0, "ms_per_step": est * 1e3, "higher_is_better": True,
-                "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        # every step is one bounded sample (about a second or two of CPU work), extrapolated
+        import oracle
+        params = oracle.params_from_state_dict(oracle.init_state_dict(1, d, F, 1234))
+        x_seq = oracle.generate_chunked_input(1, S, d, seed=1234, rows=C5_PREFIXES[-1])[0].numpy()
+        for _ in range(args.warmup):
+            cpu_chunked_step(args.config, params, x_seq)
+        ests, walls = [], []
+        for _ in range(args.steps):
+            est, wall, _ = cpu_chunked_step(args.config, params, x_seq)
+            ests.append(est)
+            walls.append(wall)
+        est = statistics.median(ests)
+        tok = B * S / est
+        P1, P2 = C5_PREFIXES
+        base = {"value": tok, "unit": "tokens/s", "cores": _host_cores(), "kind": "port",
+                "sample": f"ESTIMATE per step: NumPy fp32 restatement of the reference's chunked forward on one "
+                          f"sequence (K/V of a {P2}-row prefix, {C5_CHUNK}-row query chunks ending at {P1} and {P2}), "
+                          f"extrapolated to B={B} x S={S}; value = tokens/s of the median step's estimate "
+                          f"({est / 60:.1f} min per forward); ms_per_step = wall time of one sample"}
+        line = {"impl": "reference", "metric": METRIC, "value": tok, "unit": "tokens/s",
+                "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": statistics.median(walls) * 1e3, "estimated_ms_per_forward": est * 1e3,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic (seeded N(0,1) input, seeded default init)", "config": config_dict(args.config, 1),
                 "cpu_baseline": base,
-                "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+                "e2e": {"value": tok, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return 0
     base, med, Bs, _ = cpu_forward_rate(args.config, budget_s=0.0, min_reps=1)
@@ -372,16 +424,22 @@ def main():
         # host-side enqueue latency (Python call overhead) falls between an
         # event pair: the events then bracket device work only
         torch.cuda._sleep(QUEUE_PREFILL_CYCLES)
+        y_last = None
         for i in range(args.steps):
             flush.zero_()
             starts[i].record(stream)
-            model(x, mask)
+            y_last = model(x, mask)
             ends[i].record(stream)
         torch.cuda.synchronize()
         barrier()
         ms_rank = sum(a.elapsed_time(b) for a, b in zip(starts, ends))
         ms_total = max_over_ranks(ms_rank)
         strong = args.config in STRONG
+        # the device path's output of the timed input, kept to check the end-to-end leg's
+        # downloads against (all of it, or for the multi-GB configuration a set of rows of
+        # every sequence)
+        pos = torch.tensor(sorted({0, 1, S // 3, S // 2, S - 2, S - 1}), device=dev)
+        y_dev_ref = y_last.index_select(1, pos).cpu() if strong else y_last.cpu()
         # ---- dominant-kernel roofline (rank 0; one sequence of the multi-GB configuration)
         roof = None
         if rank == 0:
@@ -392,10 +450,11 @@ def main():
         # GPU outputs compared with the oracle in the CPU leg (rank 0, one GPU)
         y_check = None
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
-            if strong:
-                y_check = model(x[:1].contiguous(), mask[:1])[0, SAMPLED_ROWS].float().cpu()
+            if strong:  # one query chunk of sequence 0, from the timed forward's output
+                y_check = y_last[0, C5_PREFIXES[-1] - C5_CHUNK:C5_PREFIXES[-1]].float().cpu()
             else:
-                y_check = model(x, mask)[:cpu_sample_batch(args.config)].float().cpu()
+                y_check = y_last[:cpu_sample_batch(args.config)].float().cpu()
+        del y_last
         e2e_serial_ms = None
         if strong:
             del x  # make room for the two pipeline slots
@@ -438,41 +497,48 @@ def main():
         torch.cuda.synchronize()
         barrier()
         e2e_ms = max_over_ranks(t0.elapsed_time(t1))
-        ok_e2e = bool(torch.equal(y_hosts[0], y_hosts[1]))
+        y_e2e = y_hosts[(args.steps - 1) % 2]
+        ok_e2e = bool(torch.equal(y_e2e.index_select(1, pos.cpu()) if strong else y_e2e, y_dev_ref))
     clocks = clk.stop()
 
     tokens_all = (CONFIGS[args.config][0] * S) if args.config in STRONG else world * tokens_rank
     value = tokens_all * args.steps / (ms_total / 1e3)
     e2e_value = tokens_all * args.steps / (e2e_ms / 1e3)
-    launches_per_step = kernels_per_forward(model)
+    launches_per_step = kernels_per_forward(model, B, S)
 
     cpu = None
     accuracy = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         import oracle
         if strong:
-            cpu, _, _, y_ref = cpu_sampled_rows_estimate(args.config, x_seq=x_host[0].numpy())
+            P2 = C5_PREFIXES[-1]
+            cpu, _, _, y_ref = cpu_chunked_estimate(args.config, x_seq=x_host[0, :P2].numpy())
             acc = oracle.compare_outputs(y_ref, y_check.numpy())
-            sample = f"rows {SAMPLED_ROWS} of sequence 0 (exact sampled-row restatement)"
+            sample = (f"rows {P2 - C5_CHUNK}..{P2 - 1} of sequence 0 of the timed forward "
+                      f"(exact chunked restatement, oracle.chunk_rows_forward)")
         else:
             cpu, _, Bs, y_ref = cpu_forward_rate(args.config)
             acc = oracle.compare_outputs(y_ref, y_check.numpy())
             sample = f"sequences 0..{Bs - 1} of the timed input"
         accuracy = {"max_abs": acc.max_abs_error, "max_rel": acc.max_relative_error, "failed": acc.failed_elements,
                     "total": acc.total_elements, "rule": "atol 0.002 OR rtol 0.02 (reference harness)",
-                    "vs": "oracle/ (NumPy fp32 restatement of the reference module)", "sample": sample}
+                    "vs": "oracle/ (NumPy fp32 restatement of the reference module)", "sample": sample,
+                    "gelu": oracle.gelu_as_max_error()}
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_total / args.steps, "higher_is_better": True,
                 "scaling": "strong" if args.config in STRONG else "weak", "vs_baseline": None,
                 "dtype": "f16 operands / f32 accumulate, f32 in-out",
                 "data": "synthetic (seeded N(0,1) input, seeded default init)",
-                "config": dict(config_dict(args.config, world), strategy=model.last_strategy),
+                "config": config_dict(args.config, world), "strategy": model.last_strategy,
                 "e2e": {"value": e2e_value, "unit": "tokens/s", "ms_per_step": e2e_ms / args.steps,
                         "h2d_bytes_per_step": x_host.numel() * 4, "d2h_bytes_per_step": y_host.numel() * 4,
                         "api": "UserOptimizedTransformer.forward_host (pinned host in/out, upload/forward/"
                                "download overlapped across steps, L2 flushed before each forward)",
                         "outputs_match_device_path": bool(ok_e2e),
+                        "outputs_checked": ("rows " + ",".join(str(int(v)) for v in pos.tolist()) +
+                                            " of every sequence" if strong else "all") +
+                                           " of the last download vs the device path's output (bitwise)",
                         "serial": None if e2e_serial_ms is None else {
                             "value": tokens_all * args.steps / (e2e_serial_ms / 1e3),
                             "ms_per_step": e2e_serial_ms / args.steps,
@@ -486,12 +552,29 @@ def main():
     return 0
 
 
-def kernels_per_forward(model):
-    strat = model.last_strategy
-    nl = model.config.num_layers
+def kernels_per_forward(model, B, S, masked=True):
+    """Launches of the library's kernels per forward (the host code of
+    b200_block_forward / b200_block_forward_chunked, counted per layer)."""
+    cfg = model.config
+    strat, nl, d = model.last_strategy, cfg.num_layers, cfg.d_model
+    mask = (1 + (0 if cfg.causal else 1)) if masked else 0  # b200_mask_finish (+ b200_mask_prepare)
     if strat == "fused_small":
-        return nl
-    return 8 * nl if nl == 1 else 7 * nl + 1
+        return 1  # the whole model in one kernel; it reads the mask itself
+    fuse = d == 128  # residual GEMM + following LayerNorm in one kernel
+    # LN1, QKV, attention, out_proj (+LN2), ffn_in, ffn_out (+final LN)
+    mid = 6 if fuse else 7          # a layer without the final norm
+    last = 6 if fuse else 8         # the last layer (final norm)
+    per_model = mid * (nl - 1) + last
+    if strat == "chunked":          # per chunk: Q and K|V are two GEMMs
+        rows = model._chunk_plan[(B, S, torch_device_index(model))]
+        chunks = B * (-(-S // rows))
+        per_model = chunks * ((mid + 1) * (nl - 1) + last + 1)
+    return per_model + mask
+
+
+def torch_device_index(model):
+    import torch
+    return torch.cuda.current_device()
 
 
 def measured_traffic(cfg_name, kernel):

@@ -18,12 +18,15 @@ from .transformer_oracle import (  # noqa: F401
     OracleConfig,
     block_forward,
     causal_attention,
+    chunk_rows_forward,
     gelu_erf,
     layer_norm,
     linear,
     model_forward,
+    prefix_kv,
     sampled_rows_forward,
 )
+from .kernel_gelu import gelu_as_f32, gelu_as_max_error  # noqa: F401
 from .harness import (  # noqa: F401
     AccuracyResult,
     compare_outputs,

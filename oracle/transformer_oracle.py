@@ -219,3 +219,50 @@ def sampled_rows_forward(params: Dict[str, np.ndarray], num_heads: int, x_seq: n
     x2 = x1 + linear(gelu_erf(linear(n2, g("ffn_in.weight"), g("ffn_in.bias"))),
                      g("ffn_out.weight"), g("ffn_out.bias"))
     return layer_norm(x2, _p(params, "final_norm.weight", dt), _p(params, "final_norm.bias", dt))
+
+
+def prefix_kv(params: Dict[str, np.ndarray], x_seq: np.ndarray, c1: int, dtype=np.float32) -> tuple:
+    """K and V ([c1, d] each) of the first ``c1`` rows of one sequence: LN1, then the
+    k/v projections (TTB:110-112) -- the K/V cache of the reference's chunked forward."""
+    dt = np.dtype(dtype)
+    g = lambda n: _p(params, "layers.0." + n, dt)  # noqa: E731
+    n1p = layer_norm(np.asarray(x_seq)[:c1].astype(dt), g("norm1.weight"), g("norm1.bias"))
+    return (linear(n1p, g("attention.k_proj.weight"), g("attention.k_proj.bias")),
+            linear(n1p, g("attention.v_proj.weight"), g("attention.v_proj.bias")))
+
+
+def chunk_rows_forward(params: Dict[str, np.ndarray], num_heads: int, x_seq: np.ndarray, c0: int, c1: int,
+                       kv: Optional[tuple] = None, dtype=np.float32) -> np.ndarray:
+    """Exact one-layer causal output for the query chunk ``[c0, c1)`` of ONE sequence.
+
+    The body of the reference's sequence-chunked forward (TTB:1378-1609) for one
+    chunk, in fp32 and with the rows of the chunk processed together: LN1 and the
+    K/V projections over the prefix ``0..c1`` (or ``kv = (K, V)`` already
+    computed, ``[>= c1, d]``), the chunk's queries, a bottom-right-aligned causal
+    softmax over the prefix (query ``c0 + i`` sees keys ``0..c0 + i``,
+    TTB:1491-1500), then out_proj, residual, LN2, FFN, residual and final_norm
+    -- the same operations as :func:`model_forward` restricted to the chunk's rows.
+    x_seq: [S, d].  Returns [c1 - c0, d]."""
+    x_seq = np.asarray(x_seq)
+    d = x_seq.shape[-1]
+    H = num_heads
+    hd = d // H
+    dt = np.dtype(dtype)
+    g = lambda n: _p(params, "layers.0." + n, dt)  # noqa: E731
+    kk, vv = prefix_kv(params, x_seq, c1, dt) if kv is None else kv
+    xr = x_seq[c0:c1].astype(dt)
+    n1r = layer_norm(xr, g("norm1.weight"), g("norm1.bias"))
+    q = linear(n1r, g("attention.q_proj.weight"), g("attention.q_proj.bias"))
+    scale = dt.type(hd ** -0.5)
+    masked = np.arange(c1)[None, :] > (c0 + np.arange(c1 - c0))[:, None]
+    ctx = np.empty((c1 - c0, d), dtype=dt)
+    for h in range(H):
+        sl = slice(h * hd, (h + 1) * hd)
+        s = (q[:, sl] @ kk[:c1, sl].T) * scale
+        s = np.where(masked, dt.type(-np.inf), s)
+        ctx[:, sl] = _softmax_lastdim(s.astype(np.float32 if dt == np.float32 else dt)).astype(dt) @ vv[:c1, sl]
+    x1 = xr + linear(ctx, g("attention.out_proj.weight"), g("attention.out_proj.bias"))
+    n2 = layer_norm(x1, g("norm2.weight"), g("norm2.bias"))
+    x2 = x1 + linear(gelu_erf(linear(n2, g("ffn_in.weight"), g("ffn_in.bias"))),
+                     g("ffn_out.weight"), g("ffn_out.bias"))
+    return layer_norm(x2, _p(params, "final_norm.weight", dt), _p(params, "final_norm.bias", dt))

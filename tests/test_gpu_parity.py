@@ -233,3 +233,26 @@ def test_noncausal_against_oracle(tt, B, S, d, H, F, L):
                                oracle.OracleConfig(B, S, d, H, F, L, False), x.numpy())
     res = oracle.compare_outputs(ref, y, rtol=RTOL, atol=ATOL)
     assert res.passed, res
+
+
+def test_auto_routed_chunked_equals_forced_chunked(tt, pkg):
+    """The memory gate's route (budget lowered so that only 256-row chunks fit) gives
+    bit-identical outputs to a forced chunked call with the same chunk, and both pass the
+    oracle (the reference's check 2, experiments/g7_0_chunked_oversize.py:19-22)."""
+    rt = pkg.runtime
+    B, S, d, H, F = 2, 1024, 256, 4, 1024
+    auto, _ = _model(tt, B, S, d, H, F, 1, seed=9)
+    budget = rt.chunked_workspace_bytes(B * S, 256, d, F)
+    assert budget < rt.block_workspace_bytes(B * S, d, F)
+    auto._memory_budget = lambda device: budget
+    forced, _ = _model(tt, B, S, d, H, F, 1, seed=9)
+    forced.force_strategy, forced.chunk_rows = "chunked", 256
+    x, _ = oracle.generate_random_case(B, S, d, 17)
+    ya = _run(auto, x)
+    assert auto.last_strategy == "chunked" and auto._chunk_plan[(B, S, torch.cuda.current_device())] == 256
+    yf = _run(forced, x)
+    assert torch.equal(ya, yf)
+    ref = oracle.model_forward(oracle.params_from_state_dict(auto.state_dict()),
+                               oracle.OracleConfig(B, S, d, H, F, 1, True), x.numpy())
+    res = oracle.compare_outputs(ref, ya, rtol=RTOL, atol=ATOL)
+    assert res.passed, res
