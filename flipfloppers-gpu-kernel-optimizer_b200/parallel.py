@@ -11,9 +11,13 @@ block admits:
 * **tensor parallelism** (:class:`TensorParallelTransformer`): heads are split
   across the ranks of a TP group -- QKV column-parallel, attention on local
   heads, out_proj row-parallel -- then ffn_in column-parallel and ffn_out
-  row-parallel.  Each row-parallel GEMM yields an fp32 partial ``[M, d]`` that
-  one NCCL all-reduce (sum) completes; bias, residual and the next LayerNorm
-  run once, after it, in one fused kernel.
+  row-parallel.  Each row-parallel GEMM yields an fp32 partial that one NCCL
+  all-reduce (sum) completes; bias, residual and the next LayerNorm run once,
+  after it, in one fused kernel.  The block runs over query chunks of each
+  sequence with a K/V cache of the local heads, as the reference's
+  sequence-chunked forward does (TTB:1378-1609), and each chunk's two
+  all-reduces run on a side stream while the compute stream works on the next
+  chunks (:func:`tp_schedule`).
 
 :class:`TensorParallelPlan` is the pure host-side part (which heads / FFN
 columns a rank owns, how the reference's ``state_dict`` tensors are sliced);
@@ -23,7 +27,7 @@ it is shared by the GPU executor and the CPU (gloo) tests.
 from __future__ import annotations
 
 from dataclasses import dataclass
-from typing import Dict, List, Optional
+from typing import Dict, List, Optional, Tuple
 
 import torch
 import torch.distributed as dist
@@ -122,82 +126,225 @@ class TensorParallelPlan:
         }
 
 
+
+
+def tp_schedule(n_chunks: int) -> List[Tuple[str, int]]:
+    """Order of the compute stream's stages over the chunks of one layer.
+
+    ``("A", i)``: chunk i's LN1, Q and K/V projections (K/V into the cache),
+    attention on the local heads and the out_proj partial; its all-reduce is
+    then queued on the communication stream.
+    ``("B", i)``: after that all-reduce, residual + bias + LN2 in one kernel, ffn_in
+    + GELU, the ffn_out partial; its all-reduce is queued.
+    ``("F", i)``: after that all-reduce, residual + bias + final LN (or the next
+    layer's input).
+    Pipelined two deep -- A(i), B(i-1), F(i-2) -- so that chunk i's compute runs
+    while chunk i-1's and i-2's all-reduces are in flight.  Every rank issues the
+    collectives in this same order.  Per-chunk buffers alternate between two
+    slots (i % 2): a slot is rewritten by A(i+2) / B(i+2) only after B(i) / F(i),
+    the last readers of chunk i's partial sums, are on the compute stream."""
+    out: List[Tuple[str, int]] = []
+    for i in range(n_chunks + 2):
+        if i < n_chunks:
+            out.append(("A", i))
+        if 0 <= i - 1 < n_chunks:
+            out.append(("B", i - 1))
+        if 0 <= i - 2 < n_chunks:
+            out.append(("F", i - 2))
+    return out
+
+
+def tp_chunks(batch: int, seq_len: int, chunk_rows: int) -> List[Tuple[int, int, int, int]]:
+    """Query chunks ``(b0, nb, c0, c1)``: sequences ``b0 .. b0+nb-1``, query rows ``[c0, c1)``
+    of each.  Sequences longer than ``chunk_rows`` are cut into prefix chunks (nb = 1,
+    attention over keys ``[0, c1)``); shorter ones are grouped whole, several per chunk.
+    The chunk's rows are contiguous in the ``[batch*seq_len, d]`` layout."""
+    if chunk_rows <= 0:
+        raise ValueError("chunk_rows must be positive")
+    out = []
+    if seq_len >= chunk_rows:
+        for b in range(batch):
+            for c0 in range(0, seq_len, chunk_rows):
+                out.append((b, 1, c0, min(seq_len, c0 + chunk_rows)))
+    else:
+        g = max(1, chunk_rows // seq_len)
+        for b0 in range(0, batch, g):
+            out.append((b0, min(g, batch - b0), 0, seq_len))
+    return out
+
+
 class TensorParallelTransformer:
     """Causal model with heads / FFN columns split across a TP process group (NCCL).
 
-    Per layer on each rank (M = B*S tokens, dl = d/tp, fl = ffn/tp):
-      LN1(x) -> n [M,d] f16 ; QKV GEMM (local rows) -> [M,3dl] ; flash attention
-      on the local heads -> ctx [M,dl] ; out_proj partial ctx.W_o[:,hc]^T -> [M,d]
-      f32 ; all_reduce(sum) ; x1 = x + partial + b_o and n = LN2(x1) (one fused
-      kernel) ; ffn_in local + GELU -> [M,fl] ; ffn_out partial -> [M,d] f32 ;
-      all_reduce(sum) ; x2 = x1 + partial + b_out, then final LayerNorm.
-    Every rank holds the full activations x, x1 (replicated); weights are
-    sharded, so each rank streams 1/tp of them.
+    Per layer and query chunk (R rows, dl = d/tp, fl = ffn/tp), on each rank:
+      A: n = LN1(x) [R,d] f16 ; q = n.Wq[hc]^T [R,dl] ; K|V rows = n.Wkv[hc]^T into the
+         cache [M, 2dl] ; ctx = prefix-causal attention of the local heads [R,dl] ;
+         p1 = ctx.W_o[:,hc]^T [R,d] f32 ; all_reduce(p1) on the side stream
+      B: x1 = x + p1 + b_o and n = LN2(x1) (one kernel) ; h = gelu(n.W_in[fc]^T + b_in[fc])
+         [R,fl] ; p2 = h.W_out[:,fc]^T [R,d] f32 ; all_reduce(p2) on the side stream
+      F: y = LN_f(x1 + p2 + b_out) (one kernel; for a layer before the last, its output)
+    in the order of :func:`tp_schedule`.  Every rank holds the full activations of its
+    sequences (x, x1 and y are replicated across the TP group); weights and the K/V
+    cache are sharded, so each rank streams 1/tp of them.  Weights are sliced once and
+    again only when a parameter changes (the module's own parameter key); buffers are
+    allocated once per shape.  ``comm_ms()`` reports the time the all-reduces of the
+    last call spent on the side stream when built with ``profile_comm=True``.
     """
 
-    def __init__(self, model, tp_rank: int, tp_size: int, group=None):
+    def __init__(self, model, tp_rank: int, tp_size: int, group=None, chunk_rows: int = 16384,
+                 profile_comm: bool = False):
         cfg = model.config
+        if not cfg.causal:
+            raise ValueError("the chunked tensor-parallel forward is causal (prefix chunks)")
         self.model = model
         self.group = group
         self.plan = TensorParallelPlan(cfg.d_model, cfg.num_heads, cfg.ffn_dim, tp_rank, tp_size)
+        dl = cfg.d_model // tp_size
+        if dl % 32 or (cfg.ffn_dim // tp_size) % 32:
+            raise ValueError("d_model / tp and ffn_dim / tp must be multiples of 32 (GEMM granule)")
+        self.chunk_rows = int(chunk_rows)
+        self.profile_comm = profile_comm
         self._weights: Optional[List[Dict[str, torch.Tensor]]] = None
         self._key = None
+        self._bufs: Dict[tuple, Dict[str, object]] = {}
+        self._comm: Dict[int, torch.cuda.Stream] = {}
+        self._comm_events: List[Tuple[torch.cuda.Event, torch.cuda.Event]] = []
 
     def _ensure_weights(self, device):
-        key = (device, tuple((id(p), p._version) for p in self.model.parameters()))
+        key = self.model._param_key(device)
         if key == self._key:
             return
         sd = self.model.state_dict()
         out = []
-        for i in range(self.model.config.num_layers):
-            sh = self.plan.shard_layer(sd, i)
-            out.append({k: (v.detach().to(device, torch.float16) if k.startswith("w_") else
-                            v.detach().to(device, torch.float32)).contiguous() for k, v in sh.items()})
+        with torch.no_grad():
+            for i in range(self.model.config.num_layers):
+                sh = self.plan.shard_layer(sd, i)
+                out.append({k: (v.detach().to(device, torch.float16) if k.startswith("w_") else
+                                v.detach().to(device, torch.float32)).contiguous() for k, v in sh.items()})
+            self._lnf = (self.model.final_norm.weight.detach().to(device, torch.float32).contiguous(),
+                         self.model.final_norm.bias.detach().to(device, torch.float32).contiguous())
         self._weights = out
-        self._lnf = (self.model.final_norm.weight.detach().to(device, torch.float32).contiguous(),
-                     self.model.final_norm.bias.detach().to(device, torch.float32).contiguous())
         self._key = key
 
+    def _buffers(self, B: int, S: int, device) -> Dict[str, object]:
+        key = (B, S, device.index)
+        bufs = self._bufs.get(key)
+        if bufs is not None:
+            return bufs
+        cfg, pl = self.model.config, self.plan
+        d = cfg.d_model
+        dl, fl = d // pl.tp_size, cfg.ffn_dim // pl.tp_size
+        chunks = tp_chunks(B, S, self.chunk_rows)
+        R = max(nb * (c1 - c0) for _, nb, c0, c1 in chunks)
+        e = lambda *shape, dt=torch.float16: torch.empty(*shape, dtype=dt, device=device)  # noqa: E731
+        bufs = {
+            "chunks": chunks,
+            "kv": e(B * S, 2 * dl),
+            "n": e(R, d), "q": e(R, dl), "ctx": e(R, dl), "n2": e(R, d), "h": e(R, fl),
+            "p1": [e(R, d, dt=torch.float32) for _ in range(2)],
+            "x1": [e(R, d, dt=torch.float32) for _ in range(2)],
+            "p2": [e(R, d, dt=torch.float32) for _ in range(2)],
+            "scratch": e(R, d),
+            "xmid": e(B * S, d, dt=torch.float32) if cfg.num_layers > 1 else None,
+            "ev": {k: [torch.cuda.Event() for _ in range(2)] for k in ("a", "b", "c1", "c2")},
+        }
+        self._bufs[key] = bufs
+        return bufs
+
+    def _comm_stream(self, device) -> torch.cuda.Stream:
+        s = self._comm.get(device.index)
+        if s is None:
+            s = torch.cuda.Stream(device=device)
+            self._comm[device.index] = s
+        return s
+
+    def _all_reduce(self, t: torch.Tensor, after: torch.cuda.Event, done: torch.cuda.Event, comm) -> None:
+        comm.wait_event(after)
+        with torch.cuda.stream(comm):
+            if self.profile_comm:
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(comm)
+            dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
+            if self.profile_comm:
+                b.record(comm)
+                self._comm_events.append((a, b))
+        done.record(comm)
+
+    def comm_ms(self) -> float:
+        """Side-stream time (ms) of the last call's all-reduces (needs profile_comm; synchronises)."""
+        torch.cuda.synchronize()
+        return sum(a.elapsed_time(b) for a, b in self._comm_events)
+
     @torch.no_grad()
-    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+    def __call__(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         if not x.is_cuda:
-            raise RuntimeError("TensorParallelTransformer runs on CUDA devices only")
+            raise RuntimeError("TensorParallelTransformer runs on CUDA devices only (no CPU fallback)")
         cfg, pl = self.model.config, self.plan
         B, S, d = x.shape
-        M = B * S
         dev = x.device
         self._ensure_weights(dev)
+        bufs = self._buffers(B, S, dev)
+        comm = self._comm_stream(dev)
+        cur = torch.cuda.current_stream(dev)
+        comm.wait_stream(cur)  # the input (and last call's readers) are ordered before this call
+        self._comm_events = []
         dl, fl, hd, Hl = d // pl.tp_size, cfg.ffn_dim // pl.tp_size, pl.head_dim, pl.local_heads
         eps = float(self.model.layers[0].norm1.eps)
-        xf = x.reshape(M, d).to(torch.float32).contiguous()
-        n = torch.empty(M, d, dtype=torch.float16, device=dev)
-        qkv = torch.empty(M, 3 * dl, dtype=torch.float16, device=dev)
-        ctx = torch.empty(M, dl, dtype=torch.float16, device=dev)
-        part = torch.empty(M, d, dtype=torch.float32, device=dev)
-        x1 = torch.empty(M, d, dtype=torch.float32, device=dev)
-        h = torch.empty(M, fl, dtype=torch.float16, device=dev)
+        xf = x.reshape(B * S, d)
+        if xf.dtype != torch.float32 or not xf.is_contiguous():
+            xf = xf.to(torch.float32).contiguous()
+        y = torch.empty(B * S, d, dtype=torch.float32, device=dev) if out is None else out.reshape(B * S, d)
+        chunks = bufs["chunks"]
+        ev = bufs["ev"]
+        kv = bufs["kv"]
         nl = len(self._weights)
-        y = torch.empty(M, d, dtype=torch.float32, device=dev)
-        cur = xf
-        rt.layernorm(cur, self._weights[0]["ln1_w"], self._weights[0]["ln1_b"], n, eps)
-        for i, w in enumerate(self._weights):
-            rt.gemm(rt.EPI_BIAS_F16, n, w["w_qkv"], w["b_qkv"], qkv)
-            rt.flash_causal(qkv, qkv, qkv, ctx, batch=B, heads=Hl, head_dim=hd, q_len=S, kv_len=S,
-                            q_col0=0, k_col0=dl, v_col0=2 * dl, non_causal=not cfg.causal)
-            rt.gemm(rt.EPI_BIAS_F32, ctx, w["w_o"], None, part)
-            dist.all_reduce(part, op=dist.ReduceOp.SUM, group=self.group)
-            # x1 = x + partial + b_o ; n = LN2(x1)
-            rt.add_layernorm(cur, part, w["b_o"], x1, w["ln2_w"], w["ln2_b"], n, eps)
-            rt.gemm(rt.EPI_BIAS_GELU_F16, n, w["w_in"], w["b_in"], h)
-            rt.gemm(rt.EPI_BIAS_F32, h, w["w_out"], None, part)
-            dist.all_reduce(part, op=dist.ReduceOp.SUM, group=self.group)
-            if i == nl - 1:
-                # x2 = x1 + partial + b_out ; y = final_norm(x2)
-                rt.add_layernorm(x1, part, w["b_out"], x1, self._lnf[0], self._lnf[1], y, eps)
-            else:
-                # x2 = x1 + partial + b_out becomes the next layer's input; n = its LN1(x2)
-                nxt = torch.empty(M, d, dtype=torch.float32, device=dev)
-                nw = self._weights[i + 1]
-                rt.add_layernorm(x1, part, w["b_out"], nxt, nw["ln1_w"], nw["ln1_b"], n, eps)
-                cur = nxt
+        for li, w in enumerate(self._weights):
+            last = li == nl - 1
+            src = xf if li == 0 else bufs["xmid"]
+            dst = y if last else bufs["xmid"]  # in place for middle layers: a chunk's rows are
+            #                                    rewritten by F only after A and B have read them
+            wq, bq = w["w_qkv"][:dl], w["b_qkv"][:dl]
+            wkv, bkv = w["w_qkv"][dl:], w["b_qkv"][dl:]
+
+            def rows_of(i):
+                b0, nb, c0, c1 = chunks[i]
+                r0 = b0 * S + c0
+                return r0, r0 + nb * (c1 - c0)
+
+            for stage, i in tp_schedule(len(chunks)):
+                b0, nb, c0, c1 = chunks[i]
+                r0, r1 = rows_of(i)
+                R = r1 - r0
+                sl = i % 2
+                if stage == "A":
+                    n, q, ctx, p1 = bufs["n"][:R], bufs["q"][:R], bufs["ctx"][:R], bufs["p1"][sl][:R]
+                    rt.layernorm(src[r0:r1], w["ln1_w"], w["ln1_b"], n, eps)
+                    rt.gemm(rt.EPI_BIAS_F16, n, wq, bq, q)
+                    rt.gemm(rt.EPI_BIAS_F16, n, wkv, bkv, kv[r0:r1])
+                    # keys of the chunk's sequences up to its last row; the cache ends there, so the
+                    # key tile that straddles it reads zeros instead of rows not written yet
+                    kvv = kv[: r1]
+                    qlen = c1 - c0
+                    rt.flash_causal(q, kvv, kvv, ctx, batch=nb, heads=Hl, head_dim=hd, q_len=qlen,
+                                    kv_len=c1, q_offset=c0, q_seq_rows=qlen, kv_seq_rows=S, q_col0=0,
+                                    k_col0=0, v_col0=dl, kv_row0=b0 * S, out_seq_rows=qlen)
+                    rt.gemm(rt.EPI_BIAS_F32, ctx, w["w_o"], None, p1)
+                    ev["a"][sl].record(cur)
+                    self._all_reduce(bufs["p1"][sl][:R], ev["a"][sl], ev["c1"][sl], comm)
+                elif stage == "B":
+                    cur.wait_event(ev["c1"][sl])
+                    n2, h, x1, p2 = bufs["n2"][:R], bufs["h"][:R], bufs["x1"][sl][:R], bufs["p2"][sl][:R]
+                    rt.add_layernorm(src[r0:r1], bufs["p1"][sl][:R], w["b_o"], x1, w["ln2_w"], w["ln2_b"], n2, eps)
+                    rt.gemm(rt.EPI_BIAS_GELU_F16, n2, w["w_in"], w["b_in"], h)
+                    rt.gemm(rt.EPI_BIAS_F32, h, w["w_out"], None, p2)
+                    ev["b"][sl].record(cur)
+                    self._all_reduce(p2, ev["b"][sl], ev["c2"][sl], comm)
+                else:
+                    cur.wait_event(ev["c2"][sl])
+                    x1, p2 = bufs["x1"][sl][:R], bufs["p2"][sl][:R]
+                    if last:
+                        rt.add_layernorm(x1, p2, w["b_out"], x1, self._lnf[0], self._lnf[1], dst[r0:r1], eps)
+                    else:  # the next layer's input; the LayerNorm output goes to a scratch buffer
+                        rt.add_layernorm(x1, p2, w["b_out"], dst[r0:r1], w["ln2_w"], w["ln2_b"],
+                                         bufs["scratch"][:R], eps)
         return y.reshape(B, S, d)
