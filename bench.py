@@ -69,6 +69,10 @@ def parse():
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="C5")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tp", type=int, default=1,
+                    help="tensor-parallel group size (C5): heads / FFN columns split over TP ranks with an NCCL "
+                         "all-reduce per row-parallel projection; the remaining factor of --gpus splits the batch")
+    ap.add_argument("--chunk-rows", type=int, default=16384, help="query rows per chunk of the tensor-parallel forward")
     a = ap.parse_args()
     if a.steps is None:
         a.steps = 10 if a.config in STRONG else 200
@@ -377,6 +381,8 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
+    if args.tp > 1:
+        return run_tp(args, rank, world, dev)
     _, S, d, H, F, L = CONFIGS[args.config]
     B = rank_batch(args.config, rank, world)
     cfg = T.TransformerConfig(B, S, d, H, F, L, True)
@@ -549,6 +555,110 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    return 0
+
+
+def run_tp(args, rank, world, dev):
+    """Tensor-parallel (x batch-sharded) forward of a strong-scaling configuration.
+
+    Ranks [g*tp, (g+1)*tp) form TP group g; the global batch is split over the
+    world/tp groups.  Each rank runs parallel.TensorParallelTransformer (query
+    chunks, K/V cache of its heads, two NCCL all-reduces per chunk on a side
+    stream).  value = tokens of the whole job / max-over-ranks device time."""
+    import torch
+    import torch.distributed as dist
+    import torch_transformer_benchmark as T
+    par = T._pkg.parallel
+    tp = args.tp
+    if world % tp or args.config not in STRONG:
+        raise SystemExit("--tp needs --gpus divisible by it and a strong-scaling config (C5)")
+    dp = world // tp
+    g, tp_rank = rank // tp, rank % tp
+    groups = [dist.new_group(list(range(k * tp, (k + 1) * tp))) for k in range(dp)]
+    Bg, S, d, H, F, L = CONFIGS[args.config]
+    sl = par.batch_shard(Bg, g, dp)
+    B = sl.stop - sl.start
+    cfg = T.TransformerConfig(B, S, d, H, F, L, True)
+    torch.manual_seed(1234)
+    model = T.UserOptimizedTransformer(cfg).to(dev).eval()
+    tpm = par.TensorParallelTransformer(model, tp_rank, tp, group=groups[g], chunk_rows=args.chunk_rows,
+                                        profile_comm=True)
+    # every rank of a TP group holds its group's input (replicated activations)
+    gen = torch.Generator(device=dev).manual_seed(1234 + 100000 + 7919 * g)
+    x = torch.randn(B, S, d, generator=gen, device=dev)
+    y = torch.empty_like(x)
+    stream = torch.cuda.current_stream()
+
+    def max_over_ranks(v):
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    clk = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ else
+                       int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[int(os.environ.get("LOCAL_RANK", "0"))]))
+    clk.start()
+    comm_ms = []
+    with torch.inference_mode():
+        for _ in range(max(args.warmup, 3)):
+            tpm(x, out=y)
+        torch.cuda.synchronize()
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        dist.barrier()
+        torch.cuda.synchronize()
+        torch.cuda._sleep(QUEUE_PREFILL_CYCLES)
+        for i in range(args.steps):
+            starts[i].record(stream)
+            tpm(x, out=y)
+            ends[i].record(stream)
+            comm_ms.append(tpm.comm_ms() if i == args.steps - 1 else None)
+        torch.cuda.synchronize()
+        dist.barrier()
+        step_ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
+        ms_total = max_over_ranks(sum(step_ms))
+        ar_ms = max_over_ranks(comm_ms[-1])
+        last_ms = max_over_ranks(step_ms[-1])
+        # accuracy of one query chunk of the group's first sequence (rank 0, CPU restatement)
+        accuracy = None
+        y_rows = None
+        P2 = C5_PREFIXES[-1]
+        if rank == 0 and not args.no_cpu_baseline:
+            y_rows = y[0, P2 - C5_CHUNK:P2].float().cpu()
+            x_seq = x[0, :P2].float().cpu().numpy()
+    clocks = clk.stop()
+    if rank == 0 and y_rows is not None:
+        import oracle
+        params = oracle.params_from_state_dict(model.state_dict())
+        ref = oracle.chunk_rows_forward(params, H, x_seq, P2 - C5_CHUNK, P2)
+        acc = oracle.compare_outputs(ref, y_rows.numpy())
+        accuracy = {"max_abs": acc.max_abs_error, "max_rel": acc.max_relative_error, "failed": acc.failed_elements,
+                    "total": acc.total_elements, "rule": "atol 0.002 OR rtol 0.02 (reference harness)",
+                    "sample": f"rows {P2 - C5_CHUNK}..{P2 - 1} of the first sequence of TP group 0 "
+                              f"(exact chunked restatement, oracle.chunk_rows_forward)"}
+    if rank == 0:
+        chunks = len(par.tp_chunks(B, S, args.chunk_rows))
+        value = Bg * S * args.steps / (ms_total / 1e3)
+        line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_total / args.steps, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "f16 operands / f32 accumulate, f32 in-out",
+                "data": "synthetic (seeded N(0,1) input, seeded default init)",
+                "config": dict(config_dict(args.config, world),
+                               parallelism=f"tp{tp} x dp{dp} (heads / FFN columns over {tp} ranks, NCCL all-reduce "
+                                           f"after out_proj and ffn_out per {args.chunk_rows}-row query chunk; "
+                                           f"batch over {dp} groups)"),
+                "strategy": "tensor-parallel chunked",
+                "tp": {"size": tp, "dp": dp, "chunk_rows": args.chunk_rows, "chunks_per_rank": chunks,
+                       "allreduce_bytes_per_step_per_rank": 2 * B * S * d * 4 * L,
+                       "allreduce_stream_ms_last_step": ar_ms, "step_ms_last_step": last_ms,
+                       "allreduce_busy_share": ar_ms / last_ms if last_ms else None,
+                       "note": "all-reduce time = CUDA events around each NCCL call on the side stream (max over "
+                               "ranks); it overlaps the compute stream, so the share is busy time, not exposed time"},
+                "e2e": None, "roofline": None, "cpu_baseline": None, "accuracy": accuracy, "clocks": clocks,
+                "gpu_launches": (9 * chunks * L) * args.steps}
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    del groups
+    dist.destroy_process_group()
     return 0
 
 

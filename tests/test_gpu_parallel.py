@@ -98,13 +98,38 @@ def _tp_child(rank, world, port, mode, q):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
     try:
         par = T._pkg.parallel
-        B, S, d, H, F, L = 4, 256, 256, 4, 1024, 2
+        if mode == "tp_c5":
+            # the C5 head shape (d=1024, 16 heads of 64), 1024-row query chunks over S=4096
+            B, S, d, H, F, L = 2, 4096, 1024, 16, 4096, 1
+        else:
+            B, S, d, H, F, L = 4, 256, 256, 4, 1024, 2
         cfg = T.TransformerConfig(B, S, d, H, F, L, True)
         torch.manual_seed(1234)
         model = T.UserOptimizedTransformer(cfg).to(dev).eval()
         x, _ = oracle.generate_random_case(B, S, d, 77)
+        if mode == "tp_c5":
+            tpm = par.TensorParallelTransformer(model, rank, world, chunk_rows=1024)
+            with torch.inference_mode():
+                yd = tpm(x.to(dev))
+                yd2 = tpm(x.to(dev))  # a second call reuses the buffers and weight slices
+            torch.cuda.synchronize()
+            same = bool(torch.equal(yd, yd2))
+            # every TP rank holds the same (replicated) output
+            cks = torch.tensor([float(yd.double().sum()), float((yd.double() ** 2).sum())], device=dev)
+            allc = [torch.empty_like(cks) for _ in range(world)]
+            dist.all_gather(allc, cks)
+            same = same and all(torch.equal(allc[0], c) for c in allc)
+            y = yd.cpu()
+            params = oracle.params_from_state_dict(model.state_dict())
+            ok, worst = same, 0.0
+            for b, c0, c1 in ((0, 3072, 4096), (1, 0, 1024), (1, 2048, 2560)):
+                ref = oracle.chunk_rows_forward(params, H, x[b].numpy(), c0, c1)
+                res = oracle.compare_outputs(ref, y[b, c0:c1], rtol=RTOL, atol=ATOL)
+                ok, worst = ok and res.passed, max(worst, res.max_abs_error)
+            q.put((rank, ok, worst))
+            return
         if mode == "tp":
-            y = par.TensorParallelTransformer(model, rank, world)(x.to(dev)).cpu()
+            y = par.TensorParallelTransformer(model, rank, world, chunk_rows=128)(x.to(dev)).cpu()
         else:
             sl = par.batch_shard(B, rank, world)
             y = par.BatchShardedTransformer(model, rank, world)(x[sl].to(dev).contiguous(), gather=True, batch=B).cpu()
@@ -131,12 +156,12 @@ def _spawn(world, mode):
     assert all(r[1] for r in res), res
 
 
-@pytest.mark.parametrize("mode", ["tp", "batch"])
+@pytest.mark.parametrize("mode", ["tp", "batch", "tp_c5"])
 def test_single_rank_process_group(mode):
     _spawn(1, mode)
 
 
-@pytest.mark.parametrize("mode", ["tp", "batch"])
+@pytest.mark.parametrize("mode", ["tp", "batch", "tp_c5"])
 def test_two_ranks(mode):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
