@@ -26,6 +26,7 @@ it is shared by the GPU executor and the CPU (gloo) tests.
 
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 from typing import Dict, List, Optional, Tuple
 
@@ -252,9 +253,14 @@ class TensorParallelTransformer:
         return bufs
 
     def _comm_stream(self, device) -> torch.cuda.Stream:
+        """The side stream of the all-reduces, at the highest priority: as the attention
+        kernel's CTAs (one per SM) retire, the block scheduler places NCCL's blocks first
+        instead of the next compute CTAs, so a chunk's reduce is not starved by the next
+        chunk's compute (B200_TP_COMM_PRIORITY=0 gives it normal priority)."""
         s = self._comm.get(device.index)
         if s is None:
-            s = torch.cuda.Stream(device=device)
+            hi = os.environ.get("B200_TP_COMM_PRIORITY", "1") != "0"
+            s = torch.cuda.Stream(device=device, priority=-1 if hi else 0)
             self._comm[device.index] = s
         return s
 
