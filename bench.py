@@ -75,7 +75,7 @@ def parse():
     ap.add_argument("--tp", type=int, default=1,
                     help="tensor-parallel group size (C5): heads / FFN columns split over TP ranks with an NCCL "
                          "all-reduce per row-parallel projection; the remaining factor of --gpus splits the batch")
-    ap.add_argument("--chunk-rows", type=int, default=16384, help="query rows per chunk of the tensor-parallel forward")
+    ap.add_argument("--chunk-rows", type=int, default=32768, help="query rows per chunk of the tensor-parallel forward")
     a = ap.parse_args()
     if a.steps is None:
         a.steps = 10 if a.config in STRONG else 200

@@ -192,7 +192,7 @@ class TensorParallelTransformer:
     last call spent on the side stream when built with ``profile_comm=True``.
     """
 
-    def __init__(self, model, tp_rank: int, tp_size: int, group=None, chunk_rows: int = 16384,
+    def __init__(self, model, tp_rank: int, tp_size: int, group=None, chunk_rows: int = 32768,
                  profile_comm: bool = False):
         cfg = model.config
         if not cfg.causal:
