@@ -165,8 +165,26 @@ __global__ void __launch_bounds__(256)
 __device__ __forceinline__ void mask_scan(const unsigned char* __restrict__ m, int S, int& count, bool& holes) {
   int c = 0;
   bool h = false;
-#pragma unroll 4
-  for (int i = threadIdx.x; i < S; i += blockDim.x) {
+  int i0 = 0;  // first byte left to the scalar loop
+  if ((reinterpret_cast<uintptr_t>(m) & 15u) == 0) {
+    // 16 bytes per thread and step; byte k of a chunk is valid if nonzero, and a hole is a
+    // valid byte after a padded one (the byte before the chunk comes from a scalar load)
+    const int nv = S >> 4;
+    for (int v = threadIdx.x; v < nv; v += blockDim.x) {
+      const uint4 q = reinterpret_cast<const uint4*>(m)[v];
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+      bool prev = v > 0 ? m[16 * v - 1] != 0 : true;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const bool cur = ((w[k >> 2] >> (8 * (k & 3))) & 0xffu) != 0;
+        c += cur;
+        h |= cur && !prev;
+        prev = cur;
+      }
+    }
+    i0 = nv << 4;
+  }
+  for (int i = i0 + threadIdx.x; i < S; i += blockDim.x) {
     const bool v = m[i] != 0;
     c += v;
     if (v && i > 0 && m[i - 1] == 0) h = true;
