@@ -54,8 +54,10 @@ class BatchShardedTransformer:
     def local_slice(self, batch: int) -> slice:
         return batch_shard(batch, self.rank, self.world)
 
-    def __call__(self, x_local: torch.Tensor, gather: bool = False, batch: Optional[int] = None) -> torch.Tensor:
-        y = self.model(x_local)
+    def __call__(self, x_local: torch.Tensor, gather: bool = False, batch: Optional[int] = None,
+                 valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """``x_local`` / ``valid_token_mask``: this rank's batch slice (the mask as in the module's forward)."""
+        y = self.model(x_local, valid_token_mask)
         if not gather or self.world == 1:
             return y
         batch = batch if batch is not None else x_local.shape[0] * self.world
@@ -282,12 +284,18 @@ class TensorParallelTransformer:
         return sum(a.elapsed_time(b) for a, b in self._comm_events)
 
     @torch.no_grad()
-    def __call__(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    def __call__(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None,
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """y = model(x, valid_token_mask) with the work split over the TP group.  A
+        prefix-valid key-padding mask needs no change to the causal forward (a valid row
+        never sees a padded key); its padded rows are zeroed at the end by the device-side
+        mask kernel, which also turns a sequence whose mask has a hole into NaN rows."""
         if not x.is_cuda:
             raise RuntimeError("TensorParallelTransformer runs on CUDA devices only (no CPU fallback)")
         cfg, pl = self.model.config, self.plan
         B, S, d = x.shape
         dev = x.device
+        mask = self.model._mask_bytes(valid_token_mask, B, S, dev)
         self._ensure_weights(dev)
         bufs = self._buffers(B, S, dev)
         comm = self._comm_stream(dev)
@@ -353,4 +361,6 @@ class TensorParallelTransformer:
                     else:  # the next layer's input; the LayerNorm output goes to a scratch buffer
                         rt.add_layernorm(x1, p2, w["b_out"], dst[r0:r1], w["ln2_w"], w["ln2_b"],
                                          bufs["scratch"][:R], eps)
+        if mask is not None:
+            rt.mask_finish(y, mask)
         return y.reshape(B, S, d)

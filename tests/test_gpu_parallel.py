@@ -128,15 +128,18 @@ def _tp_child(rank, world, port, mode, q):
                 ok, worst = ok and res.passed, max(worst, res.max_abs_error)
             q.put((rank, ok, worst))
             return
+        # prefix-valid key padding, as the reference harness generates it with --padding-ratio
+        x, mask = oracle.generate_random_case(B, S, d, 77, padding_ratio=0.3)
         if mode == "tp":
-            y = par.TensorParallelTransformer(model, rank, world, chunk_rows=128)(x.to(dev)).cpu()
+            y = par.TensorParallelTransformer(model, rank, world, chunk_rows=128)(x.to(dev), mask.to(dev)).cpu()
         else:
             sl = par.batch_shard(B, rank, world)
-            y = par.BatchShardedTransformer(model, rank, world)(x[sl].to(dev).contiguous(), gather=True, batch=B).cpu()
+            y = par.BatchShardedTransformer(model, rank, world)(x[sl].to(dev).contiguous(), gather=True, batch=B,
+                                                               valid_token_mask=mask[sl].to(dev)).cpu()
         ref = oracle.model_forward(oracle.params_from_state_dict(model.state_dict()),
-                                   oracle.OracleConfig(B, S, d, H, F, L, True), x.numpy())
+                                   oracle.OracleConfig(B, S, d, H, F, L, True), x.numpy(), mask.numpy())
         res = oracle.compare_outputs(ref, y, rtol=RTOL, atol=ATOL)
-        q.put((rank, res.passed, res.max_abs_error))
+        q.put((rank, res.passed and bool(torch.all(y[~mask] == 0)), res.max_abs_error))
     finally:
         dist.destroy_process_group()
 
