@@ -307,7 +307,10 @@ class TensorParallelTransformer:
         xf = x.reshape(B * S, d)
         if xf.dtype != torch.float32 or not xf.is_contiguous():
             xf = xf.to(torch.float32).contiguous()
-        y = torch.empty(B * S, d, dtype=torch.float32, device=dev) if out is None else out.reshape(B * S, d)
+        if out is not None and (out.dtype != torch.float32 or not out.is_contiguous() or out.numel() != B * S * d
+                                or out.device != dev):
+            raise ValueError("out must be a contiguous float32 tensor of x's shape on x's device")
+        y = torch.empty(B * S, d, dtype=torch.float32, device=dev) if out is None else out.view(B * S, d)
         chunks = bufs["chunks"]
         ev = bufs["ev"]
         kv = bufs["kv"]
