@@ -675,7 +675,7 @@ def kernels_per_forward(model, B, S, masked=True):
     b200_block_forward / b200_block_forward_chunked, counted per layer)."""
     cfg = model.config
     strat, nl, d = model.last_strategy, cfg.num_layers, cfg.d_model
-    mask = (1 + (0 if cfg.causal else 1)) if masked else 0  # b200_mask_finish (+ b200_mask_prepare)
+    mask = 2 if masked else 0  # b200_mask_prepare + b200_zero_masked_rows
     if strat == "fused_small":
         return 1  # the whole model in one kernel; it reads the mask itself
     fuse = d == 128  # residual GEMM + following LayerNorm in one kernel

@@ -93,8 +93,37 @@ struct AttnParams {
   int out_seq_rows;      // rows between consecutive sequences in out
   float scale_log2;      // head_dim^-0.5 * log2(e)
   int non_causal;        // 1: every query sees every valid key (the reference without --causal)
-  const int* kv_lens;    // per-sequence count of valid keys (key-padding mask), may be null
+  const int* kv_lens;    // per-sequence key count (one past the last valid key; key-padding mask), may be null
+  // key-padding masks that are not prefix-valid: key_holes[b] != 0 marks such a sequence, whose
+  // key validity is read from key_bits[b * key_words + w] (bit i: key 32w + i) -- one 16-byte
+  // group per 128 keys.  Null: every key below the count is valid.
+  const uint32_t* key_bits;
+  int key_words;
+  const int* key_holes;
 };
+
+// Whether sequence b's keys must be tested one by one (its mask has holes).
+__device__ __forceinline__ bool attn_has_holes(const AttnParams& p, int b) {
+  return p.key_holes != nullptr && p.key_holes[b] != 0;
+}
+
+// s[c] = -inf for the keys k0 + c (c < N) that sequence b's mask excludes (N = 64 or 128,
+// k0 a multiple of N)
+template <int N>
+__device__ __forceinline__ void attn_mask_keys(const AttnParams& p, int b, int k0, float (&s)[N]) {
+  const uint32_t* kb = p.key_bits + static_cast<int64_t>(b) * p.key_words + (k0 >> 5);
+  uint32_t w[N / 32];
+  if constexpr (N == 128) {
+    const uint4 q = __ldg(reinterpret_cast<const uint4*>(kb));
+    w[0] = q.x; w[1] = q.y; w[2] = q.z; w[3] = q.w;
+  } else {
+    const uint2 q = __ldg(reinterpret_cast<const uint2*>(kb));
+    w[0] = q.x; w[1] = q.y;
+  }
+#pragma unroll
+  for (int c = 0; c < N; ++c)
+    if (!((w[c >> 5] >> (c & 31)) & 1u)) s[c] = -INFINITY;
+}
 
 // Keys [0, kv_eff) of sequence b are valid (at least one, so a row is never empty).
 __device__ __forceinline__ int attn_kv_eff(const AttnParams& p, int b) {
@@ -154,6 +183,7 @@ __global__ void __launch_bounds__(192, 2)  // two CTAs per SM (registers <= 170)
   const int q_first = p.q_offset + qt * 128;
   const int q_last = p.q_offset + min(p.q_len, (qt + 1) * 128) - 1;
   const int kv_eff = attn_kv_eff(p, b);
+  const bool holes = attn_has_holes(p, b);
   const int nkt = p.non_causal ? (kv_eff + BN - 1) / BN : min(q_last / BN + 1, (kv_eff + BN - 1) / BN);
 
   if (threadIdx.x == 0) {
@@ -289,6 +319,7 @@ __global__ void __launch_bounds__(192, 2)  // two CTAs per SM (registers <= 170)
         for (int c = 0; c < BN; ++c)
           if (k0 + c > klim) s[c] = -INFINITY;
       }
+      if (holes) attn_mask_keys<BN>(p, b, k0, s);
       const float m_new = fmaxf(m, row_max<BN>(s) * p.scale_log2);
       // rows with nothing visible yet keep p = 0 (cannot happen for real rows: key 0 is always visible)
       const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
@@ -333,7 +364,7 @@ __global__ void __launch_bounds__(192, 2)  // two CTAs per SM (registers <= 170)
     if (ok) ok = mbar_wait_warp(pv_done, (nkt - 1) & 1, abort_flag, DERR_WAIT_MMA);
     if (ok && !*abort_flag) {
       tc_fence_after();
-      const float inv_l = 1.f / l;
+      const float inv_l = l > 0.f ? 1.f / l : 0.f;  // a row whose visible keys are all masked: context 0
       const int row_in_seq = qt * 128 + rl;
       __half* orow = p.out + (static_cast<int64_t>(b) * p.out_seq_rows + row_in_seq) * p.ld_out + h * HD;
 #pragma unroll 1

@@ -69,6 +69,7 @@ __global__ void __launch_bounds__(320, 1)
   const int qp = npair - 1 - static_cast<int>(blockIdx.x);  // latest query rows first
   const int h = blockIdx.y, b = blockIdx.z;
   const int kv_eff = attn_kv_eff(p, b);
+  const bool holes = attn_has_holes(p, b);
   const int kv_tiles = (kv_eff + C::BN - 1) / C::BN;
   // key tiles each query tile needs (0 if the tile holds no query row)
   int ntile[2];
@@ -241,6 +242,7 @@ __global__ void __launch_bounds__(320, 1)
           for (int c = 0; c < C::BN; ++c)
             if (k0 + c > klim) s[c] = -INFINITY;
         }
+        if (holes) attn_mask_keys<C::BN>(p, b, k0, s);
         const float mx = row_max<C::BN>(s) * p.scale_log2;
         // lazy rescale: move the reference max only when this tile raises it by more than the threshold
         const bool grow = mx > m_used + C::RESCALE_THRESHOLD;
@@ -289,7 +291,7 @@ __global__ void __launch_bounds__(320, 1)
     if (ok && nt > 0) ok = mbar_wait_warp(&pv_done[t], (nt - 1) & 1, abort_flag, DERR_WAIT_MMA);
     if (ok && nt > 0 && !*abort_flag) {
       tc_fence_after();
-      const float inv_l = 1.f / l;
+      const float inv_l = l > 0.f ? 1.f / l : 0.f;  // a row whose visible keys are all masked: context 0
       __half* orow = p.out + (static_cast<int64_t>(b) * p.out_seq_rows + row_in_seq) * p.ld_out + h * HD;
 #pragma unroll 1
       for (int c = 0; c < HD; c += 32) {

@@ -40,6 +40,8 @@ __global__ void __launch_bounds__(ATTN_SMALL_ROWS)
   const int par = threadIdx.x & 1;                                          // key parity of this thread
   const int i0 = tile * ATTN_SMALL_ROWS + 2 * static_cast<int>(threadIdx.x >> 1);  // rows i0, i0 + 1
   const int kv_eff = attn_kv_eff(p, b);
+  const bool holes = attn_has_holes(p, b);
+  const uint32_t* kbits = holes ? p.key_bits + static_cast<int64_t>(b) * p.key_words : nullptr;
   int klim[2];  // last visible key of each row (-1: row not in this call)
 #pragma unroll
   for (int rr = 0; rr < 2; ++rr) {
@@ -120,9 +122,11 @@ __global__ void __launch_bounds__(ATTN_SMALL_ROWS)
 #pragma unroll
             for (int rr = 0; rr < 2; ++rr) d2[rr] = f2fma(q2[rr][2 * e + 1], kc, f2fma(q2[rr][2 * e], ka, d2[rr]));
           }
+          // a key the sequence's mask excludes scores -inf for both rows
+          const bool kvalid = !holes || ((__ldg(kbits + ((k0 + j) >> 5)) >> ((k0 + j) & 31)) & 1u);
 #pragma unroll
           for (int rr = 0; rr < 2; ++rr) {
-            if (k0 + j <= klim[rr]) {
+            if (kvalid && k0 + j <= klim[rr]) {
               float lo, hi;
               f2upk(d2[rr], lo, hi);
               a[rr] = lo + hi;
@@ -194,7 +198,7 @@ __global__ void __launch_bounds__(ATTN_SMALL_ROWS)
 #pragma unroll
   for (int e = 0; e < HD / 2; ++e) w[e] = par ? o[1][e] : o[0][e];
   if (par) lw = l[1];
-  const float inv_l = 1.f / lw;  // every row sees key 0, so l >= 1
+  const float inv_l = lw > 0.f ? 1.f / lw : 0.f;  // a row whose visible keys are all masked: context 0
   const uint64_t iv = f2pk(inv_l, inv_l);
   uint4* orow = reinterpret_cast<uint4*>(p.out + (static_cast<int64_t>(b) * p.out_seq_rows + i) * p.ld_out + h * HD);
 #pragma unroll

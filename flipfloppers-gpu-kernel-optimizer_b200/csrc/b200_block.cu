@@ -511,6 +511,9 @@ AttnParams attn_params(const B200AttnArgs& a) {
   p.scale_log2 = static_cast<float>(1.4426950408889634 / __builtin_sqrt(static_cast<double>(HD)));
   p.non_causal = a.non_causal;
   p.kv_lens = a.kv_lens;
+  p.key_bits = reinterpret_cast<const uint32_t*>(a.key_bits);
+  p.key_words = a.key_words;
+  p.key_holes = a.key_holes;
   return p;
 }
 
@@ -593,6 +596,11 @@ int attn_impl(const B200AttnArgs* a, cudaStream_t st) {
       a->kv_rows)
     return B200_ERR_ARG;
   if (a->heads > 65535 || a->batch > 65535) return B200_ERR_TILE;
+  if ((a->key_holes == nullptr) != (a->key_bits == nullptr)) return B200_ERR_ARG;
+  if (a->key_bits != nullptr) {
+    if (a->key_words % 4 || a->key_words < 4 * ((a->kv_len + 127) / 128)) return B200_ERR_ARG;
+    if (!al16(a->key_bits)) return B200_ERR_ALIGN;
+  }
   if (int rc = check_arch()) return rc;
   // Two query tiles per CTA (shared K/V loads, one tile's MMA under the other's
   // softmax, alternating exp phases) against one tile per CTA with two CTAs per
@@ -853,6 +861,9 @@ int block_impl(const B200BlockArgs* a, cudaStream_t st) {
   at.out_row0 = 0;
   at.non_causal = a->non_causal;
   at.kv_lens = a->kv_lens;
+  at.key_bits = a->key_bits;
+  at.key_words = a->key_words;
+  at.key_holes = a->key_holes;
   if ((rc = attn_impl(&at, st))) return rc;
   // 4. x1 = x + ctx . Wo^T + bo  (res += ...);  5. n = LN2(x1) -- one kernel when d == 128
   if (fuse_ln(d)) {
@@ -979,6 +990,11 @@ int block_chunked_impl(const B200BlockArgs* a, int chunk_rows, cudaStream_t st) 
       at.ld_out = d;
       at.out_seq_rows = Rc;
       at.out_row0 = 0;
+      if (a->key_holes != nullptr) {  // this sequence's key-padding mask (a one-sequence call)
+        at.key_bits = a->key_bits + static_cast<size_t>(b) * a->key_words;
+        at.key_words = a->key_words;
+        at.key_holes = a->key_holes + b;
+      }
       if ((rc = attn_impl(&at, st))) return rc;
       if (fuse_ln(d)) {
         if ((rc = gemm_ln_impl(w.ctx, d, a->w_o, d, a->b_o, res, d, a->ln2_w, a->ln2_b, a->eps, w.n, d, 1, Rc, d, d,
@@ -1078,25 +1094,23 @@ int b200_zero_masked_rows(float* y, const unsigned char* row_valid, long long ro
   if (!y || !row_valid || rows < 0 || d <= 0) return B200_ERR_ARG;
   if (rows == 0) return B200_OK;
   if (int rc = check_arch()) return rc;
-  launch_kernel(k_zero_masked_rows, dim3(static_cast<unsigned>((rows + 7) / 8)), dim3(256), 0,
-                static_cast<cudaStream_t>(stream), y, row_valid, rows, d);
+  const int vec4 = (d % 4 == 0 && al16(y)) ? 1 : 0;
+  launch_kernel(k_mask_finish, dim3(static_cast<unsigned>((rows + 7) / 8)), dim3(256), 0,
+                static_cast<cudaStream_t>(stream), y, row_valid, rows, d, vec4);
   return launch_status();
 }
 
-int b200_mask_prepare(const unsigned char* mask, int batch, int seq_len, int* kv_lens, b200_stream_t stream) {
+int b200_mask_key_words(int seq_len) { return seq_len > 0 ? 4 * ((seq_len + 127) / 128) : 0; }
+
+int b200_mask_prepare(const unsigned char* mask, int batch, int seq_len, int* kv_lens, int* key_holes,
+                      unsigned int* key_bits, b200_stream_t stream) {
   if (!mask || !kv_lens || batch <= 0 || seq_len <= 0) return B200_ERR_ARG;
+  if ((key_holes == nullptr) != (key_bits == nullptr)) return B200_ERR_ARG;
+  if (key_bits != nullptr && !al16(key_bits)) return B200_ERR_ALIGN;
   if (int rc = check_arch()) return rc;
   launch_kernel(k_mask_prepare, dim3(static_cast<unsigned>(batch)), dim3(256), 0, static_cast<cudaStream_t>(stream),
-                mask, seq_len, kv_lens);
-  return launch_status();
-}
-
-int b200_mask_finish(float* y, const unsigned char* mask, int batch, int seq_len, int d, b200_stream_t stream) {
-  if (!y || !mask || batch <= 0 || seq_len <= 0 || d <= 0) return B200_ERR_ARG;
-  if (int rc = check_arch()) return rc;
-  const int vec4 = (d % 4 == 0 && al16(y)) ? 1 : 0;
-  launch_kernel(k_mask_finish, dim3(static_cast<unsigned>(batch)), dim3(256), 0, static_cast<cudaStream_t>(stream),
-                y, mask, seq_len, d, vec4);
+                mask, seq_len, kv_lens, key_holes, reinterpret_cast<uint32_t*>(key_bits),
+                b200_mask_key_words(seq_len));
   return launch_status();
 }
 

@@ -29,7 +29,6 @@ enum DeviceErr : int {
   DERR_WAIT_SOFTMAX = 4,  // MMA issuer gave up waiting for P
   DERR_WAIT_DRAIN = 5,    // teardown gave up draining in-flight work
   DERR_WAIT_GRID = 6,     // cross-CTA flag wait gave up
-  DERR_MASK_HOLES = 7,    // key-padding mask not prefix-valid on a path that needs it (outputs NaN)
 };
 
 #ifndef B200_WAIT_TIMEOUT_NS

@@ -160,7 +160,7 @@ class UserOptimizedTransformer(nn.Module):
         self.chunk_rows: Optional[int] = None      # query rows per chunk of the chunked strategy (None: gate decides)
         self._chunk_plan: Dict[Tuple, int] = {}
         self._ws: Dict[Tuple, torch.Tensor] = {}
-        self._kv_lens: Dict[Tuple, torch.Tensor] = {}
+        self._mask_bufs: Dict[Tuple, Tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = {}
         self._plan: Dict[Tuple, str] = {}
         self._graphs: "OrderedDict[Tuple, torch.cuda.CUDAGraph]" = OrderedDict()
         self._warm: set = set()
@@ -241,12 +241,10 @@ class UserOptimizedTransformer(nn.Module):
 
         The kernels read these bytes on every call, so a mask edited in place or a new
         mask at a reused address is always seen.  Semantics (TTB:125-128, 140-141,
-        163-164, 190-191): padded keys are excluded from attention and padded rows of
-        the output are 0.  The single-kernel path masks keys one by one and takes any
-        mask; the kernel chain supports prefix-valid masks (valid tokens first, what
-        ``generate_random_case`` produces, TTB:1793-1803) and checks that on the device:
-        a sequence whose mask has a hole comes back as NaN rows with device error
-        ``runtime.DERR_MASK_HOLES`` recorded."""
+        163-164, 190-191), for any mask: padded keys are excluded from attention and
+        padded rows of the output are 0.  The single-kernel path tests each key's byte;
+        the kernel chain gets per-sequence key counts, hole flags and (for masks that are
+        not prefix-valid) packed key bits from ``b200_mask_prepare`` on the device."""
         if m is None:
             return None
         if m.dim() != 2 or tuple(m.shape) != (B, S):
@@ -255,15 +253,18 @@ class UserOptimizedTransformer(nn.Module):
             return m.view(torch.uint8)
         return m.to(device=device, dtype=torch.bool).contiguous().view(torch.uint8)
 
-    def _kv_lens_buffer(self, B: int, device: torch.device) -> torch.Tensor:
-        """Per-sequence valid-key counts (int32 [B]) that ``b200_mask_prepare`` fills on the device."""
-        key = (B, device.index)
-        buf = self._kv_lens.get(key)
-        if buf is None:
-            self._graphs.clear()  # captured graphs point at the old buffer
-            buf = torch.zeros(B, dtype=torch.int32, device=device)
-            self._kv_lens[key] = buf
-        return buf
+    def _mask_buffers(self, B: int, S: int, device: torch.device) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """Device buffers ``b200_mask_prepare`` fills every call: per-sequence key counts and
+        hole flags (int32 [B]) and packed key bits (int32 [B, 4 * ceil(S / 128)])."""
+        key = (B, S, device.index)
+        bufs = self._mask_bufs.get(key)
+        if bufs is None:
+            self._graphs.clear()  # captured graphs point at the old buffers
+            bufs = (torch.zeros(B, dtype=torch.int32, device=device),
+                    torch.zeros(B, dtype=torch.int32, device=device),
+                    torch.zeros(B, rt.mask_key_words(S), dtype=torch.int32, device=device))
+            self._mask_bufs[key] = bufs
+        return bufs
 
     def _fused_small_eligible(self) -> bool:
         """Shapes the single-kernel whole-model path takes: the tensor-core kernels
@@ -399,23 +400,23 @@ class UserOptimizedTransformer(nn.Module):
     def _launch(self, x: torch.Tensor, y: torch.Tensor, ws: torch.Tensor, strat: str,
                 mask: Optional[torch.Tensor] = None) -> None:
         """Launch the forward on the current stream.  With a mask: the single kernel masks
-        keys and rows itself; the chain gets per-sequence key counts from the device
-        (non-causal attention; causal attention of a valid row under a prefix-valid mask
-        never reaches a padded key) and a last kernel that zeroes padded rows and turns
-        a mask with holes into NaN rows plus a device error."""
+        keys and rows itself; for the chain, ``b200_mask_prepare`` turns the mask into the
+        attention kernels' key counts, hole flags and key bits on the device, and the
+        padded rows of the output are zeroed last."""
         B, S, _ = x.shape
         if strat == "fused_small":
             self._forward_fused_small(x, y, mask)
             return
-        kv_lens = None
-        if mask is not None and not self.config.causal:
-            kv_lens = rt.mask_prepare(mask, self._kv_lens_buffer(B, x.device))
-        if strat == "chunked":
-            self._forward_chain(x, y, ws, chunk_rows=self._chunk_plan[(B, S, x.device.index)])
-        else:
-            self._forward_chain(x, y, ws, kv_lens=kv_lens)
+        keys = None
         if mask is not None:
-            rt.mask_finish(y, mask)
+            keys = self._mask_buffers(B, S, x.device)
+            rt.mask_prepare(mask, *keys)
+        if strat == "chunked":
+            self._forward_chain(x, y, ws, chunk_rows=self._chunk_plan[(B, S, x.device.index)], keys=keys)
+        else:
+            self._forward_chain(x, y, ws, keys=keys)
+        if mask is not None:
+            rt.zero_masked_rows(y, mask)
 
     def _forward_fused_small(self, x: torch.Tensor, y: torch.Tensor,
                              mask: Optional[torch.Tensor] = None) -> None:
@@ -436,7 +437,9 @@ class UserOptimizedTransformer(nn.Module):
         rt.fused_small(a)
 
     def _forward_chain(self, x: torch.Tensor, y: torch.Tensor, ws: torch.Tensor,
-                       chunk_rows: Optional[int] = None, kv_lens: Optional[torch.Tensor] = None) -> None:
+                       chunk_rows: Optional[int] = None, keys: Optional[Tuple] = None) -> None:
+        """The kernel chain, one ``b200_block_forward`` (or chunked) call per layer;
+        ``keys``: (key counts, hole flags, key bits) of a key-padding mask."""
         cfg = self.config
         B, S, d = x.shape
         cur = x
@@ -461,7 +464,9 @@ class UserOptimizedTransformer(nn.Module):
             a.eps = float(self.layers[i].norm1.eps)
             a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
             a.non_causal = 0 if cfg.causal else 1
-            a.kv_lens = None if kv_lens is None else kv_lens.data_ptr()
+            if keys is not None:
+                a.kv_lens, a.key_holes, a.key_bits = keys[0].data_ptr(), keys[1].data_ptr(), keys[2].data_ptr()
+                a.key_words = keys[2].shape[1]
             if chunk_rows:
                 rt.block_forward_chunked(a, chunk_rows)
             else:

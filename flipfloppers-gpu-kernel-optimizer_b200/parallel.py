@@ -286,16 +286,20 @@ class TensorParallelTransformer:
     @torch.no_grad()
     def __call__(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None,
                  out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """y = model(x, valid_token_mask) with the work split over the TP group.  A
-        prefix-valid key-padding mask needs no change to the causal forward (a valid row
-        never sees a padded key); its padded rows are zeroed at the end by the device-side
-        mask kernel, which also turns a sequence whose mask has a hole into NaN rows."""
+        """y = model(x, valid_token_mask) with the work split over the TP group.  A key-padding
+        mask is turned into key counts, hole flags and key bits on the device
+        (``b200_mask_prepare``), which every chunk's attention applies; padded rows of the
+        output are zeroed at the end."""
         if not x.is_cuda:
             raise RuntimeError("TensorParallelTransformer runs on CUDA devices only (no CPU fallback)")
         cfg, pl = self.model.config, self.plan
         B, S, d = x.shape
         dev = x.device
         mask = self.model._mask_bytes(valid_token_mask, B, S, dev)
+        keys = None
+        if mask is not None:
+            keys = self.model._mask_buffers(B, S, dev)
+            rt.mask_prepare(mask, *keys)
         self._ensure_weights(dev)
         bufs = self._buffers(B, S, dev)
         comm = self._comm_stream(dev)
@@ -342,9 +346,10 @@ class TensorParallelTransformer:
                     # key tile that straddles it reads zeros instead of rows not written yet
                     kvv = kv[: r1]
                     qlen = c1 - c0
+                    mk = {} if keys is None else dict(key_holes=keys[1][b0:b0 + nb], key_bits=keys[2][b0:b0 + nb])
                     rt.flash_causal(q, kvv, kvv, ctx, batch=nb, heads=Hl, head_dim=hd, q_len=qlen,
                                     kv_len=c1, q_offset=c0, q_seq_rows=qlen, kv_seq_rows=S, q_col0=0,
-                                    k_col0=0, v_col0=dl, kv_row0=b0 * S, out_seq_rows=qlen)
+                                    k_col0=0, v_col0=dl, kv_row0=b0 * S, out_seq_rows=qlen, **mk)
                     rt.gemm(rt.EPI_BIAS_F32, ctx, w["w_o"], None, p1)
                     ev["a"][sl].record(cur)
                     self._all_reduce(bufs["p1"][sl][:R], ev["a"][sl], ev["c1"][sl], comm)
@@ -365,5 +370,5 @@ class TensorParallelTransformer:
                         rt.add_layernorm(x1, p2, w["b_out"], dst[r0:r1], w["ln2_w"], w["ln2_b"],
                                          bufs["scratch"][:R], eps)
         if mask is not None:
-            rt.mask_finish(y, mask)
+            rt.zero_masked_rows(y, mask)
         return y.reshape(B, S, d)

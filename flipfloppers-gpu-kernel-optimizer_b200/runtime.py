@@ -58,6 +58,7 @@ class AttnArgs(ctypes.Structure):
         ("q_col0", ctypes.c_int), ("k_col0", ctypes.c_int), ("v_col0", ctypes.c_int),
         ("out", _vp), ("ld_out", _c_ll), ("out_seq_rows", ctypes.c_int), ("out_row0", ctypes.c_int),
         ("non_causal", ctypes.c_int), ("kv_lens", _vp),
+        ("key_bits", _vp), ("key_words", ctypes.c_int), ("key_holes", _vp),
     ]
 
 
@@ -76,6 +77,7 @@ class BlockArgs(ctypes.Structure):
         ("eps", ctypes.c_float),
         ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
         ("non_causal", ctypes.c_int), ("kv_lens", _vp),
+        ("key_bits", _vp), ("key_words", ctypes.c_int), ("key_holes", _vp),
     ]
 
 
@@ -110,8 +112,8 @@ EXPORTS = [
     ("b200_add_layernorm_launch", ctypes.c_int,
      [_vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, _vp]),
     ("b200_zero_masked_rows", ctypes.c_int, [_vp, _vp, _c_ll, ctypes.c_int, _vp]),
-    ("b200_mask_prepare", ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp, _vp]),
-    ("b200_mask_finish", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
+    ("b200_mask_key_words", ctypes.c_int, [ctypes.c_int]),
+    ("b200_mask_prepare", ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp, _vp]),
     ("b200_gemm_launch", ctypes.c_int,
      [ctypes.c_int, _vp, _c_ll, _vp, _c_ll, _vp, _vp, _c_ll, _vp, _c_ll, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
     ("b200_gemm_residual_layernorm_launch", ctypes.c_int,
@@ -228,29 +230,26 @@ def zero_masked_rows(y: torch.Tensor, row_valid: torch.Tensor, stream=None) -> t
     return y
 
 
-# device error word value recorded when a key-padding mask with a hole reaches the kernel chain
-DERR_MASK_HOLES = 7
+def mask_key_words(seq_len: int) -> int:
+    """32-bit words per sequence of the packed key mask (one 16-byte group per 128 keys)."""
+    return int(lib().b200_mask_key_words(int(seq_len)))
 
 
-def mask_prepare(mask: torch.Tensor, kv_lens: torch.Tensor, stream=None) -> torch.Tensor:
-    """kv_lens[b] = valid tokens of sequence b of ``mask`` ([B, S] bool/uint8 on the device,
-    contiguous), computed on the device; a mask with a hole records DERR_MASK_HOLES."""
-    _require_cuda(mask, kv_lens)
+def mask_prepare(mask: torch.Tensor, kv_lens: torch.Tensor, key_holes: Optional[torch.Tensor] = None,
+                 key_bits: Optional[torch.Tensor] = None, stream=None) -> None:
+    """From ``mask`` ([B, S] bool/uint8 on the device, contiguous), on the device: kv_lens[b] =
+    one past the last valid token, key_holes[b] = 1 if the mask is not prefix-valid, and for such
+    a sequence key_bits[b, :] the mask as bits (int32 [B, mask_key_words(S)])."""
+    _require_cuda(mask, kv_lens, key_holes, key_bits)
     B, S = mask.shape
     if kv_lens.dtype != torch.int32 or kv_lens.numel() < B:
         raise TypeError("mask_prepare: kv_lens must be int32 with one entry per sequence")
-    check(lib().b200_mask_prepare(_p(mask), B, S, _p(kv_lens), _stream(stream)), "b200_mask_prepare")
-    return kv_lens
-
-
-def mask_finish(y: torch.Tensor, mask: torch.Tensor, stream=None) -> torch.Tensor:
-    """Padded rows of y (fp32 [B, S, d] / [B*S, d]) set to 0 from ``mask`` ([B, S], on the
-    device); every row of a sequence whose mask has a hole is set to NaN (DERR_MASK_HOLES)."""
-    _require_cuda(y, mask)
-    B, S = mask.shape
-    d = y.shape[-1]
-    check(lib().b200_mask_finish(_p(y), _p(mask), B, S, d, _stream(stream)), "b200_mask_finish")
-    return y
+    if (key_holes is None) != (key_bits is None):
+        raise ValueError("mask_prepare: key_holes and key_bits go together")
+    if key_bits is not None and key_bits.numel() < B * mask_key_words(S):
+        raise ValueError("mask_prepare: key_bits too small")
+    check(lib().b200_mask_prepare(_p(mask), B, S, _p(kv_lens), _p(key_holes), _p(key_bits), _stream(stream)),
+          "b200_mask_prepare")
 
 
 def gemm(epilogue: int, a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor], out: torch.Tensor,
@@ -291,8 +290,11 @@ def flash_causal(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.T
                  head_dim: int, q_len: int, kv_len: int, q_offset: int = 0, q_seq_rows: int = None,
                  kv_seq_rows: int = None, q_col0: int = 0, k_col0: int = 0, v_col0: int = 0, q_row0: int = 0,
                  kv_row0: int = 0, out_seq_rows: int = None, out_row0: int = 0, non_causal: bool = False,
-                 kv_lens: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
-    """Prefix-causal (or full) attention over 2-D fp16 tensors (see B200AttnArgs)."""
+                 kv_lens: Optional[torch.Tensor] = None, key_holes: Optional[torch.Tensor] = None,
+                 key_bits: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """Prefix-causal (or full) attention over 2-D fp16 tensors (see B200AttnArgs); key_holes /
+    key_bits ([batch] / [batch, words] int32, from mask_prepare) mask keys of sequences whose
+    key-padding mask is not prefix-valid."""
     _require_cuda(q, k, v, out)
     a = AttnArgs()
     a.q, a.k, a.v = q.data_ptr(), k.data_ptr(), v.data_ptr()
@@ -309,6 +311,8 @@ def flash_causal(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.T
     a.out_row0 = out_row0
     a.non_causal = int(bool(non_causal))
     a.kv_lens = None if kv_lens is None else kv_lens.data_ptr()
+    if key_bits is not None:
+        a.key_bits, a.key_words, a.key_holes = key_bits.data_ptr(), key_bits.shape[-1], key_holes.data_ptr()
     check(lib().b200_flash_causal_launch(ctypes.byref(a), _stream(stream)), "b200_flash_causal_launch")
     return out
 

@@ -41,7 +41,7 @@ extern "C" {
 /* A cudaStream_t passed as an opaque pointer; 0 is the legacy default stream. */
 typedef void* b200_stream_t;
 
-#define B200_ABI_VERSION 1
+#define B200_ABI_VERSION 2  /* 2: key-padding masks of any shape (key_bits / key_holes) */
 
 /* Status codes.  -1..-4 keep the meaning of the reference's ws_launch return
  * codes (csrc/g4_4_warpspec_gemm.cu:958-975); the rest are new. */
@@ -107,31 +107,31 @@ int b200_add_layernorm_launch(const float* a, const float* b, const float* bias,
 
 /* y[r, :] = 0 for every row r with row_valid[r] == 0: the reference zeroes
  * padded query rows of the model output (torch_transformer_benchmark.py:190-191).
- * With causal attention and a prefix-valid padding mask, valid rows never
- * attend a padded key, so masking the output is the whole of the padding
- * semantics.  y fp32 [rows, d], row_valid uint8 [rows]. */
+ * y fp32 [rows, d], row_valid uint8 [rows] (nonzero = valid). */
 int b200_zero_masked_rows(float* y, const unsigned char* row_valid, long long rows, int d, b200_stream_t stream);
 
 /* The key-padding mask of the kernel chain (b200_block_forward and the chunked
- * forward), checked on the device on every call so that nothing about a mask's
+ * forward), read on the device on every call so that nothing about a mask's
  * contents has to be cached on the host.  Replaces the reference's
- * `_mask_is_all_ones` property cache (torch_transformer_benchmark.py:1011-1025)
- * and its masking of padded keys and rows (TTB:125-128, 140-141, 163-164,
- * 190-191).  mask: [batch, seq_len] bytes, nonzero = valid token (a torch bool
- * tensor as is).  The chain supports prefix-valid masks (valid tokens first,
- * padding last, what the reference harness generates, TTB:1793-1803).
+ * `_mask_is_all_ones` property cache (torch_transformer_benchmark.py:1011-1025);
+ * the semantics are the reference's masking of padded keys and rows (TTB:125-128,
+ * 140-141, 163-164, 190-191) for any mask.  mask: [batch, seq_len] bytes,
+ * nonzero = valid token (a torch bool tensor as is).
  *
- * b200_mask_prepare: kv_lens[b] = number of valid tokens of sequence b (the
- * per-sequence key count of non-causal attention, B200BlockArgs.kv_lens).
- * b200_mask_finish: after the forward, rows of y past each sequence's valid
- * prefix are set to 0.
- * A mask with a hole (a valid token after a padded one) records device error
- * 7 (see b200_device_error), and b200_mask_finish sets every row of such a
- * sequence to NaN, so a result computed with the wrong key set is never
- * returned as a plausible one.  (The single-kernel path,
- * b200_block_fused_small_launch, masks keys one by one and takes any mask.) */
-int b200_mask_prepare(const unsigned char* mask, int batch, int seq_len, int* kv_lens, b200_stream_t stream);
-int b200_mask_finish(float* y, const unsigned char* mask, int batch, int seq_len, int d, b200_stream_t stream);
+ * b200_mask_prepare writes, per sequence b: kv_lens[b] = one past the last valid
+ * token (attention scans no key past it); key_holes[b] = 1 if a valid token
+ * follows a padded one (the mask is not prefix-valid), else 0; and for such a
+ * sequence the mask as bits, key_bits[b * b200_mask_key_words(seq_len) + w] bit i
+ * = token 32w + i valid.  Pass the three to B200BlockArgs / B200AttnArgs
+ * (key_words = b200_mask_key_words(seq_len)).  key_holes / key_bits may be NULL
+ * when only prefix-valid masks occur (what the reference harness generates,
+ * TTB:1793-1803); kv_lens is then all attention needs under causal attention.
+ * After the forward, b200_zero_masked_rows(y, mask, batch*seq_len, d) zeroes the
+ * padded rows.  (The single-kernel path, b200_block_fused_small_launch, reads the
+ * mask bytes itself.) */
+int b200_mask_key_words(int seq_len);
+int b200_mask_prepare(const unsigned char* mask, int batch, int seq_len, int* kv_lens, int* key_holes,
+                      unsigned int* key_bits, b200_stream_t stream);
 
 /* out[M,N] = epilogue(A[M,K] . W[N,K]^T + bias[N]).  A, W fp16 row-major with
  * leading dimensions lda, ldw (elements); bias fp32 (may be null); resid fp32
@@ -182,7 +182,14 @@ typedef struct {
   int out_seq_rows;
   int out_row0;
   int non_causal;        /* 0: causal (query i sees keys <= q_offset+i); 1: every valid key */
-  const int* kv_lens;    /* device [batch]: valid keys per sequence (key padding); NULL = kv_len */
+  const int* kv_lens;    /* device [batch]: keys to scan per sequence (one past the last valid key); NULL = kv_len */
+  /* Key-padding masks that are not prefix-valid (see b200_mask_prepare): for a sequence b with
+   * key_holes[b] != 0, key k is valid iff bit (k % 32) of key_bits[b * key_words + k / 32] is set.
+   * key_words: a multiple of 4 (one 16-byte group per 128 keys), >= 4 * ceil(kv_len / 128);
+   * key_bits 16-byte aligned.  NULL key_holes: every key below kv_lens / kv_len is valid. */
+  const unsigned int* key_bits;
+  int key_words;
+  const int* key_holes;
 } B200AttnArgs;
 
 int b200_flash_causal_launch(const B200AttnArgs* args, b200_stream_t stream);
@@ -215,7 +222,10 @@ typedef struct {
   void* workspace;         /* >= b200_block_workspace_bytes(batch*seq_len, d_model, ffn_dim) */
   size_t workspace_bytes;
   int non_causal;          /* 0: causal block; 1: full attention (the reference without --causal) */
-  const int* kv_lens;      /* device [batch] valid tokens per sequence (key padding), NULL = all */
+  const int* kv_lens;      /* device [batch] keys to scan per sequence (b200_mask_prepare), NULL = all */
+  const unsigned int* key_bits;  /* key-padding masks with holes (b200_mask_prepare), NULL = none */
+  int key_words;
+  const int* key_holes;
 } B200BlockArgs;
 
 size_t b200_block_workspace_bytes(long long tokens, int d_model, int ffn_dim);

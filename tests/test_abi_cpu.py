@@ -34,7 +34,7 @@ def test_library_exports_every_declared_symbol(pkg):
 
 def test_abi_version_and_status_strings(pkg):
     rt = pkg.runtime
-    assert rt.lib().b200_abi_version() == 1
+    assert rt.lib().b200_abi_version() == 2
     assert rt.status_str(0) == "ok"
     assert "head_dim" in rt.status_str(-6)
     assert rt.status_str(12345) == "unknown status"
