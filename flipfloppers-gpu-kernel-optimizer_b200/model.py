@@ -235,8 +235,8 @@ class UserOptimizedTransformer(nn.Module):
 
     @staticmethod
     def _mask_bytes(m: Optional[torch.Tensor], B: int, S: int, device: torch.device) -> Optional[torch.Tensor]:
-        """The key-padding mask as one byte per token on ``device`` ([B, S] uint8, nonzero =
-        valid), or None without a mask.  A contiguous bool mask on the device is used as it
+        """The key-padding mask as one byte per token on ``device`` ([B, S] bool, contiguous),
+        or None without a mask.  A contiguous bool mask on the device is used as it
         is (no copy, no host synchronisation); anything else is converted on the stream.
 
         The kernels read these bytes on every call, so a mask edited in place or a new
@@ -247,11 +247,13 @@ class UserOptimizedTransformer(nn.Module):
         not prefix-valid) packed key bits from ``b200_mask_prepare`` on the device."""
         if m is None:
             return None
-        if m.dim() != 2 or tuple(m.shape) != (B, S):
+        if m.shape != (B, S):
             raise ValueError(f"valid_token_mask must be [{B}, {S}], got {tuple(m.shape)}")
-        if m.dtype == torch.bool and m.device == device and m.is_contiguous():
-            return m.view(torch.uint8)
-        return m.to(device=device, dtype=torch.bool).contiguous().view(torch.uint8)
+        # a contiguous bool mask on the device is what the kernels read (one byte per token,
+        # 0 or 1): no copy and no view on the per-call path
+        if m.dtype is torch.bool and m.is_cuda and m.get_device() == device.index and m.is_contiguous():
+            return m
+        return m.to(device=device, dtype=torch.bool).contiguous()
 
     def _mask_buffers(self, B: int, S: int, device: torch.device) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
         """Device buffers ``b200_mask_prepare`` fills every call: per-sequence key counts and
