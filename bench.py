@@ -183,6 +183,17 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
+    def median_mhz(self):
+        """Median SM clock of the samples taken so far (None without samples)."""
+        sm = []
+        for ln in list(self.lines):
+            parts = [p.strip() for p in ln.split(",")]
+            try:
+                sm.append(float(parts[1]))
+            except (IndexError, ValueError):
+                continue
+        return statistics.median(sm) if sm else None
+
     def stop(self):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
@@ -458,7 +469,8 @@ def main():
         if rank == 0:
             xp = x[:1].contiguous() if strong else x
             roof = roofline_pass(model, xp, mask, flush if flushes(args.config) else None, cfg,
-                                 steps=3 if strong else max(20, min(args.steps, 200)), cfg_name=args.config)
+                                 steps=3 if strong else max(20, min(args.steps, 200)), cfg_name=args.config,
+                                 clock_mhz=clk.median_mhz())
             del xp
         # GPU outputs compared with the oracle in the CPU leg (rank 0, one GPU)
         y_check = None
@@ -708,7 +720,7 @@ def measured_traffic(cfg_name, kernel):
     return int(t["bytes"]), "profiles/" + t["source"]
 
 
-def roofline_pass(model, x, mask, flush, cfg, steps, cfg_name=None):
+def roofline_pass(model, x, mask, flush, cfg, steps, cfg_name=None, clock_mhz=None):
     """Dominant-kernel roofline: per-stage CUDA-event timing of an eager pass on the same inputs."""
     import torch
     peaks = load_peaks()
@@ -734,6 +746,17 @@ def roofline_pass(model, x, mask, flush, cfg, steps, cfg_name=None):
         ach = by / (ms * 1e-3) / 1e9
         out = {"bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s"}
     traffic, traffic_src = measured_traffic(cfg_name, name)
+    if name == "attn":
+        # the exponentials: one exp2 per causal score (B*H*S(S+1)/2) against the SFU's 16 per
+        # clock per SM -- for head_dim 64 the unit that binds before the tensor pipe
+        import torch
+        exps = B * H * S * (S + 1) / 2
+        sms = torch.cuda.get_device_properties(x.device).multi_processor_count
+        clk_hz = clock_mhz * 1e6 if clock_mhz else 1.965e9
+        peak = 16 * sms * clk_hz
+        out["sfu"] = {"exp2_per_s": exps / (ms * 1e-3), "peak_exp2_per_s": peak,
+                      "frac": exps / (ms * 1e-3) / peak, "clock_mhz": clk_hz / 1e6,
+                      "note": "16 exp2 per clock per SM at the median SM clock sampled during the timed region"}
     out.update(frac=out["achieved"] / out["peak"], traffic=traffic, traffic_src=traffic_src, kernel=name,
                ms_per_launch=ms,
                peak_src=f"{peaks['src']} (MEASURED_PEAKS.json burst)" if peaks["src"] == "measured" else "fallback",

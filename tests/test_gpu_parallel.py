@@ -128,8 +128,11 @@ def _tp_child(rank, world, port, mode, q):
                 ok, worst = ok and res.passed, max(worst, res.max_abs_error)
             q.put((rank, ok, worst))
             return
-        # prefix-valid key padding, as the reference harness generates it with --padding-ratio
+        # key padding as the reference harness generates it (--padding-ratio), plus holes in
+        # sequence 1 (the chunks' attention applies key bits)
         x, mask = oracle.generate_random_case(B, S, d, 77, padding_ratio=0.3)
+        mask[1, 7] = False
+        mask[1, 130:140] = False
         if mode == "tp":
             y = par.TensorParallelTransformer(model, rank, world, chunk_rows=128)(x.to(dev), mask.to(dev)).cpu()
         else:
