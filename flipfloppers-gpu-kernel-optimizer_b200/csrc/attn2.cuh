@@ -166,36 +166,55 @@ __global__ void __launch_bounds__(320, 1)
         if (ntile[0] > 0) issue_s(0, 0);
         if (ntile[1] > 0) issue_s(1, 0);
       }
-      for (int j = 0; ok && j < n_all; ++j) {
-        // S of key tile j+1 as soon as the softmax has read S of tile j
-        for (int t = 0; t < 2; ++t) {
-          if (j + 1 >= ntile[t]) continue;
-          if (!mbar_wait(&s_free[t], j & 1, abort_flag, DERR_WAIT_SOFTMAX)) {
-            ok = false;
-            break;
-          }
-          if (!need_kv(j + 1)) break;
-          issue_s(t, j + 1);
-        }
-        if (!ok) break;
+      auto issue_pv = [&](int t, int j) {
+        tc_fence_after();
         const uint32_t vb = v_addr + (j % C::ST) * C::KV_BYTES;
-        for (int t = 0; t < 2; ++t) {
-          if (j >= ntile[t]) continue;
-          if (!mbar_wait(&p_full[t], j & 1, abort_flag, DERR_WAIT_SOFTMAX)) {
+        const uint32_t pt = tmem + C::TM_P + 64 * t;  // P_t: 16 keys per 8 columns
+#pragma unroll
+        for (int kk = 0; kk < C::BN / 16; ++kk)
+          umma_f16_ts(tmem + 256 + t * HD, pt + 8 * kk,
+                      make_sdesc(vb + kk * 16 * C::ROWB, C::BN * C::ROWB, 8 * C::ROWB, C::SWZ), idesc_o,
+                      (j > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&pv_done[t]);
+      };
+      // Issue order = the order the softmax events arrive (the two tiles' exp phases
+      // alternate, so tile 0 frees S of key tile j before tile 1 hands over P of tile j-1,
+      // and so on): S_0,j+1 | P_1,j-1.V (then key tile j-1's K/V slot is released) |
+      // S_1,j+1 | P_0,j.V.  Waiting for the four in a fixed per-tile order instead held
+      // tile 0's next QK^T behind tile 1's PV by most of an exp phase.
+      for (int j = 0; ok && j <= n_all; ++j) {
+        if (j + 1 < ntile[0]) {
+          if (!mbar_wait(&s_free[0], j & 1, abort_flag, DERR_WAIT_SOFTMAX) || !need_kv(j + 1)) {
             ok = false;
             break;
           }
-          tc_fence_after();
-          const uint32_t pt = tmem + C::TM_P + 64 * t;  // P_t: 16 keys per 8 columns
-#pragma unroll
-          for (int kk = 0; kk < C::BN / 16; ++kk)
-            umma_f16_ts(tmem + 256 + t * HD, pt + 8 * kk,
-                        make_sdesc(vb + kk * 16 * C::ROWB, C::BN * C::ROWB, 8 * C::ROWB, C::SWZ), idesc_o,
-                        (j > 0 || kk > 0) ? 1u : 0u);
-          tc_commit(&pv_done[t]);
+          issue_s(0, j + 1);
         }
-        if (!ok) break;
-        tc_commit(&kv_empty[j % C::ST]);
+        if (j >= 1) {
+          if (j - 1 < ntile[1]) {
+            if (!mbar_wait(&p_full[1], (j - 1) & 1, abort_flag, DERR_WAIT_SOFTMAX)) {
+              ok = false;
+              break;
+            }
+            issue_pv(1, j - 1);
+          }
+          tc_commit(&kv_empty[(j - 1) % C::ST]);  // both query tiles are done with key tile j-1
+        }
+        if (j == n_all) break;
+        if (j + 1 < ntile[1]) {
+          if (!mbar_wait(&s_free[1], j & 1, abort_flag, DERR_WAIT_SOFTMAX) || !need_kv(j + 1)) {
+            ok = false;
+            break;
+          }
+          issue_s(1, j + 1);
+        }
+        if (j < ntile[0]) {
+          if (!mbar_wait(&p_full[0], j & 1, abort_flag, DERR_WAIT_SOFTMAX)) {
+            ok = false;
+            break;
+          }
+          issue_pv(0, j);
+        }
       }
       if (*abort_flag) {
         tc_commit(drain);
