@@ -1095,7 +1095,7 @@ int b200_zero_masked_rows(float* y, const unsigned char* row_valid, long long ro
   if (rows == 0) return B200_OK;
   if (int rc = check_arch()) return rc;
   const int vec4 = (d % 4 == 0 && al16(y)) ? 1 : 0;
-  launch_kernel(k_mask_finish, dim3(static_cast<unsigned>((rows + 7) / 8)), dim3(256), 0,
+  launch_kernel(k_mask_finish, dim3(static_cast<unsigned>((rows + 255) / 256)), dim3(256), 0,
                 static_cast<cudaStream_t>(stream), y, row_valid, rows, d, vec4);
   return launch_status();
 }

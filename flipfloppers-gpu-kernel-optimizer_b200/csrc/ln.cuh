@@ -234,18 +234,26 @@ __global__ void __launch_bounds__(256)
 }
 
 // After the forward: every row whose mask byte is 0 is set to 0 (the reference zeroes
-// padded rows of the output, TTB:190-191).  One warp per row; y fp32 [rows, d].
+// padded rows of the output, TTB:190-191).  A warp takes 32 consecutive rows: one
+// coalesced byte load per lane, a ballot, then the whole warp zeroes each padded row of
+// the 32 (a mask without padding costs one pass over its bytes).  y fp32 [rows, d].
 __global__ void __launch_bounds__(256)
     k_mask_finish(float* __restrict__ y, const unsigned char* __restrict__ mask, long long rows, int d, int vec4) {
   griddep_sync();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long long row = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + warp;
-  if (row >= rows || mask[row] != 0) return;
-  float* yr = y + row * d;
-  if (vec4) {  // d % 4 == 0 and y 16-byte aligned (checked by the launcher)
-    for (int c = lane; c < d / 4; c += 32) reinterpret_cast<float4*>(yr)[c] = make_float4(0.f, 0.f, 0.f, 0.f);
-  } else {
-    for (int c = lane; c < d; c += 32) yr[c] = 0.f;
+  const long long r0 = (static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + warp) * 32;
+  if (r0 >= rows) return;
+  const long long r = r0 + lane;
+  uint32_t pad = __ballot_sync(0xffffffffu, r < rows && mask[r] == 0);
+  while (pad) {
+    const int k = __ffs(pad) - 1;
+    pad &= pad - 1;
+    float* yr = y + (r0 + k) * d;
+    if (vec4) {  // d % 4 == 0 and y 16-byte aligned (checked by the launcher)
+      for (int c = lane; c < d / 4; c += 32) reinterpret_cast<float4*>(yr)[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+    } else {
+      for (int c = lane; c < d; c += 32) yr[c] = 0.f;
+    }
   }
 }
 
