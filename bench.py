@@ -436,8 +436,13 @@ def main():
                        int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local]))
     clk.start()
     with torch.inference_mode():
+        # keep each warm-up output alive across the next call, as the timed loop does: the
+        # output then alternates between two blocks and both CUDA graphs (one per output
+        # address) are captured here, not inside the timed region
+        y_w = None
         for _ in range(max(args.warmup, 3)):
-            model(x, mask)
+            y_w = model(x, mask)
+        del y_w
         torch.cuda.synchronize()
         # ---- device-resident timed region
         starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -490,6 +495,12 @@ def main():
             e_st = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
             e_en = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
             xd = torch.empty_like(x)
+            y_w = None
+            for _ in range(3):  # capture this loop's graphs (new input address) before timing it
+                xd.copy_(x_host, non_blocking=True)
+                y_w = model(xd, mask)
+                y_host.copy_(y_w, non_blocking=True)
+            del y_w
             barrier()
             torch.cuda.synchronize()
             for i in range(args.steps):

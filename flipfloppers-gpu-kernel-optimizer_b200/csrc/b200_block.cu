@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
@@ -495,6 +496,7 @@ template <int HD>
 AttnParams attn_params(const B200AttnArgs& a) {
   AttnParams p{};
   p.H = a.heads;
+  p.batch = a.batch;
   p.q_len = a.q_len;
   p.q_offset = a.q_offset;
   p.kv_len = a.kv_len;
@@ -532,8 +534,12 @@ int launch_attn_t(const B200AttnArgs& a, cudaStream_t st) {
   if (C::TMEM_COLS == 256 && smem < 80 * 1024) smem = 80 * 1024;
   auto kern = k_flash_causal<HD, BN>;
   if (int rc = set_smem(reinterpret_cast<const void*>(kern), smem)) return rc;
-  dim3 grid((a.q_len + 127) / 128, a.heads, a.batch);
-  launch_kernel(kern, dim3(grid), dim3(192), smem, st, tq, tk, tv, p);
+  // persistent: as many CTAs as can be resident (two per SM when two fit in
+  // shared memory), each walking its share of the (query tile, head, sequence) items
+  const long long items = static_cast<long long>((a.q_len + 127) / 128) * a.heads * a.batch;
+  const long long per_sm = 2LL * smem + 2048 <= 228LL * 1024 ? 2 : 1;
+  const long long ctas = std::min(items, per_sm * num_sms());
+  launch_kernel(kern, dim3(static_cast<unsigned>(ctas)), dim3(192), smem, st, tq, tk, tv, p);
   return launch_status();
 }
 

@@ -232,6 +232,62 @@ def test_flash_prefix_chunks_equal_full(rt, hd, chunk, S):
     assert (parts.float() - ref).abs().max().item() < 4e-3
 
 
+# (B, H, S, hd): more (query tile, head, sequence) items than the persistent one-tile
+# kernel has CTAs (two per SM for head_dim <= 64, one for 128 / 256), so every CTA runs
+# several items back to back with the next item's Q, K/V and first S issued early
+PERSISTENT_CASES = [(24, 4, 1000, 32), (40, 4, 384, 64), (48, 4, 300, 128), (40, 4, 200, 256), (12, 2, 1900, 32)]
+
+
+@pytest.mark.parametrize("B,H,S,hd", PERSISTENT_CASES)
+@pytest.mark.parametrize("mode", ["causal", "noncausal_holes", "prefix_lens"])
+def test_flash_persistent_many_items_vs_torch(rt, B, H, S, hd, mode):
+    g = torch.Generator().manual_seed(B * 7 + S + hd)
+    d = H * hd
+    nqt = -(-S // 128)
+    assert B * H * nqt > 2 * torch.cuda.get_device_properties(0).multi_processor_count or hd >= 128
+    qkv = torch.randn(B * S, 3 * d, generator=g).to(torch.float16).to(DEV)
+    t = qkv.float().view(B, S, 3, H, hd).permute(2, 0, 3, 1, 4)
+    out = torch.full((B * S, d), float("nan"), dtype=torch.float16, device=DEV)
+    valid = torch.ones(B, S, dtype=torch.bool)
+    kw = {}
+    q_offset = 0
+    if mode == "noncausal_holes":
+        for b in range(B):  # sequences alternate between holes and a plain padded tail
+            if b % 2:
+                valid[b, torch.randperm(S, generator=g)[: S // 5]] = False
+            else:
+                valid[b, S - 13 * (b + 1):] = False
+            valid[b, 0] = True
+    elif mode == "prefix_lens":
+        for b in range(B):
+            valid[b, S - 17 * (b % 5 + 1):] = False
+    if mode != "causal":
+        m = valid.to(DEV)
+        lens = torch.zeros(B, dtype=torch.int32, device=DEV)
+        holes = torch.zeros(B, dtype=torch.int32, device=DEV)
+        bits = torch.zeros(B, rt.mask_key_words(S), dtype=torch.int32, device=DEV)
+        rt.mask_prepare(m, lens, holes, bits)
+        kw = dict(kv_lens=lens, key_holes=holes, key_bits=bits)
+    if mode == "prefix_lens":  # queries [q_offset, S) over the whole K/V prefix
+        q_offset = S // 3 + 3
+    qn = S - q_offset
+    rt.flash_causal(qkv, qkv, qkv, out, batch=B, heads=H, head_dim=hd, q_len=qn, q_offset=q_offset, kv_len=S,
+                    q_seq_rows=S, kv_seq_rows=S, q_row0=q_offset, k_col0=d, v_col0=2 * d, out_seq_rows=S,
+                    out_row0=q_offset, non_causal=(mode == "noncausal_holes"), **kw)
+    s_ = (t[0] @ t[1].transpose(-1, -2)) * hd ** -0.5
+    if mode != "noncausal_holes":
+        causal = torch.arange(S, device=DEV)[None, :] > torch.arange(S, device=DEV)[:, None]
+        s_ = s_.masked_fill(causal, float("-inf"))
+    s_ = s_.masked_fill(~valid.to(DEV)[:, None, None, :], float("-inf"))
+    ref = (torch.softmax(s_, -1) @ t[2]).permute(0, 2, 1, 3)[:, q_offset:]
+    got = out.float().view(B, S, H, hd)[:, q_offset:]
+    torch.cuda.synchronize()
+    assert torch.isfinite(got).all()
+    err = (got - ref).abs().max().item()
+    assert err < 4e-3, err
+    assert rt.device_error(clear=True) == 0
+
+
 def test_launch_rejects_unsupported_shapes(rt):
     a = torch.zeros(64, 40, dtype=torch.float16, device=DEV)
     w = torch.zeros(48, 40, dtype=torch.float16, device=DEV)
