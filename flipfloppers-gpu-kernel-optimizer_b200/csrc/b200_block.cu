@@ -571,9 +571,9 @@ int launch_attn2_t(const B200AttnArgs& a, cudaStream_t st) {
 }
 
 // B200_ATTN_TILES=1 / =2 forces the one- / two-query-tile kernel (head_dim 32
-// and 64) for every shape (A/B comparisons); unset: by sequence length.
-constexpr int ATTN_TWO_TILE_MIN_Q = 2048;
-constexpr int ATTN_TWO_TILE_MIN_Q_HD64 = 512;
+// and 64) for every shape (A/B comparisons); unset: by shape (attn_impl).
+constexpr int ATTN_TWO_TILE_MIN_Q_HD64 = 2048;
+constexpr int ATTN_TWO_TILE_MIN_WAVES = 16;
 
 int attn_tiles_forced() {
   static const int forced = [] {
@@ -608,18 +608,26 @@ int attn_impl(const B200AttnArgs* a, cudaStream_t st) {
     if (!al16(a->key_bits)) return B200_ERR_ALIGN;
   }
   if (int rc = check_arch()) return rc;
-  // Two query tiles per CTA (shared K/V loads, one tile's MMA under the other's
-  // softmax, alternating exp phases) against one tile per CTA with two CTAs per
-  // SM, measured (L2 flushed): head_dim 64 favours two tiles from short
-  // sequences on (B=16 S=1024 H=16: 107 vs 146 us; B=8 S=2048: 158 vs 223 us);
-  // head_dim 32 keeps one tile below S=2048 (B=64 S=1024 H=4: 86 vs 99 us).
+  // Two query tiles per CTA (k_flash_causal2: shared K/V loads, one tile's MMA
+  // under the other's softmax, alternating exp phases; one CTA per pair of
+  // tiles) against the persistent one-tile kernel (two CTAs per SM walking all
+  // items), measured (L2 flushed, B*S = 64K or 128K tokens):
+  //   head_dim 32, H=4: one tile at every length, S=512..16384 (S=1024 79.7 vs
+  //     100.5 us, S=16384 737 vs 830 us);
+  //   head_dim 64, H=16: one tile to S=1024 (330 vs 365 us), two from S=2048
+  //     (S=2048 543 vs 560, S=16384 3069 vs 3437 us: 27.7 waves of pairs);
+  //   head_dim 64, H=2: one tile at every length (S=2048 141 vs 158, S=16384 776
+  //     vs 855 us: 6.9 waves of pairs, whose tail the persistent kernel avoids).
+  // So two tiles for head_dim 64 from S=2048 when the pairs fill >= 16 waves.
   if (hd == 8) return launch_attn_small_t<8>(*a, st);
   if (hd == 16) return launch_attn_small_t<16>(*a, st);
   const int forced = attn_tiles_forced();
-  const int min_q = hd == 64 ? ATTN_TWO_TILE_MIN_Q_HD64 : ATTN_TWO_TILE_MIN_Q;
-  if (forced == 2 || (forced == 0 && a->q_len >= min_q)) {
-    if (hd == 32) return launch_attn2_t<32>(*a, st);
-    if (hd == 64) return launch_attn2_t<64>(*a, st);
+  if (forced == 2 && hd == 32) return launch_attn2_t<32>(*a, st);
+  if (hd == 64) {
+    const long long pairs = static_cast<long long>((a->q_len + 255) / 256) * a->heads * a->batch;
+    const bool two = forced == 2 || (forced == 0 && a->q_len >= ATTN_TWO_TILE_MIN_Q_HD64 &&
+                                      pairs >= static_cast<long long>(ATTN_TWO_TILE_MIN_WAVES) * num_sms());
+    if (two) return launch_attn2_t<64>(*a, st);
   }
   switch (hd) {
     case 32: return launch_attn_t<32, 128>(*a, st);

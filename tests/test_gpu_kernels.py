@@ -188,7 +188,7 @@ def _attn_ref(q, k, v, q_offset):
 ATTN_CASES = [  # B, H, S, hd
     (2, 4, 128, 32), (3, 2, 100, 32), (2, 4, 384, 64), (1, 2, 300, 128), (2, 4, 128, 256), (1, 2, 200, 256),
     (2, 4, 1024, 32),
-    (1, 2, 2304, 64), (2, 2, 2100, 32),  # q_len >= 2048: two query tiles per CTA
+    (1, 2, 2304, 64), (2, 2, 2100, 32),  # long rows; two query tiles per CTA only when forced (below)
     (2, 4, 128, 8), (3, 16, 100, 8), (2, 8, 300, 16), (1, 4, 1000, 8),  # head_dim 8 / 16: CUDA-core kernel
 ]
 

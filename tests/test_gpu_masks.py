@@ -142,7 +142,7 @@ HOLES = [
     ("chain_noncausal", 3, 256, 256, 4, 1024, 1, False, "chain", None),
     ("chain_2layers", 3, 200, 256, 4, 512, 2, True, "chain", None),
     ("chain_hd8", 2, 160, 128, 16, 512, 1, True, None, None),            # head_dim 8: CUDA-core attention
-    ("chain_hd64_two_tiles", 2, 1100, 256, 4, 512, 1, True, "chain", None),  # two-query-tile kernel
+    ("chain_hd64_long", 2, 1100, 256, 4, 512, 1, True, "chain", None),  # 9 query tiles per sequence
 ]
 
 
@@ -166,6 +166,48 @@ def test_masks_with_holes_on_the_chain(tt, pkg, sid, B, S, d, H, F, L, causal, s
     assert rt.device_error(clear=True) == 0
     assert torch.isfinite(y).all()
     _check(model, x, y, m)
+
+
+@pytest.mark.parametrize("causal", [True, False], ids=["causal", "noncausal"])
+def test_masks_with_holes_on_the_two_tile_kernel_in_subprocess(causal):
+    """The same masks through the two-query-tile attention kernel (k_flash_causal2), which the
+    library picks by itself only for head_dim-64 grids of many waves; B200_ATTN_TILES=2 (read
+    once per process, hence the child) forces it here at a size the oracle checks quickly."""
+    import os
+    import subprocess
+    import sys
+    code = r'''
+import sys, torch
+import oracle
+import torch_transformer_benchmark as tt
+causal = sys.argv[1] == "1"
+B, S, d, H, F, L = 2, 1100, 256, 4, 512, 1
+cfg = tt.TransformerConfig(B, S, d, H, F, L, causal)
+torch.manual_seed(77)
+model = tt.UserOptimizedTransformer(cfg).to("cuda").eval()
+model.force_strategy = "chain"
+x, _ = oracle.generate_random_case(B, S, d, 7)
+m = torch.ones(B, S, dtype=torch.bool)
+m[1, S - 40:] = False
+m[0, 0] = False
+m[0, S // 3:S // 3 + 5] = False
+m[1, 50] = False
+with torch.inference_mode():
+    y = model(x.to("cuda"), m.to("cuda")).cpu()
+rt = tt._pkg.runtime
+assert rt.device_error(clear=True) == 0
+ref = oracle.model_forward(oracle.params_from_state_dict(model.state_dict()),
+                           oracle.OracleConfig(B, S, d, H, F, L, causal), x.numpy(), m.numpy())
+res = oracle.compare_outputs(ref, y, rtol=0.02, atol=0.002)
+assert res.passed, res
+assert torch.all(y[~m] == 0) and torch.isfinite(y).all()
+print("OK", res.max_abs_error)
+'''
+    env = dict(os.environ, B200_ATTN_TILES="2")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", code, "1" if causal else "0"], cwd=root, env=env,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and "OK" in r.stdout, r.stdout + r.stderr
 
 
 def test_mask_is_never_cached_on_the_host(tt):

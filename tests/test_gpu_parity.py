@@ -208,8 +208,8 @@ def test_forward_host_pipeline_matches_device_path(tt, d, H, F):
 def test_padding_masks_against_oracle(tt, B, S, d, H, F, L, causal):
     """Prefix-valid key-padding masks (generate_random_case with padding_ratio > 0):
     valid rows match the reference's masked forward, padded rows are exactly 0 --
-    on the fused small-model kernel (d=128), on the chain, and (S >= 2048) with
-    the two-query-tile attention kernel; causal and non-causal."""
+    on the fused small-model kernel (d=128) and on the chain (S = 2300: 18 query
+    tiles per sequence); causal and non-causal."""
     model, _ = _model(tt, B, S, d, H, F, L, seed=31, causal=causal)
     x, mask = oracle.generate_random_case(B, S, d, 32, padding_ratio=0.5)
     assert not bool(mask.all())
