@@ -248,21 +248,24 @@ int pick_bn(long long M, int N) {
   return N % 256 == 0 ? 256 : 128;
 }
 
-// CTA-pair kernel: clusters that can be resident at once (queried once per device)
-int g_pair_clusters[128] = {0};
+// CTA-pair kernel: clusters that can be resident at once (queried once per device
+// and epilogue-warp count)
+int g_pair_clusters[2][128] = {{0}};
 
-template <int EPI>
+template <int EPI, int EW>
 int launch_gemm2_t(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const GemmParams& p,
                    cudaStream_t st) {
-  auto kern = k_gemm2_tn<EPI>;
-  const int smem = Gemm2Smem<GEMM2_STAGES>::TOTAL;
+  auto kern = k_gemm2_tn<EPI, EW>;
+  const int smem = Gemm2Smem<gemm2_stages(EW), EW>::TOTAL;
+  const int threads = gemm2_threads(EW);
   if (int rc = set_smem(reinterpret_cast<const void*>(kern), smem)) return rc;
   const int dev = current_device();
-  int maxcl = (dev >= 0 && dev < 128) ? g_pair_clusters[dev] : 0;
+  int* cache = g_pair_clusters[EW == 16 ? 1 : 0];
+  int maxcl = (dev >= 0 && dev < 128) ? cache[dev] : 0;
   if (maxcl <= 0) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(num_sms()));
-    cfg.blockDim = dim3(GEMM_THREADS);
+    cfg.blockDim = dim3(threads);
     cfg.dynamicSmemBytes = static_cast<size_t>(smem);
     int n = 0;
     if (cudaOccupancyMaxActiveClusters(&n, reinterpret_cast<const void*>(kern), &cfg) != cudaSuccess || n <= 0) {
@@ -270,12 +273,21 @@ int launch_gemm2_t(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorM
       n = num_sms() / 2;
     }
     maxcl = n;
-    if (dev >= 0 && dev < 128) g_pair_clusters[dev] = n;
+    if (dev >= 0 && dev < 128) cache[dev] = n;
   }
   const long long tiles = static_cast<long long>((p.M + 255) / 256) * ((p.N + 255) / 256);
   const int clusters = static_cast<int>(tiles < maxcl ? tiles : maxcl);
-  launch_kernel(kern, dim3(2 * clusters), dim3(GEMM_THREADS), smem, st, ta, tw, to, p);
+  launch_kernel(kern, dim3(2 * clusters), dim3(threads), smem, st, ta, tw, to, p);
   return launch_status();
+}
+
+// Epilogue warps of the pair kernel: 16 when K is short (<= 256: at most four
+// 64-wide K slices per tile, so the epilogue sets the speed), else 8.
+template <int EPI>
+int launch_gemm2_k(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const GemmParams& p,
+                   cudaStream_t st) {
+  if (p.K <= 256) return launch_gemm2_t<EPI, 16>(ta, tw, to, p, st);
+  return launch_gemm2_t<EPI, 8>(ta, tw, to, p, st);
 }
 
 // 0: one-SM kernel, 1: CTA-pair kernel, -1 (default): by shape
@@ -345,10 +357,10 @@ int gemm_impl(int epi, const void* A, long long lda, const void* W, long long ld
     CUtensorMap tw2;  // each CTA of the pair loads 128 rows (half the tile's N range) of W
     if (int rc = make_map_f16(&tw2, W, N, K, ldw, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
     switch (epi) {
-      case EPI_BIAS_F16: return launch_gemm2_t<EPI_BIAS_F16>(ta, tw2, to, p, st);
-      case EPI_BIAS_GELU_F16: return launch_gemm2_t<EPI_BIAS_GELU_F16>(ta, tw2, to, p, st);
-      case EPI_BIAS_RESID_F32: return launch_gemm2_t<EPI_BIAS_RESID_F32>(ta, tw2, to, p, st);
-      default: return launch_gemm2_t<EPI_BIAS_F32>(ta, tw2, to, p, st);
+      case EPI_BIAS_F16: return launch_gemm2_k<EPI_BIAS_F16>(ta, tw2, to, p, st);
+      case EPI_BIAS_GELU_F16: return launch_gemm2_k<EPI_BIAS_GELU_F16>(ta, tw2, to, p, st);
+      case EPI_BIAS_RESID_F32: return launch_gemm2_k<EPI_BIAS_RESID_F32>(ta, tw2, to, p, st);
+      default: return launch_gemm2_k<EPI_BIAS_F32>(ta, tw2, to, p, st);
     }
   }
   if (BN == 256) return launch_gemm_bn<256, 4>(epi, ta, tw, to, p, st);

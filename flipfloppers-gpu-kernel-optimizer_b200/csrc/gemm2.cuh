@@ -18,9 +18,9 @@
 //   warp 1, leader      TMEM double buffer (2 x 256 columns, allocated as a
 //                       pair) and the MMA issuer; accumulator-full is committed
 //                       to both CTAs.
-//   warps 2-9, both     epilogue of the CTA's 128 rows (gemm_epilogue_cols);
-//                       each warp arrives on the leader's accumulator-empty
-//                       barrier.
+//   warps 2.., both     epilogue of the CTA's 128 rows (gemm_epilogue_cols;
+//                       8 or 16 warps); each warp arrives on the leader's
+//                       accumulator-empty barrier.
 // No TMA load uses multicast: every CTA loads only its own operand halves.
 // Every wait is bounded (ptx.cuh); the CTAs meet at a cluster barrier before
 // the pair frees its tensor memory and exits, so no remote arrival or copy
@@ -68,24 +68,30 @@ __device__ __forceinline__ void umma_f16_ss_pair(uint32_t d_tmem, uint64_t adesc
       : "memory");
 }
 
-template <int STAGES>
+template <int STAGES, int EW>
 struct Gemm2Smem {
   static constexpr int A_BYTES = 128 * 64 * 2;  // this CTA's 128 rows of A
   static constexpr int B_BYTES = 128 * 64 * 2;  // this CTA's 128 rows (N half) of W
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STG_OFF = STAGES * STAGE_BYTES;
-  static constexpr int BAR_OFF = STG_OFF + 8 * 4096;
+  static constexpr int BAR_OFF = STG_OFF + EW * 4096;  // two 2 KB staging slots per epilogue warp
   static constexpr int TOTAL = BAR_OFF + 256 + 1024;
 };
 
-constexpr int GEMM2_STAGES = 6;
+// EW epilogue warps per CTA: 8 (two per SMSP) with a 6-stage operand ring, or
+// 16 (four per SMSP, each taking 64 of the tile's columns) with 4 stages for
+// short K, where the mainloop is a few K slices and the epilogue alone sets the
+// speed (its warps are latency-bound one by one).
+__host__ __device__ constexpr int gemm2_stages(int ew) { return ew == 16 ? 4 : 6; }
+__host__ __device__ constexpr int gemm2_threads(int ew) { return 64 + 32 * ew; }
 
-template <int EPI>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
+template <int EPI, int EW>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2_threads(EW), 1)
     k_gemm2_tn(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                const __grid_constant__ CUtensorMap tmO, const GemmParams p) {
-  constexpr int STAGES = GEMM2_STAGES;
-  using L = Gemm2Smem<STAGES>;
+  static_assert(EW == 8 || EW == 16, "8 or 16 epilogue warps");
+  constexpr int STAGES = gemm2_stages(EW);
+  using L = Gemm2Smem<STAGES, EW>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_align1024(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
@@ -112,7 +118,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 16);  // 8 epilogue warps in each of the two CTAs
+      mbar_init(&acc_empty[b], 2 * EW);  // EW epilogue warps in each of the two CTAs
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -189,9 +195,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
       }
     }
   } else {
-    // epilogue warps 2..9: this CTA's 128 rows of each 256x256 tile
+    // epilogue warps 2..EW+1: this CTA's 128 rows of each 256x256 tile; the EW/4 warps
+    // of TMEM lane quadrant q split its 256 columns
+    constexpr int CWE = 256 / (EW / 4);
     const int q = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int part = (warp - 2) >> 2;
     uint8_t* stg = smem + L::STG_OFF + (warp - 2) * 4096;
     const uint32_t empty_leader0 = mapa_shared(smem_u32(&acc_empty[0]), 0);
     if (lane == 0) tma_prefetch_desc(&tmO);
@@ -203,8 +211,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
       const bool ok = mbar_wait_warp(&acc_full[b], (i >> 1) & 1, abort_flag, DERR_WAIT_MMA);
       if (!ok || *abort_flag) break;
       tc_fence_after();
-      gemm_epilogue_cols<EPI>(&tmO, p, tmem + (static_cast<uint32_t>(q * 32) << 16) + b * 256, half * 128,
-                              (half + 1) * 128, n0, m0 + q * 32, stg, gc, lane);
+      gemm_epilogue_cols<EPI>(&tmO, p, tmem + (static_cast<uint32_t>(q * 32) << 16) + b * 256, part * CWE,
+                              (part + 1) * CWE, n0, m0 + q * 32, stg, gc, lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(empty_leader0 + b * 8);
