@@ -92,23 +92,30 @@ __device__ __forceinline__ void gemm_epilogue_cols(const CUtensorMap* tmO, const
     const int col = col0 + c;
     uint8_t* slot = stg + (gc & 1) * 2048;
     uint32_t w[16];  // the chunk's 64 bytes of this row
+    // the chunk's bias is loaded before the TMEM load (whose wait orders every
+    // memory access after it), so the two latencies overlap
+    const bool has_bias = p.bias != nullptr && col < p.N;
+    float4 bb[CC / 4];
+#pragma unroll
+    for (int j = 0; j < CC / 4; ++j)
+      bb[j] = has_bias ? __ldg(reinterpret_cast<const float4*>(p.bias + col) + j) : make_float4(0.f, 0.f, 0.f, 0.f);
     if constexpr (F32) {
       float v[16];
       tmem_ld16(taddr, v);
-      if (p.bias != nullptr && col < p.N) {
-        const float4* b4 = reinterpret_cast<const float4*>(p.bias + col);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float4 bb = __ldg(b4 + j);
-          v[4 * j] += bb.x; v[4 * j + 1] += bb.y; v[4 * j + 2] += bb.z; v[4 * j + 3] += bb.w;
-        }
+      for (int j = 0; j < 4; ++j) {
+        v[4 * j] += bb[j].x; v[4 * j + 1] += bb[j].y; v[4 * j + 2] += bb[j].z; v[4 * j + 3] += bb[j].w;
       }
 #pragma unroll
       for (int j = 0; j < 16; ++j) w[j] = __float_as_uint(v[j]);
     } else {
       float v[32];
       tmem_ld32(taddr, v);
-      if (p.bias != nullptr && col < p.N) f2_add_bias32_global(v, p.bias + col);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        f2upk(f2add(f2pk(v[4 * j], v[4 * j + 1]), f2pk(bb[j].x, bb[j].y)), v[4 * j], v[4 * j + 1]);
+        f2upk(f2add(f2pk(v[4 * j + 2], v[4 * j + 3]), f2pk(bb[j].z, bb[j].w)), v[4 * j + 2], v[4 * j + 3]);
+      }
       if constexpr (EPI == EPI_BIAS_GELU_F16) {
 #pragma unroll
         for (int j = 0; j < 32; j += 2) gelu_as2(v[j], v[j + 1]);
