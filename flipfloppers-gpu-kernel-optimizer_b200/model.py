@@ -35,7 +35,7 @@ import math
 import os
 from dataclasses import dataclass
 from collections import OrderedDict
-from typing import Dict, Optional, Tuple
+from typing import Dict, List, Optional, Tuple
 
 import torch
 import torch.nn as nn
@@ -116,6 +116,8 @@ _GRAPH_MAX_ELEMS = int(os.environ.get("B200_GRAPH_MAX_ELEMS", str(1 << 26)))
 _GRAPHS_ON = os.environ.get("B200_CUDA_GRAPHS", "1") != "0"
 _GRAPH_CACHE = 8
 _FUSED_SMALL_ON = os.environ.get("B200_FUSED_SMALL", "1") != "0"
+# forward_host splits inputs larger than this into batch groups pipelined inside the call
+_HOST_GROUP_BYTES = 2 << 30
 
 
 def _gemm_ln_fused(d: int) -> bool:
@@ -490,6 +492,15 @@ class UserOptimizedTransformer(nn.Module):
         ``out`` is valid after ``synchronize_host()``.  Pass pinned tensors for
         the copies to be asynchronous.  ``flush`` (a device buffer) is zeroed on
         the forward stream before the forward, for benchmarks that flush L2.
+
+        Inputs of several GB are also pipelined inside the call: the batch is
+        split into groups of whole sequences (about 2 GiB of x each, the group
+        count a divisor of B), and each group's upload, forward and download
+        follow one another on the three streams, so the first forward starts
+        after one group's upload instead of the whole batch's and the last
+        download waits for one group's forward.  Sequences are independent and
+        every kernel computes a row the same way at any batch size, so the
+        result is bitwise the one-piece forward's.
         """
         dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         if x_host.dtype != torch.float32 or x_host.dim() != 3:
@@ -503,28 +514,41 @@ class UserOptimizedTransformer(nn.Module):
         slot = i % nslot
         xd, yd = pipe["x"][slot], pipe["y"][slot]
         ev = pipe["ev"][slot]
+        gev = pipe["gev"][slot]
         with torch.cuda.device(dev):
             up, comp, down = pipe["streams"]
-            with torch.cuda.stream(up):
-                if i >= nslot:
-                    up.wait_event(ev["comp"])      # slot's previous forward has read x
-                xd.copy_(x_host, non_blocking=True)
-                ev["up"].record(up)
-            with torch.cuda.stream(comp):
-                comp.wait_event(ev["up"])
-                if i >= nslot:
-                    comp.wait_event(ev["down"])    # slot's previous y has been downloaded
-                if flush is not None:
-                    flush.zero_()
-                self._forward_into(xd, yd)
-                ev["comp"].record(comp)
-            with torch.cuda.stream(down):
-                down.wait_event(ev["comp"])
-                out.copy_(yd, non_blocking=True)
-                ev["down"].record(down)
+            if i >= nslot:
+                up.wait_event(ev["comp"])      # slot's previous forward has read x
+                comp.wait_event(ev["down"])    # slot's previous y has been downloaded
+            for g, (b0, b1) in enumerate(pipe["groups"]):
+                with torch.cuda.stream(up):
+                    xd[b0:b1].copy_(x_host[b0:b1], non_blocking=True)
+                    gev[g]["up"].record(up)
+                with torch.cuda.stream(comp):
+                    comp.wait_event(gev[g]["up"])
+                    if g == 0 and flush is not None:
+                        flush.zero_()
+                    self._forward_into(xd[b0:b1], yd[b0:b1])
+                    gev[g]["comp"].record(comp)
+                with torch.cuda.stream(down):
+                    down.wait_event(gev[g]["comp"])
+                    out[b0:b1].copy_(yd[b0:b1], non_blocking=True)
+            ev["comp"].record(comp)
+            ev["down"].record(down)
         if wait:
             pipe["streams"][2].synchronize()
         return out
+
+    @staticmethod
+    def _host_groups(shape) -> List[Tuple[int, int]]:
+        """Batch ranges of ``forward_host``'s in-call pipeline: about 2 GiB of fp32 x per
+        group, as many groups as the largest divisor of B not above that count."""
+        B = int(shape[0])
+        nbytes = 4 * B * int(shape[1]) * int(shape[2])
+        want = max(1, -(-nbytes // _HOST_GROUP_BYTES))
+        G = max(g for g in range(1, min(B, want) + 1) if B % g == 0)
+        step = B // G
+        return [(k * step, (k + 1) * step) for k in range(G)]
 
     def host_done_event(self, shape, device=None) -> "torch.cuda.Event":
         """Event recorded after the last queued ``forward_host`` download of ``shape``."""
@@ -556,7 +580,10 @@ class UserOptimizedTransformer(nn.Module):
                     "y": [torch.empty(shape, dtype=torch.float32, device=dev) for _ in range(nslot)],
                     "streams": [torch.cuda.Stream(device=dev) for _ in range(3)],
                     "ev": [{k: torch.cuda.Event() for k in ("up", "comp", "down")} for _ in range(nslot)],
+                    "groups": self._host_groups(shape),
                 }
+                pipe["gev"] = [[{k: torch.cuda.Event() for k in ("up", "comp")} for _ in pipe["groups"]]
+                               for _ in range(nslot)]
             pipes[key] = pipe
         return pipe
 

@@ -185,12 +185,19 @@ def test_c5_shape_sampled_rows(tt):
     assert res.passed, res
 
 
-@pytest.mark.parametrize("d,H,F", [(128, 4, 512), (256, 4, 1024)])
-def test_forward_host_pipeline_matches_device_path(tt, d, H, F):
+@pytest.mark.parametrize("d,H,F,group_bytes", [(128, 4, 512, None), (256, 4, 1024, None), (256, 4, 1024, 262_144)],
+                         ids=["d128", "d256", "d256_groups"])
+def test_forward_host_pipeline_matches_device_path(tt, pkg, monkeypatch, d, H, F, group_bytes):
     """Pipelined host-buffer calls (uploads, forwards and downloads of consecutive
     calls overlapping on three streams, device slots reused) give exactly the
-    device path's outputs, each call its own."""
+    device path's outputs, each call its own -- also with each call split into
+    batch groups pipelined inside the call (what inputs of several GB get; here
+    forced by a small group size: 2 MB of x in 8 groups of 2 sequences)."""
+    if group_bytes is not None:
+        monkeypatch.setattr(pkg.model, "_HOST_GROUP_BYTES", group_bytes)
     model, _ = _model(tt, 16, 128, d, H, F, 1)
+    if group_bytes is not None:
+        assert len(model._host_groups((16, 128, d))) == 8
     xs = [oracle.generate_random_case(16, 128, d, 300 + i)[0].pin_memory() for i in range(5)]
     outs = [torch.empty_like(x).pin_memory() for x in xs]
     with torch.inference_mode():
