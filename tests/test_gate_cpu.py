@@ -96,3 +96,18 @@ def test_non_causal_never_chunks(tt):
     m = tt.UserOptimizedTransformer(cfg)
     m._memory_budget = lambda device: 0
     assert m._strategy(2, 4096, torch.device("cuda", 0)) == "chain"
+
+
+@pytest.mark.parametrize("shape,groups", [((32, 100000, 1024), 4), ((16, 100000, 1024), 4), ((8, 100000, 1024), 2),
+                                          ((4, 100000, 1024), 1), ((64, 128, 128), 1), ((10000, 128, 128), 1),
+                                          ((3, 300000, 1024), 1), ((12, 100000, 1024), 3)])
+def test_forward_host_batch_groups(tt, shape, groups):
+    """``forward_host`` splits inputs of several GB into batch groups of about 2 GiB of x
+    (the group count a divisor of B): whole, equal, contiguous, in-order ranges covering the
+    batch once; small inputs stay one group."""
+    g = tt.UserOptimizedTransformer._host_groups(shape)
+    assert len(g) == groups
+    B = shape[0]
+    assert g[0][0] == 0 and g[-1][1] == B
+    assert all(a[1] == b[0] for a, b in zip(g, g[1:]))
+    assert len({b1 - b0 for b0, b1 in g}) == 1
