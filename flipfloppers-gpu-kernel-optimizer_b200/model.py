@@ -579,9 +579,11 @@ class UserOptimizedTransformer(nn.Module):
                     "x": [torch.empty(shape, dtype=torch.float32, device=dev) for _ in range(nslot)],
                     "y": [torch.empty(shape, dtype=torch.float32, device=dev) for _ in range(nslot)],
                     "streams": [torch.cuda.Stream(device=dev) for _ in range(3)],
-                    "ev": [{k: torch.cuda.Event() for k in ("up", "comp", "down")} for _ in range(nslot)],
+                    # per slot: its call's last forward and last download (whole-call order)
+                    "ev": [{k: torch.cuda.Event() for k in ("comp", "down")} for _ in range(nslot)],
                     "groups": self._host_groups(shape),
                 }
+                # per slot and batch group: its upload and its forward (order inside the call)
                 pipe["gev"] = [[{k: torch.cuda.Event() for k in ("up", "comp")} for _ in pipe["groups"]]
                                for _ in range(nslot)]
             pipes[key] = pipe
