@@ -183,9 +183,11 @@ __device__ __forceinline__ long long attn_item_index(long long k, int G, int c) 
 template <int BN>
 __device__ __forceinline__ AttnItem attn_item(const AttnParams& p, long long t, int nqt) {
   AttnItem it;
-  const long long hb = static_cast<long long>(p.H) * p.batch;
-  const int r = static_cast<int>(t / hb);
-  const int rem = static_cast<int>(t - r * hb);
+  // 32-bit arithmetic: the launcher admits fewer than 2^31 items
+  const int hb = p.H * p.batch;
+  const int ti = static_cast<int>(t);
+  const int r = ti / hb;
+  const int rem = ti - r * hb;
   it.qt = nqt - 1 - r;
   it.h = rem % p.H;
   it.b = rem / p.H;

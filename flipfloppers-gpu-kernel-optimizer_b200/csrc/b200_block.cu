@@ -549,6 +549,7 @@ int launch_attn_t(const B200AttnArgs& a, cudaStream_t st) {
   // persistent: as many CTAs as can be resident (two per SM when two fit in
   // shared memory), each walking its share of the (query tile, head, sequence) items
   const long long items = static_cast<long long>((a.q_len + 127) / 128) * a.heads * a.batch;
+  if (items > 0x7fffffffLL) return B200_ERR_TILE;  // the kernel numbers its items in 32 bits
   const long long per_sm = 2LL * smem + 2048 <= 228LL * 1024 ? 2 : 1;
   const long long ctas = std::min(items, per_sm * num_sms());
   launch_kernel(kern, dim3(static_cast<unsigned>(ctas)), dim3(192), smem, st, tq, tk, tv, p);
