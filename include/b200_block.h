@@ -192,6 +192,8 @@ typedef struct {
   const int* key_holes;
 } B200AttnArgs;
 
+/* heads and batch at most 65535 each, and fewer than 2^31 query tiles of 128 rows in all
+ * (ceil(q_len / 128) * heads * batch); larger launches return B200_ERR_TILE. */
 int b200_flash_causal_launch(const B200AttnArgs* args, b200_stream_t stream);
 
 /* One pre-LN causal block, the reference's per-layer body
